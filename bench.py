@@ -1,0 +1,460 @@
+#!/usr/bin/env python3
+"""NVFP4 QSA benchmark: sparse-decode KV read GB/s (headline) and KV-write tokens/s on B200.
+
+Workload (per GPU, weak scaling): the scale-out decode configuration -- 96
+independent sequences of 131,072 tokens, 12 full-attention layers, 2 KV heads
+x d=256 in an NVFP4 paged cache (page 3,136, random block tables), one query
+row per sequence with 2,048 sorted selected tokens.  Each rank owns its own
+96 sequences; there is no data-path collective.  One step = one decode step
+(12 layers) = 12 reader launches, replayed from a CUDA graph.  The 12 layers'
+selected records (1.36 GB) exceed L2 (126 MB), so every step streams from HBM.
+
+Reported: value (GB/s of algorithmic bytes, all ranks) with the reader's
+roofline against the measured HBM copy bandwidth; e2e (same metric through the
+public API with pinned host inputs/outputs copied inside the timed region);
+the writer on the prefill configuration (8,192 tokens into 64 x 3,136);
+cpu_baseline (the C oracle on a bounded sample, rank 0, N=1).
+`--impl reference` times the reference algorithm's CPU restatement (oracle/)
+on this host -- the reference itself is Python+Triton with no compiled CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "nvfp4-qsa_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+HEAD_DIM, KV_HEADS, QUERY_HEADS, RECORD = 256, 2, 24, 288
+METRIC = "NVFP4 sparse-decode KV read GB/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seqs", type=int, default=96)
+    ap.add_argument("--context", type=int, default=131072)
+    ap.add_argument("--layers", type=int, default=12)
+    ap.add_argument("--topk", type=int, default=2048)
+    ap.add_argument("--page", type=int, default=3136)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    ap.add_argument("--skip-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def read_bytes(rows, topk, layers):
+    """Algorithmic bytes of one reader step: unique records + indices + q + out."""
+    return layers * (rows * KV_HEADS * topk * RECORD + rows * topk * 4 + rows * QUERY_HEADS * HEAD_DIM * 2 * 2)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram read+write bytes per launch recorded from an ncu capture in profiles/<name>."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle"}
+
+    def __init__(self, torch_device):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._handle = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_device)
+            self._nvml = pynvml
+            try:
+                uuid = str(props.uuid)
+                self._handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # clocks are reported as unavailable, never fatal
+            self.error = f"{type(exc).__name__}: {exc}"
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._handle is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._handle is not None:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if self._handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        s = sorted(self.samples)
+        return {"sm_mhz": s[len(s) // 2] if s else None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(s)}
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def build_workload(args, device, seed):
+    """Per-rank NVFP4 caches (written by our writer), block tables, selections, queries."""
+    import torch
+    from nvfp4_qsa import kernels
+
+    seqs, ctx, page, layers, topk = args.seqs, args.context, args.page, args.layers, args.topk
+    width = (ctx + page - 1) // page
+    blocks = seqs * width
+    gen = torch.Generator(device=device).manual_seed(seed)
+    L = []
+    chunk = 1 << 20
+    for layer in range(layers):
+        storage = torch.empty(blocks, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        total = blocks * page
+        for s0 in range(0, total, chunk):
+            n = min(chunk, total - s0)
+            kv = torch.randn(2, n, KV_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+            slots = torch.arange(s0, s0 + n, device=device, dtype=torch.int64)
+            kernels.qsa_write_cache_nvfp4(kv[0], kv[1], kd, ks, vd, vs, slots, 1.0, 1.0)
+        table = torch.randperm(blocks, device=device, generator=gen).to(torch.int32).view(seqs, width).contiguous()
+        idx = torch.rand(seqs, ctx, device=device, generator=gen).topk(topk, dim=1).indices
+        idx = idx.sort(dim=1).values.to(torch.int32).contiguous()
+        q = torch.randn(seqs, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+        L.append(dict(storage=storage, kd=kd, ks=ks, vd=vd, vs=vs, table=table, idx=idx, q=q,
+                      out=torch.empty_like(q)))
+    t2r = torch.arange(seqs, device=device, dtype=torch.int32)
+    torch.cuda.synchronize(device)
+    return L, t2r
+
+
+def run_step(L, t2r, q_override=None, idx_override=None):
+    from nvfp4_qsa import kernels
+    for i, d in enumerate(L):
+        q = d["q"] if q_override is None else q_override[i]
+        idx = d["idx"] if idx_override is None else idx_override[i]
+        kernels.qsa_sparse_paged_attention_nvfp4(q, d["kd"], d["ks"], d["vd"], d["vs"], 1.0, 1.0, idx, d["table"],
+                                                 t2r, d["out"])
+
+
+def timed(fn, steps, device):
+    import torch
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / 1e3
+
+
+def bench_write(device, steps):
+    """Writer on the prefill configuration: 8,192 tokens x (K+V) into a 64 x 3,136 cache."""
+    import torch
+    from nvfp4_qsa import kernels
+    from nvfp4_qsa import workloads as W
+
+    tokens, blocks, page, sets = 8192, 64, 3136, 8  # 8 input sets: 134 MB of inputs > L2
+    gen = torch.Generator(device=device).manual_seed(99)
+    bufs = []
+    for i in range(sets):
+        kv = torch.randn(2, tokens, KV_HEADS, HEAD_DIM, device=device, generator=gen)
+        kv = torch.where(torch.rand(kv.shape, device=device, generator=gen) < 0.02, kv * 32, kv).to(torch.bfloat16)
+        storage = torch.zeros(blocks, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        slots = torch.randperm(blocks * page, device=device, generator=gen)[:tokens].contiguous()
+        bufs.append((kv[0], kv[1], kd, ks, vd, vs, slots))
+
+    def one_round():
+        for b in bufs:
+            kernels.qsa_write_cache_nvfp4(*b, 1.0, 1.0)
+
+    one_round()
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        one_round()
+    torch.cuda.current_stream(device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        one_round()
+    for _ in range(3):
+        graph.replay()
+    rounds = max(20, steps)
+    secs = timed(graph.replay, rounds, device)
+    launches = rounds * sets
+    per_launch = secs / launches
+    algo = tokens * (KV_HEADS * HEAD_DIM * 2 * 2 + 8 + KV_HEADS * RECORD)
+    peak, kind = measured_peaks()
+    # CPU baseline for the writer: the oracle restatement on one prefill batch (port).
+    del W
+    return {
+        "config": {"workload": "prefill: 8192 tokens bf16 K/V [8192,2,256], 2% x32 outliers, into a 64 x 3136 "
+                               "NVFP4 cache at random free slots; 8 rotating buffer sets (inputs > L2)",
+                   "launches": launches},
+        "tokens_per_s": tokens / per_launch,
+        "gb_per_s": algo / per_launch / 1e9,
+        "us_per_launch": per_launch * 1e6,
+        "roofline": {"bound": "hbm", "achieved": algo / per_launch / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algo / per_launch / 1e9 / peak, "peak_kind": kind,
+                     "algorithmic_bytes_per_launch": algo,
+                     "traffic": profile_traffic("write_cache_prefill.md")},
+        "gpu_launches": launches,
+    }
+
+
+def cpu_baseline_read(args, budget_s):
+    """C oracle (float64) over a bounded sample of the decode workload; rank 0 only."""
+    import numpy as np
+    import torch
+    import oracle
+
+    page, ctx, topk = args.page, args.context, args.topk
+    width = (ctx + page - 1) // page
+    nseq = 4  # distinct sequences in the host-side sample cache
+    blocks = nseq * width
+    gen = torch.Generator().manual_seed(7)
+    storage = np.zeros((blocks, KV_HEADS, page, RECORD), np.uint8)
+    total = blocks * page
+    chunk = 1 << 18
+    rng = np.random.default_rng(7)
+    for s0 in range(0, total, chunk):
+        n = min(chunk, total - s0)
+        kv = torch.randn(2, n, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
+        oracle.write_cache(kv[0].view(np.uint16), kv[1].view(np.uint16), storage,
+                           np.arange(s0, s0 + n, dtype=np.int64))
+    table = rng.permutation(blocks).astype(np.int32).reshape(nseq, width)
+    threads = oracle.get_threads()
+    rows_done, secs = 0, 0.0
+    batch = max(threads, 8)
+    while secs < budget_s:
+        q = torch.randn(batch, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
+        idx = np.stack([np.sort(rng.choice(ctx, topk, replace=False)) for _ in range(batch)]).astype(np.int32)
+        t2r = (np.arange(batch) % nseq).astype(np.int32)
+        t0 = time.perf_counter()
+        oracle.sparse_attention(q.view(np.uint16), storage, idx, table, t2r)
+        secs += time.perf_counter() - t0
+        rows_done += batch
+    per_row_bytes = read_bytes(1, topk, 1)
+    return {"value": rows_done * per_row_bytes / secs / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle/nvfp4_oracle.c float64 reader over {rows_done} decode rows (2 KV heads x {topk} "
+                      f"selected of {ctx} tokens, page {page}) in {secs:.1f} s on {threads} OpenMP threads"}
+
+
+def main_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    from nvfp4_qsa import kernels
+
+    L, t2r = build_workload(args, device, seed=1000 + rank)
+    # warm-up eager, then capture one decode step (12 layers) into a CUDA graph
+    run_step(L, t2r)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        run_step(L, t2r)
+    torch.cuda.current_stream(device).wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run_step(L, t2r)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(device) as clocks:
+        secs = timed(graph.replay, args.steps, device)
+    if world > 1:
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    step_bytes = read_bytes(args.seqs, args.topk, args.layers)
+    value = world * step_bytes * args.steps / secs / 1e9
+    ws = kernels.attention_workspace_bytes(args.seqs, QUERY_HEADS, KV_HEADS, HEAD_DIM, args.topk, device)
+    launches_per_layer = 2 if ws > 0 else 1
+    per_layer = secs / args.steps / args.layers
+    peak, kind = measured_peaks()
+    achieved = step_bytes / args.layers / per_layer / 1e9
+
+    # e2e: pinned host inputs -> device, 12 public-API calls, device -> pinned host outputs
+    qh = torch.stack([d["q"] for d in L]).cpu().pin_memory()
+    ih = torch.stack([d["idx"] for d in L]).cpu().pin_memory()
+    oh = torch.empty_like(qh).pin_memory()
+    qd, idd = torch.empty_like(qh, device=device), torch.empty_like(ih, device=device)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        idd.copy_(ih, non_blocking=True)
+        run_step(L, t2r, qd, idd)
+        for i, d in enumerate(L):
+            oh[i].copy_(d["out"], non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(10, args.steps // 4)
+    e2e_secs = timed(e2e_step, e2e_steps, device)
+    if world > 1:
+        t = torch.tensor([e2e_secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_secs = float(t.item())
+    e2e_value = world * step_bytes * e2e_steps / e2e_secs / 1e9
+
+    write = bench_write(device, args.steps) if rank == 0 else None
+    del graph
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 storage, f16 mma, fp32 softmax+acc",
+            "data": "synthetic (seeded torch.randn K/V written by our writer; uniform sorted selections)",
+            "config": {
+                "workload": f"scale-out decode (config 5a per GPU): {args.seqs} sequences x {args.context} tokens x "
+                            f"{args.layers} layers per GPU, 2 KV heads x 256, 24 query heads, top-{args.topk} "
+                            f"selected, page {args.page}, random block tables",
+                "rows_per_layer": args.seqs, "layers": args.layers, "topk": args.topk, "context": args.context,
+                "page": args.page, "cache_gb_per_gpu": sum(d["storage"].numel() for d in L) / 1e9,
+                "step_bytes_per_gpu": step_bytes, "l2": "inputs larger than L2: 12 layers x 113 MB of records",
+                "launch": "one CUDA graph per step (12 layers)", "parallelism": f"dp{world} (sequence-sharded)"},
+            "clocks": clocks.summary(),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": kind, "kernel": "sparse_attention_kernel + merge_kernel (one layer)",
+                         "algorithmic_bytes_per_launch": step_bytes / args.layers,
+                         "us_per_launch": per_layer * 1e6,
+                         "traffic": profile_traffic("sparse_attention_decode.md")},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": qh.numel() * 2 + ih.numel() * 4,
+                    "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": e2e_secs / e2e_steps * 1e3,
+                    "api": "nvfp4_qsa.kernels.qsa_sparse_paged_attention_nvfp4 x12 (eager) + pinned copies"},
+            "gpu_launches": args.steps * args.layers * launches_per_layer,
+            "write": write,
+        }
+        if world == 1 and not args.skip_cpu:
+            result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main_reference(args):
+    """Reference arm: the reference algorithm's CPU restatement (oracle/) on this host, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    import oracle
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    page, ctx, topk = args.page, args.context, args.topk
+    width = (ctx + page - 1) // page
+    nseq = 4
+    blocks = nseq * width
+    gen = torch.Generator().manual_seed(7)
+    rng = np.random.default_rng(7)
+    storage = np.zeros((blocks, KV_HEADS, page, RECORD), np.uint8)
+    total = blocks * page
+    for s0 in range(0, total, 1 << 18):
+        n = min(1 << 18, total - s0)
+        kv = torch.randn(2, n, KV_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
+        oracle.write_cache(kv[0].view(np.uint16), kv[1].view(np.uint16), storage,
+                           np.arange(s0, s0 + n, dtype=np.int64))
+    table = rng.permutation(blocks).astype(np.int32).reshape(nseq, width)
+    threads = oracle.get_threads()
+    rows = max(threads, 8)  # one step = a bounded sample of the workload's rows (one layer)
+    q = torch.randn(rows, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
+    idx = np.stack([np.sort(rng.choice(ctx, topk, replace=False)) for _ in range(rows)]).astype(np.int32)
+    t2r = (np.arange(rows) % nseq).astype(np.int32)
+    steps, warmup = min(args.steps, 20), min(args.warmup, 3)
+    for _ in range(warmup):
+        oracle.sparse_attention(q.view(np.uint16), storage, idx, table, t2r)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.sparse_attention(q.view(np.uint16), storage, idx, table, t2r)
+    secs = time.perf_counter() - t0
+    value = rows * steps * read_bytes(1, topk, 1) / secs / 1e9
+    sample = (f"oracle/nvfp4_oracle.c float64 reader: {rows} decode rows of one layer per step (2 KV heads x {topk} "
+              f"selected of {ctx} tokens, page {page}), {threads} OpenMP threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": secs / steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"scale-out decode (config 5a), bounded CPU sample: {sample}", "topk": topk,
+                   "context": ctx, "page": page},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        main_reference(args)
+    else:
+        main_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,202 @@
+/*
+ * nvfp4_qsa.h -- C ABI of the B200 (sm_100a) NVFP4 paged KV-cache writer and
+ * QSA sparse decode attention.
+ *
+ * Every entry point takes plain device pointers, element counts and strides,
+ * and a cudaStream_t passed as `void*` (NULL = legacy default stream).  No
+ * entry point allocates, synchronizes the stream, or reads device memory from
+ * the host, so every launch is legal inside CUDA graph capture.  All entry
+ * points return an nvqsa_status code; NVQSA_OK is 0.
+ *
+ * Cache layout (reference python/nvfp4_qsa/cache.py:20-24): one uint8 tensor
+ * [blocks, kv_heads, page, 2*(head_dim/2 + head_dim/16)] viewed as four
+ * regions, each indexed [block, token_in_page, kv_head, byte]:
+ *   key_data   head_dim/2  bytes  E2M1 nibbles, low nibble = element 2j
+ *   key_scale  head_dim/16 bytes  E4M3 group scale, one per 16 elements
+ *   value_data head_dim/2  bytes
+ *   value_scale head_dim/16 bytes
+ * The ABI takes each region's base pointer and its (block, token, head) byte
+ * strides, so any layout whose innermost byte run is contiguous is accepted.
+ */
+#ifndef NVFP4_QSA_H_
+#define NVFP4_QSA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvqsa_status {
+  NVQSA_OK = 0,
+  NVQSA_ERR_NULL_POINTER = 1,   /* a required pointer is NULL */
+  NVQSA_ERR_BAD_SHAPE = 2,      /* negative / inconsistent sizes */
+  NVQSA_ERR_HEAD_DIM = 3,       /* head_dim not supported by this build */
+  NVQSA_ERR_MISALIGNED = 4,     /* pointer or stride breaks the alignment contract */
+  NVQSA_ERR_WORKSPACE = 5,      /* workspace missing or smaller than required */
+  NVQSA_ERR_UNSUPPORTED = 6,    /* head grouping / block size outside this build */
+  NVQSA_ERR_LAUNCH = 7,         /* the CUDA launch itself failed */
+  NVQSA_ERR_CUDA = 8            /* a CUDA runtime query failed */
+};
+
+/* Human-readable text for a status code (static storage). */
+const char* nvqsa_status_string(int status);
+
+/* ABI revision of this library; bumped when a signature changes. */
+int nvqsa_abi_version(void);
+
+/*
+ * Quantize BF16 K and V rows to NVFP4 and scatter them into the paged cache in
+ * ONE launch.
+ *
+ * Replaces qsa_write_cache_nvfp4 (reference python/nvfp4_qsa/kernels.py:152-165),
+ * which runs _write_one (kernels.py:118-149) twice.  Per (token t, kv head h):
+ * slot = slot_mapping[t]; the token is skipped when slot < 0 or
+ * slot / page_size >= num_blocks (kernels.py:71-77).  Each group of 16
+ * values gets scale = e4m3_rn(min(g * amax / 6, 448)) and nibbles
+ * e2m1_rn(clamp(x * g / max(scale, 1e-30), -6, 6)); the bytes equal the
+ * reference codec oracle (python/nvfp4_qsa/oracle.py:47-69) for every finite
+ * input, including groups whose scale rounds to zero.
+ *
+ * key, value : bf16 [num_tokens, kv_heads, head_dim], element strides given,
+ *              innermost stride 1.
+ * *_data / *_scale : cache regions, byte strides (block, token, head).
+ * slot_mapping : int64 [num_tokens].
+ * head_dim : 64, 128, 256 or 512.
+ */
+int nvqsa_write_cache(
+    const void* key, int64_t key_stride_token, int64_t key_stride_head,
+    const void* value, int64_t value_stride_token, int64_t value_stride_head,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int64_t num_tokens, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size,
+    float key_global_scale, float value_global_scale, void* stream);
+
+/*
+ * Bytes of workspace nvqsa_sparse_attention needs for this problem on the
+ * current device (0 when the problem runs without a split-KV merge).
+ */
+int nvqsa_sparse_attention_workspace_size(
+    int64_t rows, int32_t query_heads, int32_t kv_heads, int32_t head_dim,
+    int64_t topk, size_t* workspace_bytes);
+
+/*
+ * QSA sparse paged decode attention over an NVFP4 cache.
+ *
+ * Replaces qsa_sparse_paged_attention_nvfp4 (reference
+ * python/nvfp4_qsa/kernels.py:348-403, kernel :168-345).  For query row r and
+ * kv head h, the query heads h*G .. h*G+G-1 (G = query_heads / kv_heads)
+ * attend to the selected tokens logical_indices[r, 0:topk] of request
+ * token_to_request[r]: token i lives in physical block
+ * block_table[req, i / page_size] at offset i % page_size.  A selection is
+ * masked when req is outside [0, num_requests), the index is negative, its
+ * page is >= table_width, or the physical block is outside [0, num_blocks)
+ * (kernels.py:241-257); duplicates count once per occurrence; a row with no
+ * valid selection produces zeros (kernels.py:333-337).  Scores use
+ * head_dim^-0.5 / key_global_scale, the output is divided by
+ * value_global_scale and stored as bf16.
+ *
+ * query, output : bf16 [rows, query_heads, head_dim], element strides given,
+ *                 innermost stride 1.  Only rows [0, rows) are written.
+ * logical_indices : int32 [rows, topk] contiguous.
+ * block_table     : int32 [num_requests, table_width] contiguous.
+ * token_to_request: int32 [rows].
+ * Cache region pointers and byte strides must be 16-byte aligned.
+ * head_dim must be 256 and G must be 1..16.
+ * workspace : device memory of at least nvqsa_sparse_attention_workspace_size
+ *             bytes (may be NULL when that size is 0); contents need no
+ *             initialisation and are dead after the call.
+ */
+int nvqsa_sparse_attention(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Partial (un-merged) variant for split-KV across devices: writes, for every
+ * (row, query head), the softmax-normalized output of the selections this
+ * device holds, already divided by value_global_scale, and its base-2
+ * log-sum-exp (max + log2(sum), or -inf when the device holds none of the
+ * row's selections).  Selections whose block-table entry is outside
+ * [0, num_blocks) are masked, so each device passes a block table that maps
+ * only the pages it owns.  Partial format follows the reference's split-K
+ * sibling (src/qsa_fp8_harness.py:183-208).
+ *
+ * partial_out : fp32 [rows, query_heads, head_dim] contiguous.
+ * partial_lse : fp32 [rows, query_heads] contiguous.
+ * Other arguments as nvqsa_sparse_attention; workspace sized by
+ * nvqsa_sparse_attention_workspace_size.
+ */
+int nvqsa_sparse_attention_partial(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    float* partial_out, float* partial_lse,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Log-sum-exp merge of `splits` partials into the bf16 output: for each
+ * (row, head), out = sum_s 2^(lse_s - M) * O_s / sum_s 2^(lse_s - M) with
+ * M = max_s lse_s; rows whose partials are all -inf become zeros.  The
+ * merge step of the reference's split-K sibling (src/qsa_fp8_harness.py:308-321).
+ *
+ * partial_out : fp32 [splits, rows, query_heads, head_dim] contiguous.
+ * partial_lse : fp32 [splits, rows, query_heads] contiguous.
+ * output      : bf16 [rows, query_heads, head_dim], innermost stride 1.
+ */
+int nvqsa_merge_partials(
+    const float* partial_out, const float* partial_lse, int32_t splits,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, void* stream);
+
+/*
+ * Flat NVFP4 codec on device rows (the GPU form of the reference codec
+ * encode(), python/nvfp4_qsa/oracle.py:47-69).
+ *
+ * x           : fp32 [m, n] contiguous, n % block_size == 0, block_size even.
+ * global_scale: device pointer to one fp32.
+ * nibbles     : uint8 [m, n] (may be NULL), packed : uint8 [m, n/2],
+ * scales      : uint8 [m, n/block_size].
+ * counts      : device int64[2], accumulated (caller zeroes): [0] = elements
+ *               with |x * g / scale| > 6, [1] = groups whose unrounded scale
+ *               is >= 448 - 1e-3 (may be NULL).
+ */
+int nvqsa_encode_rows(
+    const float* x, int64_t m, int64_t n, int32_t block_size, const float* global_scale,
+    uint8_t* nibbles, uint8_t* packed, uint8_t* scales, int64_t* counts, void* stream);
+
+/*
+ * Inverse of nvqsa_encode_rows (reference oracle.py:72-85):
+ * out[i, j] = e2m1(nibble) * (e4m3(scale) / g), fp32 [m, n] contiguous.
+ */
+int nvqsa_decode_rows(
+    const uint8_t* packed, const uint8_t* scales, int64_t m, int64_t n, int32_t block_size,
+    const float* global_scale, float* out, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* NVFP4_QSA_H_ */

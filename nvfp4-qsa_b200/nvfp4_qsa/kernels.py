@@ -1,0 +1,295 @@
+"""NVFP4 paged-cache writer and QSA sparse reader: the reference's raw ops.
+
+Same names, argument order and meaning as the reference module
+``nvfp4_qsa.kernels`` (python/nvfp4_qsa/kernels.py:152-165 and :348-403), so
+the vLLM backend hooks that import ``qsa_write_cache_nvfp4`` and
+``qsa_sparse_paged_attention_nvfp4`` run unchanged.  Both launch hand-written
+sm_100a kernels through the C ABI (include/nvfp4_qsa.h) on the current CUDA
+stream and never synchronize, so they are legal inside CUDA graph capture.
+
+Physical layout per K or V region (reference kernels.py:4-6):
+  data  [blocks, page, kv_heads, head_dim / 2] uint8 (low nibble is element 2j)
+  scale [blocks, page, kv_heads, head_dim / 16] uint8 holding float8_e4m3fn bytes
+The global K/V scales are fixed for the lifetime of a cache.
+"""
+from __future__ import annotations
+
+import contextlib
+from functools import lru_cache
+
+import torch
+
+from . import _native
+
+__all__ = [
+    "qsa_sparse_paged_attention_nvfp4",
+    "qsa_write_cache_nvfp4",
+    "qsa_sparse_paged_attention_nvfp4_partial",
+    "qsa_merge_partials",
+    "attention_workspace_bytes",
+]
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _device_ctx(device: torch.device):
+    if device.type != "cuda":
+        raise ValueError("NVFP4 QSA kernels require CUDA tensors")
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+def _check_same_device(tensors, device):
+    for t in tensors:
+        if t.device != device:
+            raise ValueError("All NVFP4 QSA tensors must be on the same CUDA device")
+
+
+def _check_write_region(source, data, scale, slot_mapping):
+    """Host checks of the reference's _write_one (kernels.py:118-129)."""
+    if source.dim() != 3:
+        raise ValueError("NVFP4 QSA K/V must be [tokens, kv_heads, head_dim]")
+    head_dim = source.shape[2]
+    if source.dtype != torch.bfloat16:
+        raise TypeError("NVFP4 QSA writer requires BF16 K/V")
+    if data.dtype != torch.uint8 or scale.dtype != torch.uint8:
+        raise TypeError("NVFP4 QSA data and scale caches must use uint8 storage")
+    if slot_mapping.dtype != torch.int64:
+        raise TypeError("NVFP4 QSA slot_mapping must be int64")
+    if head_dim % 16 or data.shape[-1] != head_dim // 2:
+        raise ValueError("invalid NVFP4 QSA packed-data shape")
+    if scale.shape[-1] != head_dim // 16:
+        raise ValueError("invalid NVFP4 QSA group-scale shape")
+    if data.dim() != 4 or scale.dim() != 4:
+        raise ValueError("NVFP4 QSA cache regions must be [blocks, page, kv_heads, bytes]")
+    if source.stride(-1) != 1 or data.stride(-1) != 1 or scale.stride(-1) != 1:
+        raise ValueError("NVFP4 QSA tensors need a contiguous last dimension")
+    if slot_mapping.dim() != 1 or slot_mapping.shape[0] != source.shape[0] or slot_mapping.stride(0) != 1:
+        raise ValueError("NVFP4 QSA slot_mapping must be a contiguous [tokens] vector")
+
+
+def qsa_write_cache_nvfp4(
+    key,
+    value,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    slot_mapping,
+    key_global_scale,
+    value_global_scale,
+):
+    """Quantize and write K/V without synchronizing the serving hot path.
+
+    One kernel launch writes both K and V (the reference launches twice).
+    Tokens whose slot is negative or beyond the cache are skipped
+    (kernels.py:71-77).  Valid slots must be unique: duplicates race, exactly
+    as in the reference; ``PackedCache.write`` rejects them on the host.
+    """
+    _check_write_region(key, key_data, key_scale, slot_mapping)
+    _check_write_region(value, value_data, value_scale, slot_mapping)
+    if key.shape != value.shape:
+        raise ValueError("NVFP4 QSA K and V must have the same shape")
+    if key_data.shape[:3] != value_data.shape[:3]:
+        raise ValueError("NVFP4 QSA K and V caches must share [blocks, page, kv_heads]")
+    if key_data.shape[2] != key.shape[1]:
+        raise ValueError("NVFP4 QSA cache kv_heads does not match K/V")
+    device = key.device
+    _check_same_device((value, key_data, key_scale, value_data, value_scale, slot_mapping), device)
+    num_tokens, kv_heads, head_dim = key.shape
+    if num_tokens == 0:
+        return
+    lib = _native.load()
+    with _device_ctx(device):
+        status = lib.nvqsa_write_cache(
+            key.data_ptr(), key.stride(0), key.stride(1),
+            value.data_ptr(), value.stride(0), value.stride(1),
+            key_data.data_ptr(), key_data.stride(0), key_data.stride(1), key_data.stride(2),
+            key_scale.data_ptr(), key_scale.stride(0), key_scale.stride(1), key_scale.stride(2),
+            value_data.data_ptr(), value_data.stride(0), value_data.stride(1), value_data.stride(2),
+            value_scale.data_ptr(), value_scale.stride(0), value_scale.stride(1), value_scale.stride(2),
+            slot_mapping.data_ptr(), num_tokens, kv_heads, head_dim,
+            key_data.shape[0], key_data.shape[1],
+            float(key_global_scale), float(value_global_scale), _stream_ptr(device))
+    _native.check(status, "qsa_write_cache_nvfp4")
+
+
+@lru_cache(maxsize=256)
+def _workspace_bytes(device_index, rows, query_heads, kv_heads, head_dim, topk):
+    import ctypes
+
+    out = ctypes.c_size_t(0)
+    status = _native.load().nvqsa_sparse_attention_workspace_size(rows, query_heads, kv_heads, head_dim, topk,
+                                                                  ctypes.byref(out))
+    _native.check(status, "nvqsa_sparse_attention_workspace_size")
+    return int(out.value)
+
+
+def attention_workspace_bytes(rows, query_heads, kv_heads, head_dim, topk, device=None):
+    """Scratch bytes the reader needs for this problem on ``device``."""
+    device = torch.device("cuda") if device is None else torch.device(device)
+    with _device_ctx(device):
+        index = torch.cuda.current_device()
+        return _workspace_bytes(index, int(rows), int(query_heads), int(kv_heads), int(head_dim), int(topk))
+
+
+def _check_read(query, key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                token_to_request):
+    if query.dim() != 3 or query.dtype != torch.bfloat16 or query.stride(-1) != 1:
+        raise ValueError("NVFP4 QSA query must be bf16 [rows, query_heads, head_dim] with contiguous last dim")
+    for t in (key_data, key_scale, value_data, value_scale):
+        if t.dtype != torch.uint8 or t.dim() != 4 or t.stride(-1) != 1:
+            raise ValueError("NVFP4 QSA cache regions must be uint8 [blocks, page, kv_heads, bytes]")
+    head_dim = query.shape[2]
+    if key_data.shape[-1] != head_dim // 2 or value_data.shape[-1] != head_dim // 2:
+        raise ValueError("invalid NVFP4 QSA packed-data shape")
+    if key_scale.shape[-1] != head_dim // 16 or value_scale.shape[-1] != head_dim // 16:
+        raise ValueError("invalid NVFP4 QSA group-scale shape")
+    for t in (logical_indices, block_table, token_to_request):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("NVFP4 QSA metadata must be contiguous int32")
+    if logical_indices.dim() != 2 or logical_indices.shape[0] < query.shape[0]:
+        raise ValueError("NVFP4 QSA logical_indices must be [rows, topk]")
+    if block_table.dim() != 2:
+        raise ValueError("NVFP4 QSA block_table must be [requests, pages]")
+    if token_to_request.dim() != 1 or token_to_request.shape[0] < query.shape[0]:
+        raise ValueError("NVFP4 QSA token_to_request must be [rows]")
+
+
+def _cache_args(key_data, key_scale, value_data, value_scale):
+    return (
+        key_data.data_ptr(), key_data.stride(0), key_data.stride(1), key_data.stride(2),
+        key_scale.data_ptr(), key_scale.stride(0), key_scale.stride(1), key_scale.stride(2),
+        value_data.data_ptr(), value_data.stride(0), value_data.stride(1), value_data.stride(2),
+        value_scale.data_ptr(), value_scale.stride(0), value_scale.stride(1), value_scale.stride(2),
+        key_data.shape[0], key_data.shape[1], key_data.shape[2])
+
+
+def qsa_sparse_paged_attention_nvfp4(
+    query,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    key_global_scale,
+    value_global_scale,
+    logical_indices,
+    block_table,
+    token_to_request,
+    output,
+):
+    """Sparse paged GQA decode over an NVFP4 cache; writes ``output`` in place.
+
+    Semantics of the reference kernel (kernels.py:168-345): query heads
+    ``h*G .. h*G+G-1`` use kv head ``h``; selection ``logical_indices[r, i]``
+    of request ``token_to_request[r]`` is masked when the request, index,
+    page or physical block is out of range; rows without a valid selection
+    become zeros.  Split-KV scratch comes from the caching allocator on the
+    current stream.
+    """
+    _check_read(query, key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                token_to_request)
+    if output.shape != query.shape or output.dtype != torch.bfloat16 or output.stride(-1) != 1:
+        raise ValueError("NVFP4 QSA output must be bf16 shaped like query with contiguous last dim")
+    device = query.device
+    _check_same_device((key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                        token_to_request, output), device)
+    rows, query_heads, head_dim = query.shape
+    if rows == 0:
+        return
+    topk = logical_indices.shape[1]
+    kv_heads = key_data.shape[2]
+    lib = _native.load()
+    with _device_ctx(device):
+        ws_bytes = _workspace_bytes(torch.cuda.current_device(), rows, query_heads, kv_heads, head_dim, topk)
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+        status = lib.nvqsa_sparse_attention(
+            query.data_ptr(), query.stride(0), query.stride(1),
+            *_cache_args(key_data, key_scale, value_data, value_scale),
+            float(key_global_scale), float(value_global_scale),
+            logical_indices.data_ptr(), topk,
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            token_to_request.data_ptr(),
+            output.data_ptr(), output.stride(0), output.stride(1),
+            rows, query_heads, head_dim,
+            workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+    _native.check(status, "qsa_sparse_paged_attention_nvfp4")
+
+
+def qsa_sparse_paged_attention_nvfp4_partial(
+    query,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    key_global_scale,
+    value_global_scale,
+    logical_indices,
+    block_table,
+    token_to_request,
+    partial_out,
+    partial_lse,
+):
+    """Un-merged reader output for split-KV across devices.
+
+    Writes fp32 ``partial_out[rows, query_heads, head_dim]`` (softmax over this
+    device's valid selections, divided by ``value_global_scale``) and
+    ``partial_lse[rows, query_heads]`` = max + log2(sum), or -inf when none of
+    the row's selections is valid here.  Merge with ``qsa_merge_partials``.
+    """
+    _check_read(query, key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                token_to_request)
+    rows, query_heads, head_dim = query.shape
+    if (partial_out.dtype != torch.float32 or not partial_out.is_contiguous()
+            or tuple(partial_out.shape) != (rows, query_heads, head_dim)):
+        raise ValueError("partial_out must be contiguous fp32 [rows, query_heads, head_dim]")
+    if (partial_lse.dtype != torch.float32 or not partial_lse.is_contiguous()
+            or tuple(partial_lse.shape) != (rows, query_heads)):
+        raise ValueError("partial_lse must be contiguous fp32 [rows, query_heads]")
+    device = query.device
+    _check_same_device((key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                        token_to_request, partial_out, partial_lse), device)
+    if rows == 0:
+        return
+    topk = logical_indices.shape[1]
+    kv_heads = key_data.shape[2]
+    lib = _native.load()
+    with _device_ctx(device):
+        ws_bytes = _workspace_bytes(torch.cuda.current_device(), rows, query_heads, kv_heads, head_dim, topk)
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+        status = lib.nvqsa_sparse_attention_partial(
+            query.data_ptr(), query.stride(0), query.stride(1),
+            *_cache_args(key_data, key_scale, value_data, value_scale),
+            float(key_global_scale), float(value_global_scale),
+            logical_indices.data_ptr(), topk,
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            token_to_request.data_ptr(),
+            partial_out.data_ptr(), partial_lse.data_ptr(),
+            rows, query_heads, head_dim,
+            workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+    _native.check(status, "qsa_sparse_paged_attention_nvfp4_partial")
+
+
+def qsa_merge_partials(partial_out, partial_lse, output):
+    """Log-sum-exp merge of stacked partials ``[splits, rows, heads, dim]`` into bf16 ``output``."""
+    if partial_out.dim() != 4 or partial_out.dtype != torch.float32 or not partial_out.is_contiguous():
+        raise ValueError("partial_out must be contiguous fp32 [splits, rows, heads, dim]")
+    splits, rows, query_heads, head_dim = partial_out.shape
+    if (partial_lse.dtype != torch.float32 or not partial_lse.is_contiguous()
+            or tuple(partial_lse.shape) != (splits, rows, query_heads)):
+        raise ValueError("partial_lse must be contiguous fp32 [splits, rows, heads]")
+    if tuple(output.shape) != (rows, query_heads, head_dim) or output.dtype != torch.bfloat16 or output.stride(-1) != 1:
+        raise ValueError("output must be bf16 [rows, heads, dim] with contiguous last dim")
+    device = output.device
+    _check_same_device((partial_out, partial_lse), device)
+    if rows == 0:
+        return
+    lib = _native.load()
+    with _device_ctx(device):
+        status = lib.nvqsa_merge_partials(partial_out.data_ptr(), partial_lse.data_ptr(), splits,
+                                          output.data_ptr(), output.stride(0), output.stride(1),
+                                          rows, query_heads, head_dim, _stream_ptr(device))
+    _native.check(status, "qsa_merge_partials")

@@ -1,0 +1,202 @@
+"""GPU: the sm_100a NVFP4 writer is bit-exact with the reference codec.
+
+Checks against the reference's golden vectors (tests/golden/) and against the
+pinned C oracle; ports the reference's writer tests (tests/test_gpu_portable.py:9-31)
+and write gates W1/W4/W5 (slice5/src/w_validate.py) with byte equality in place
+of decoded-value or cosine gates.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import bits_to_cuda, cuda_to_bits, gpu_write, regions, sha
+from nvfp4_qsa import PackedCache, kernels
+from nvfp4_qsa import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_storage(key_bits, value_bits, slots, blocks, page, gk=1.0, gv=1.0, head_dim=256):
+    st = np.zeros((blocks, key_bits.shape[1], page, 2 * (head_dim // 2 + head_dim // 16)), np.uint8)
+    oracle.write_cache(key_bits, value_bits, st, slots, gk, gv)
+    return st
+
+
+def test_codec_config_bytes_match_reference(golden_hashes):
+    ref = golden_hashes["codec"]
+    k, v = W.codec_config(seed=ref["seed"], tokens=ref["tokens"])
+    cache = PackedCache(blocks=ref["tokens"] // 16)
+    cache.write(bits_to_cuda(k), bits_to_cuda(v), torch.arange(ref["tokens"], dtype=torch.int64, device="cuda"))
+    torch.cuda.synchronize()
+    assert sha(cache.kd.reshape(-1, 128)) == ref["key_packed_sha256"]
+    assert sha(cache.ks.reshape(-1, 16)) == ref["key_scale_sha256"]
+    assert sha(cache.vd.reshape(-1, 128)) == ref["value_packed_sha256"]
+    assert sha(cache.vs.reshape(-1, 16)) == ref["value_scale_sha256"]
+
+
+def test_prefill_config_storage_matches_reference(golden_hashes):
+    ref = golden_hashes["prefill"]
+    k, v, slots = W.prefill_config(seed=ref["seed"], tokens=ref["tokens"], blocks=ref["blocks"], page=ref["page"])
+    cache = PackedCache(blocks=ref["blocks"], page_size=ref["page"])
+    cache.write(bits_to_cuda(k), bits_to_cuda(v), torch.from_numpy(slots).cuda())
+    assert sha(cache.storage) == ref["storage_sha256"]
+
+
+@pytest.mark.parametrize("amplitude", [0.0, 1e-4, 1.0, 10000.0])
+def test_writer_amplitudes_and_slot_reuse(amplitude):
+    # reference tests/test_gpu_portable.py:9-22, compared byte for byte
+    rng = np.random.default_rng(42)
+    key = W.f32_to_bf16_bits(rng.standard_normal((8, 2, 256), dtype=np.float32) * amplitude)
+    slots = np.array([0, 1, 15, 16, 35, 63, -1, 64], np.int64)
+    cache = PackedCache(4)
+    cache.write(bits_to_cuda(key), bits_to_cuda(key), torch.from_numpy(slots).cuda())
+    expect = oracle_storage(key, key, slots, 4, 16)
+    np.testing.assert_array_equal(cache.storage.cpu().numpy(), expect)
+    cache.write(torch.zeros(1, 2, 256, dtype=torch.bfloat16, device="cuda"),
+                torch.zeros(1, 2, 256, dtype=torch.bfloat16, device="cuda"),
+                torch.zeros(1, dtype=torch.int64, device="cuda"))
+    assert not cache.kd[0, 0].any().item()
+
+
+def test_guard_rejects_duplicate_and_nonfinite():
+    # reference tests/test_gpu_portable.py:24-31
+    cache = PackedCache(1)
+    key = torch.zeros(2, 2, 256, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="Duplicate"):
+        cache.write(key, key, torch.zeros(2, dtype=torch.int64, device="cuda"))
+    key[0, 0, 0] = float("nan")
+    with pytest.raises(ValueError, match="Non-finite"):
+        cache.write(key, key, torch.arange(2, dtype=torch.int64, device="cuda"))
+
+
+def test_codec_cases_through_writer(codec_cases):
+    data, names = codec_cases
+    checked = 0
+    for name in names:
+        x, g = data[f"{name}__x"], float(data[f"{name}__g"][0])
+        bits = W.f32_to_bf16_bits(x)
+        if not np.array_equal(W.bf16_bits_to_f32(bits), x) or x.shape[0] % 2:
+            continue  # the paged writer takes bf16 rows
+        tokens = x.shape[0] // 2
+        key = bits.reshape(tokens, 2, 256)
+        cache = PackedCache(blocks=(tokens + 15) // 16, key_scale=g, value_scale=g)
+        cache.write(bits_to_cuda(key), bits_to_cuda(key), torch.arange(tokens, dtype=torch.int64, device="cuda"))
+        got_p = cache.kd.reshape(-1, 128)[: 2 * tokens].cpu().numpy()
+        got_s = cache.ks.reshape(-1, 16)[: 2 * tokens].cpu().numpy()
+        np.testing.assert_array_equal(got_p, data[f"{name}__packed"], err_msg=name)
+        np.testing.assert_array_equal(got_s, data[f"{name}__scales"], err_msg=name)
+        checked += 1
+    assert checked >= 7
+
+
+def test_infinite_and_tiny_values_follow_oracle():
+    # +-inf saturate the group scale to 448 and the code to +-6; groups whose
+    # scale rounds to zero saturate like the codec oracle (oracle.py:57).
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((6, 2, 256), dtype=np.float32)
+    x[0, 0, 3], x[1, 1, 40], x[2, 0, 200] = np.inf, -np.inf, np.inf
+    x[3:] *= 1e-6
+    bits = W.f32_to_bf16_bits(x)
+    slots = np.arange(6, dtype=np.int64)
+    st = torch.zeros(1, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(bits), bits_to_cuda(bits), torch.from_numpy(slots).cuda())
+    np.testing.assert_array_equal(st.cpu().numpy(), oracle_storage(bits, bits, slots, 1, 16))
+
+
+def test_slot_lifecycle_overwrite():
+    # slice5/src/w_validate.py:167-200 (W4): overwrite slots, no stale bytes
+    rng = np.random.default_rng(11)
+    a = W.f32_to_bf16_bits(rng.standard_normal((64, 2, 256), dtype=np.float32))
+    b = W.f32_to_bf16_bits(rng.standard_normal((3, 2, 256), dtype=np.float32) * 7)
+    slots_a = rng.permutation(64).astype(np.int64)
+    slots_b = np.array([15, 0, 47], np.int64)
+    st = torch.zeros(4, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(a), bits_to_cuda(a[::-1].copy()), torch.from_numpy(slots_a).cuda())
+    gpu_write(st, bits_to_cuda(b), bits_to_cuda(b), torch.from_numpy(slots_b).cuda())
+    exp = oracle_storage(a, a[::-1].copy(), slots_a, 4, 16)
+    oracle.write_cache(b, b, exp, slots_b)
+    np.testing.assert_array_equal(st.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("tokens", [1, 2, 15, 16, 17, 64, 256])
+@pytest.mark.parametrize("dist", ["zeros", "normal", "heavytail", "outliers"])
+def test_boundary_matrix(tokens, dist):
+    # slice5/src/w_validate.py:217-253 (W5) cells, byte-exact
+    rng = np.random.default_rng(1000 + tokens)
+    blocks = (18 + tokens + 15) // 16 + 1
+    src = W.f32_to_bf16_bits(W.gen_values(rng, (tokens, 2, 256), dist))
+    g = 1.0 if dist == "zeros" else float(np.float32(2688.0 / max(np.abs(W.bf16_bits_to_f32(src)).max(), 1e-8)))
+    boundary = [-1, 0, 15, 16, 17, blocks * 16 - 1]
+    slots = np.array((boundary[: min(6, tokens)] + list(range(18, 18 + tokens)))[:tokens], np.int64)
+    slots = slots[rng.permutation(tokens)]
+    st = torch.zeros(blocks, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(src), bits_to_cuda(src), torch.from_numpy(slots).cuda(), g, g)
+    np.testing.assert_array_equal(st.cpu().numpy(), oracle_storage(src, src, slots, blocks, 16, g, g))
+
+
+def test_generic_strides_and_separate_regions():
+    # Non-canonical layout: separate padded K/V tensors, strided sources.
+    rng = np.random.default_rng(21)
+    big = torch.from_numpy(W.f32_to_bf16_bits(rng.standard_normal((40, 3, 384), dtype=np.float32)).view(np.int16))
+    big = big.view(torch.bfloat16).cuda()
+    key, value = big[:, :2, :256], big[:, 1:, 128:]
+    slots = torch.from_numpy(rng.permutation(96)[:40].astype(np.int64)).cuda()
+    kbuf = torch.zeros(6, 16, 2, 160, dtype=torch.uint8, device="cuda")
+    vbuf = torch.zeros(6, 16, 2, 176, dtype=torch.uint8, device="cuda")
+    kd, ks = kbuf[..., :128], kbuf[..., 144:160]
+    vd, vs = vbuf[..., 16:144], vbuf[..., 160:176]
+    kernels.qsa_write_cache_nvfp4(key, value, kd, ks, vd, vs, slots, 1.0, 2.0)
+    kb, vb = cuda_to_bits(key), cuda_to_bits(value)
+    exp = oracle_storage(kb, vb, slots.cpu().numpy(), 6, 16, 1.0, 2.0)
+    ekd, eks, evd, evs = regions(torch.from_numpy(exp))
+    np.testing.assert_array_equal(kd.cpu().numpy(), ekd.numpy())
+    np.testing.assert_array_equal(ks.cpu().numpy(), eks.numpy())
+    np.testing.assert_array_equal(vd.cpu().numpy(), evd.numpy())
+    np.testing.assert_array_equal(vs.cpu().numpy(), evs.numpy())
+
+
+@pytest.mark.parametrize("head_dim", [64, 128, 512])
+def test_other_head_dims(head_dim):
+    rng = np.random.default_rng(head_dim)
+    src = W.f32_to_bf16_bits(W.gen_values(rng, (20, 2, head_dim), "heavytail"))
+    slots = rng.permutation(32)[:20].astype(np.int64)
+    width = 2 * (head_dim // 2 + head_dim // 16)
+    st = torch.zeros(2, 2, 16, width, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(src), bits_to_cuda(src[::-1].copy()), torch.from_numpy(slots).cuda())
+    exp = oracle_storage(src, src[::-1].copy(), slots, 2, 16, head_dim=head_dim)
+    np.testing.assert_array_equal(st.cpu().numpy(), exp)
+
+
+def test_write_inside_cuda_graph():
+    rng = np.random.default_rng(5)
+    src = bits_to_cuda(W.f32_to_bf16_bits(rng.standard_normal((48, 2, 256), dtype=np.float32)))
+    slots = torch.from_numpy(rng.permutation(64)[:48].astype(np.int64)).cuda()
+    st = torch.zeros(4, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    eager = torch.zeros_like(st)
+    gpu_write(eager, src, src, slots)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        gpu_write(st, src, src, slots)  # warm-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    st.zero_()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gpu_write(st, src, src, slots)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(st, eager)
+
+
+def test_raw_op_type_errors():
+    st = torch.zeros(1, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    kd, ks, vd, vs = regions(st)
+    k = torch.zeros(1, 2, 256, dtype=torch.bfloat16, device="cuda")
+    slots = torch.zeros(1, dtype=torch.int64, device="cuda")
+    with pytest.raises(TypeError, match="BF16"):
+        kernels.qsa_write_cache_nvfp4(k.float(), k, kd, ks, vd, vs, slots, 1.0, 1.0)
+    with pytest.raises(TypeError, match="int64"):
+        kernels.qsa_write_cache_nvfp4(k, k, kd, ks, vd, vs, slots.int(), 1.0, 1.0)
+    with pytest.raises(ValueError, match="group-scale"):
+        kernels.qsa_write_cache_nvfp4(k, k, kd, ks[..., :8], vd, vs, slots, 1.0, 1.0)
