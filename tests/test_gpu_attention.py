@@ -238,3 +238,9 @@ def test_raw_reader_rejects_bad_metadata_types():
                                                  torch.zeros(1, 4, dtype=torch.int64, device="cuda"),
                                                  torch.zeros(1, 1, dtype=torch.int32, device="cuda"),
                                                  torch.zeros(1, dtype=torch.int32, device="cuda"), torch.empty_like(q))
+
+
+def test_no_device_error_flags_raised():
+    from nvfp4_qsa import _native
+    torch.cuda.synchronize()
+    assert _native.read_error_flags(clear=True) == 0
