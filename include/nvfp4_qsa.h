@@ -37,7 +37,8 @@ enum nvqsa_status {
   NVQSA_ERR_WORKSPACE = 5,      /* workspace missing or smaller than required */
   NVQSA_ERR_UNSUPPORTED = 6,    /* head grouping / block size outside this build */
   NVQSA_ERR_LAUNCH = 7,         /* the CUDA launch itself failed */
-  NVQSA_ERR_CUDA = 8            /* a CUDA runtime query failed */
+  NVQSA_ERR_CUDA = 8,           /* a CUDA runtime query failed */
+  NVQSA_ERR_SCRATCH_LIMIT = 9   /* problem needs more scratch than the built-in buffer holds */
 };
 
 /* Human-readable text for a status code (static storage). */
@@ -204,6 +205,44 @@ int nvqsa_encode_rows(
 int nvqsa_decode_rows(
     const uint8_t* packed, const uint8_t* scales, int64_t m, int64_t n, int32_t block_size,
     const float* global_scale, float* out, void* stream);
+
+
+/*
+ * Same computation as nvqsa_sparse_attention, for callers that cannot
+ * allocate device memory: code that runs where cudaMalloc is unavailable or
+ * forbidden (a host that hands this library only fixed, pre-registered
+ * buffers, a real-time or embedded serving loop with a no-allocation rule, a
+ * plugin whose framework owns every allocation).  It takes no workspace
+ * argument and allocates nothing; the split-KV partials live in a static
+ * device buffer of NVQSA_NOALLOC_SCRATCH_BYTES (16 MiB) that every device
+ * loading this library keeps for the life of the process.
+ *
+ * Limit: problems whose split-KV partials need more than
+ * NVQSA_NOALLOC_SCRATCH_BYTES (nvqsa_sparse_attention_workspace_size reports
+ * the need; about splits * rows * query_heads * 1 KiB) are rejected with
+ * NVQSA_ERR_SCRATCH_LIMIT before anything is launched.
+ * The first call on each device looks up the buffer's device address; make
+ * that first call outside any stream capture.  All calls on a device share
+ * the one buffer, so calls that may overlap on the GPU (different streams
+ * without ordering between them) race and must be serialised by the caller.
+ * Nothing in the buffer needs to start at zero: each call writes every
+ * partial it later reads.  No counterpart in the reference.
+ */
+#define NVQSA_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+int nvqsa_sparse_attention_noalloc(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

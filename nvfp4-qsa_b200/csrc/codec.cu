@@ -111,6 +111,7 @@ extern "C" const char* nvqsa_status_string(int status) {
     case NVQSA_ERR_UNSUPPORTED: return "head grouping or block size not supported by this build";
     case NVQSA_ERR_LAUNCH: return "CUDA kernel launch failed";
     case NVQSA_ERR_CUDA: return "CUDA runtime query failed";
+    case NVQSA_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the built-in no-allocation buffer holds";
     default: return "unknown status";
   }
 }

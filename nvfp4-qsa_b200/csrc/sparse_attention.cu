@@ -1040,3 +1040,61 @@ extern "C" int nvqsa_merge_partials(const float* partial_out, const float* parti
                                                                 o_stride_head, vec_o, nullptr, nullptr);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }
+
+// ---------------------------------------------------------------------------
+// No-allocation entry point.  For callers that may not allocate device memory
+// (fixed-buffer hosts, no-allocation serving loops, plugins whose framework
+// owns all allocations), the split-KV partials go to this static buffer
+// instead of a caller-provided workspace.  Every device that loads the
+// library holds the buffer until the process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NVQSA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+// Device address of g_noalloc_scratch, looked up once per device.  In host
+// code the symbol names a host-side stand-in, never the device memory, so only
+// this address may be handed to a kernel.
+void* g_noalloc_scratch_ptr[nvqsa::kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= nvqsa::kMaxDevices) return NVQSA_ERR_CUDA;
+  if (!g_noalloc_scratch_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return NVQSA_ERR_CUDA;
+    g_noalloc_scratch_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return NVQSA_OK;
+}
+}  // namespace
+
+extern "C" int nvqsa_sparse_attention_noalloc(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, void* stream) {
+  size_t need = 0;
+  if (const int st = nvqsa_sparse_attention_workspace_size(rows, query_heads, kv_heads, head_dim, topk, &need))
+    return st;
+  if (need > NVQSA_NOALLOC_SCRATCH_BYTES) return NVQSA_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (need > 0) {
+    if (const int st = noalloc_scratch(&scratch)) return st;
+  }
+  return nvqsa_sparse_attention(query, q_stride_row, q_stride_head, key_data, kd_stride_block, kd_stride_token,
+                                kd_stride_head, key_scale, ks_stride_block, ks_stride_token, ks_stride_head,
+                                value_data, vd_stride_block, vd_stride_token, vd_stride_head, value_scale,
+                                vs_stride_block, vs_stride_token, vs_stride_head, num_blocks, page_size, kv_heads,
+                                key_global_scale, value_global_scale, logical_indices, topk, block_table,
+                                num_requests, table_width, token_to_request, output, o_stride_row, o_stride_head, rows,
+                                query_heads, head_dim, scratch, need, stream);
+}

@@ -21,6 +21,7 @@ _STATUS_EXC = {
     6: NotImplementedError,  # NVQSA_ERR_UNSUPPORTED
     7: RuntimeError,        # NVQSA_ERR_LAUNCH
     8: RuntimeError,        # NVQSA_ERR_CUDA
+    9: ValueError,          # NVQSA_ERR_SCRATCH_LIMIT
 }
 
 _P = c_void_p
@@ -72,6 +73,20 @@ _SIGNATURES = {
         _P, _P,
         _I64, _I32, _I32,
         _P, c_size_t, _P]),
+    "nvqsa_sparse_attention_noalloc": (c_int, [
+        _P, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _I64, _I64, _I32,
+        _F, _F,
+        _P, _I64,
+        _P, _I64, _I64,
+        _P,
+        _P, _I64, _I64,
+        _I64, _I32, _I32,
+        _P]),
     "nvqsa_merge_partials": (c_int, [_P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "nvqsa_encode_rows": (c_int, [_P, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P]),
     "nvqsa_decode_rows": (c_int, [_P, _P, _I64, _I64, _I32, _P, _P, _P]),
