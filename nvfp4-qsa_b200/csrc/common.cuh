@@ -33,6 +33,21 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float hi, float lo) {
   return out & 0xffu;
 }
 
+// Eight fp32 -> one word of eight E2M1 codes (element 2j in the low nibble of
+// byte j), same rounding as cvt_e2m1x2.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&y)[8]) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(y[0]), "f"(y[1]), "f"(y[2]), "f"(y[3]), "f"(y[4]), "f"(y[5]), "f"(y[6]), "f"(y[7]));
+  return out;
+}
+
 // The reference takes sign = (y < 0) and maps NaN to code 0 (all its threshold
 // comparisons are false).  Hardware cvt keeps the sign of -0 and saturates NaN,
 // so normalise first: -0 + 0 = +0 under round-to-nearest, NaN -> 0.

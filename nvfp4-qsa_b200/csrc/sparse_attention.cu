@@ -271,11 +271,13 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       if (pos < len && req_ok) {
         const int32_t idx = __ldg(idx_row + pos);
         if (idx >= 0) {
-          const int64_t lpage = (int64_t)idx / p.page_size;
-          if (lpage < p.table_width) {
+          // 0 <= idx < 2^31: a 32-bit division (a page larger than that holds every index in page 0)
+          const bool huge_page = p.page_size > 0x7fffffffLL;
+          const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
+          if ((int64_t)lpage < p.table_width) {
             const int32_t phys = __ldg(bt_row + lpage);
             valid = phys >= 0 && (int64_t)phys < p.num_blocks;
-            ent[it] = make_int2(phys, (int)((int64_t)idx - lpage * p.page_size));
+            ent[it] = make_int2(phys, huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size));
           }
         }
       }
