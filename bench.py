@@ -51,6 +51,9 @@ def parse_args():
     ap.add_argument("--page", type=int, default=3136)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--split-context", type=int, default=169984, help="split-KV section: one sequence of this length")
+    ap.add_argument("--split-topk", type=int, default=8192, help="split-KV section: selected tokens per row")
+    ap.add_argument("--skip-split", action="store_true", help="skip the split-KV section")
     return ap.parse_args()
 
 
@@ -254,6 +257,77 @@ def bench_write(device, steps):
     }
 
 
+def bench_split_kv(args, device, world, rank, steps):
+    """Config 5b: one 169,984-token sequence, 8,192 selected per row, 12 layers, split-KV over the ranks.
+
+    Rank r holds only its contiguous share of the sequence's pages (nvfp4_qsa.distributed.SplitKV); per layer
+    every rank computes its partial, the ranks all_gather the packed partials over NCCL, and each merges them.
+    At N=1 the same step is the plain single-GPU reader.  Timed eagerly with CUDA events, max over ranks.
+    """
+    import torch
+    import torch.distributed as dist
+    from nvfp4_qsa import distributed as D
+    from nvfp4_qsa import kernels
+
+    ctx, topk, page, layers = args.split_context, args.split_topk, args.page, args.layers
+    pages = (ctx + page - 1) // page
+    sk = D.SplitKV(pages, page, world, rank)
+    gen = torch.Generator(device=device).manual_seed(4242 + rank)
+    shared = torch.Generator(device=device).manual_seed(777)  # indices and queries identical on every rank
+    L = []
+    positions = torch.arange(ctx, device=device)
+    slots = sk.slot_mapping(positions) if world > 1 else positions
+    for layer in range(layers):
+        nblk = sk.local_blocks if world > 1 else pages
+        storage = torch.zeros(max(nblk, 1), KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        kv = torch.randn(2, ctx, KV_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+        kernels.qsa_write_cache_nvfp4(kv[0], kv[1], kd, ks, vd, vs, slots, 1.0, 1.0)
+        del kv
+        idx = torch.rand(1, ctx, device=device, generator=shared).topk(topk, dim=1).indices
+        idx = idx.sort(dim=1).values.to(torch.int32).contiguous()
+        q = torch.randn(1, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=shared)
+        table = sk.block_table(device) if world > 1 else torch.arange(pages, device=device,
+                                                                      dtype=torch.int32).view(1, -1)
+        L.append(dict(regions=(kd, ks, vd, vs), idx=idx, q=q, table=table, out=torch.empty_like(q),
+                      buf=sk.partial_buffer(1, QUERY_HEADS, HEAD_DIM, device)))
+    t2r = torch.zeros(1, device=device, dtype=torch.int32)
+
+    def step():
+        for d in L:
+            if world > 1:
+                sk.attend(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], block_table=d["table"],
+                          buffer=d["buf"])
+            else:
+                kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
+                                                         d["out"])
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    n = max(10, steps // 4)
+    secs = timed(step, n, device)
+    if world > 1:
+        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        secs = float(t.item())
+    per_layer_bytes = KV_HEADS * topk * RECORD + topk * 4 + 2 * QUERY_HEADS * HEAD_DIM * 2
+    return {
+        "config": {"workload": f"split-KV decode (config 5b): one sequence of {ctx} tokens, {topk} selected per row, "
+                               f"{layers} layers, page {page}, pages split contiguously over {world} GPU(s); "
+                               "per layer: partial + one NCCL all_gather of packed (O, lse) + merge (eager launches)",
+                   "scaling": "strong"},
+        "ms_per_step": secs / n * 1e3,
+        "us_per_layer": secs / n / layers * 1e6,
+        "gb_per_s": per_layer_bytes * layers * n / secs / 1e9,
+        "exchange_bytes_per_rank_per_layer": L[0]["buf"].numel() * 4 if world > 1 else 0,
+    }
+
+
 def cpu_baseline_read(args, budget_s):
     """C oracle (float64) over a bounded sample of the decode workload; rank 0 only."""
     import numpy as np
@@ -361,6 +435,7 @@ def main_ours(args):
         e2e_secs = float(t.item())
     e2e_value = world * step_bytes * e2e_steps / e2e_secs / 1e9
 
+    split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
     del graph
     result = None
@@ -390,6 +465,8 @@ def main_ours(args):
             "gpu_launches": args.steps * args.layers * launches_per_layer,
             "write": write,
         }
+        if split is not None:
+            result["split_kv"] = split
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
         print(json.dumps(result), flush=True)

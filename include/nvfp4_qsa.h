@@ -183,6 +183,22 @@ int nvqsa_merge_partials(
     int64_t rows, int32_t query_heads, int32_t head_dim, void* stream);
 
 /*
+ * nvqsa_merge_partials with the splits at any distance: split s starts at
+ * partial_out + s * out_split_stride and partial_lse + s * lse_split_stride
+ * (in floats), each split dense [rows, query_heads, head_dim] / [rows,
+ * query_heads].  Used by the split-KV decode across GPUs, whose all_gather
+ * leaves every rank's outputs and lse packed in one buffer.  No reference
+ * counterpart of its own: the reference's split-K merge is the vLLM kernel
+ * called at src/qsa_fp8_harness.py:308-321.
+ * out_split_stride must be a multiple of 4 floats.
+ */
+int nvqsa_merge_partials_strided(
+    const float* partial_out, int64_t out_split_stride,
+    const float* partial_lse, int64_t lse_split_stride, int32_t splits,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, void* stream);
+
+/*
  * Flat NVFP4 codec on device rows (the GPU form of the reference codec
  * encode(), python/nvfp4_qsa/oracle.py:47-69).
  *

@@ -7,10 +7,14 @@
 // layout of the reference's split-K sibling (src/qsa_fp8_harness.py:183-208).
 //
 // One CTA = (row, kv head, split) = 4 warps = 2 warp pairs.
-//  * Prologue: the CTA resolves its range of selections through
+//  * Prologue: the CTA resolves its share of the row's selections through
 //    token_to_request / block_table (masking rules of kernels.py:241-257) and
 //    compacts the valid ones into a shared list, so masked selections cost
-//    nothing (they contribute exp2(-1e20 - m) = 0 in the reference).
+//    nothing (they contribute exp2(-1e20 - m) = 0 in the reference).  The
+//    share is every splits-th chunk of 32 index positions (chunks split,
+//    split + splits, ...), so a row whose valid selections are bunched in one
+//    part of its list -- a sorted list on a device that holds only some of the
+//    sequence's pages -- still spreads them evenly over the CTAs.
 //  * Gather: for the reference cache layout (one contiguous 288-byte record
 //    K data | K scales | V data | V scales per (block, head, token), rows of a
 //    [blocks*kv_heads*page, 288] byte matrix) warp 0 fetches each stage of 32
@@ -57,10 +61,11 @@ constexpr int kHeadDim = 256;
 constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kTile = 16;                        // tokens per warp tile (one m16n8k16 K-step of P V)
-constexpr int kStageTokens = kTile;              // planning granularity
 constexpr int kWarpStages = 3;                   // private ring slots per warp
 constexpr int kAhead = kWarpStages - 1;          // tiles in flight ahead of the one being consumed
 constexpr int kMaxRange = 1024;                  // selections per CTA
+constexpr int kChunk = 32;                       // index positions per interleaved chunk (one warp load)
+constexpr int kMaxChunks = kMaxRange / kChunk;   // chunks per CTA
 constexpr int kCompactIters = kMaxRange / kThreads;
 constexpr int kRecordBytes = 288;                // K data + K scales + V data + V scales
 constexpr int kStageBytes = kTile * kRecordBytes;
@@ -87,7 +92,7 @@ struct AttnParams {
   int64_t num_requests, table_width;
   const int32_t* token_to_request;
   int64_t rows;
-  int32_t splits, range;
+  int32_t splits;                // CTAs per (row, kv head); CTA s takes chunks s, s + splits, ...
   int32_t mode;                  // 0: bf16 output; 1: fp32 partial (normalised O, lse)
   int32_t vec_q;                 // 16-byte aligned query rows
   int32_t vec_o;                 // 16-byte aligned output rows
@@ -145,13 +150,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
   atomicOr(&g_error_flags, kErrWaitTimeout);
   return false;
 }
-// Global -> shared bulk copy completing on an mbarrier (no multicast).
+// Global -> shared bulk copy into this CTA, completing on an mbarrier.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
                ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
-// TMA tile::gather4: four rows of the record matrix into 4*288 contiguous bytes (no multicast).
+// TMA tile::gather4: four rows of the record matrix into 4*288 contiguous bytes of this CTA.
 __device__ __forceinline__ void gather4_g2s(uint32_t dst, const CUtensorMap* map, int32_t r0, int32_t r1, int32_t r2,
                                             int32_t r3, uint32_t bar) {
   asm volatile(
@@ -216,10 +221,8 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   const int kvh = (int)(bid % p.kv_heads);
   const int64_t row = bid / p.kv_heads;
 
-  const int64_t pos0 = (int64_t)split * p.range;
-  int64_t pos1 = pos0 + p.range;
-  if (pos1 > p.topk) pos1 = p.topk;
-  const int len = pos1 > pos0 ? (int)(pos1 - pos0) : 0;
+  const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
+  const int my_chunks = split < chunks ? (int)((chunks - 1 - split) / p.splits + 1) : 0;  // <= kMaxChunks
   const int G = p.group;
 
   if (lane == 0) {
@@ -255,9 +258,9 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   // ---------------- resolve + compact the CTA's selections ----------------
   const int32_t req = __ldg(p.token_to_request + row);
   const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
-  const int32_t* idx_row = p.indices + row * p.topk + pos0;
+  const int32_t* idx_row = p.indices + row * p.topk;
   const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
-  const int iters = (len + kThreads - 1) / kThreads;
+  const int iters = (my_chunks + kWarps - 1) / kWarps;
   uint32_t vmask = 0;
   int2 ent[kCompactIters];
   int pre[kCompactIters];
@@ -266,9 +269,10 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     ent[it] = make_int2(0, 0);
     pre[it] = 0;
     if (it < iters) {
-      const int pos = it * kThreads + tid;
+      const int lc = it * kWarps + warp;  // local chunk: global chunk split + lc * splits
+      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
       bool valid = false;
-      if (pos < len && req_ok) {
+      if (lc < my_chunks && pos < p.topk && req_ok) {
         const int32_t idx = __ldg(idx_row + pos);
         if (idx >= 0) {
           // 0 <= idx < 2^31: a 32-bit division (a page larger than that holds every index in page 0)
@@ -661,10 +665,13 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   }
 }
 
-// One warp per (row, query head): log-sum-exp merge of `splits` partials.
+// One warp per (row, query head): log-sum-exp merge of `splits` partials, split s
+// at part_out + s * out_split_stride ([rows][heads][256] dense) and
+// part_lse + s * lse_split_stride ([rows][heads] dense).
 // mode 0 -> bf16 output; mode 1 -> fp32 normalised output + merged lse.
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_out, const float* __restrict__ part_lse,
-                                                    int splits, int64_t rows, int query_heads, int mode,
+                                                    int splits, int64_t out_split_stride, int64_t lse_split_stride,
+                                                    int64_t rows, int query_heads, int mode,
                                                     __nv_bfloat16* out, int64_t o_stride_row, int64_t o_stride_head,
                                                     int vec_o, float* out_f32, float* out_lse) {
   const int lane = threadIdx.x & 31;
@@ -674,16 +681,17 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ pa
   const int64_t row = w / query_heads;
   const int head = (int)(w - row * query_heads);
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldg(part_lse + (int64_t)s * items + w));
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldg(part_lse + (int64_t)s * lse_split_stride + w));
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   float den = 0.0f;
   if (M != -INFINITY) {
     for (int s = 0; s < splits; ++s) {
-      const float lse = __ldg(part_lse + (int64_t)s * items + w);
+      const float lse = __ldg(part_lse + (int64_t)s * lse_split_stride + w);
       const float wt = exp2f(lse - M);  // 0 for -inf partials
       if (wt == 0.0f) continue;
       den += wt;
-      const float4* po = reinterpret_cast<const float4*>(part_out + ((int64_t)s * items + w) * kHeadDim + lane * 8);
+      const float4* po =
+          reinterpret_cast<const float4*>(part_out + (int64_t)s * out_split_stride + w * kHeadDim + lane * 8);
       const float4 a = __ldg(po), b = __ldg(po + 1);
       acc[0] += wt * a.x; acc[1] += wt * a.y; acc[2] += wt * a.z; acc[3] += wt * a.w;
       acc[4] += wt * b.x; acc[5] += wt * b.y; acc[6] += wt * b.z; acc[7] += wt * b.w;
@@ -774,29 +782,24 @@ bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
 
 struct Plan {
   int splits;
-  int range;
 };
 
 // Split plan.  Each CTA pays a fixed prologue (selection resolution, Q
 // fragments) and epilogue (warp combine, partial write), so CTAs stay long: a
-// batch with at least one (row, kv head) unit per SM keeps the fewest
-// splits the 1024-selection CTA limit allows; batches with fewer units than
-// SMs are split until every SM has a CTA.
+// batch with at least one (row, kv head) unit per SM keeps the fewest splits
+// the 1024-selection CTA limit allows; batches with fewer units than SMs are
+// split until every SM has a CTA, down to one 32-position chunk per CTA.
 Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   Plan pl;
   const int64_t units = rows * kv_heads;
-  const int64_t min_splits = topk > 0 ? (topk + kMaxRange - 1) / kMaxRange : 1;
-  const int64_t max_splits = topk > 0 ? (topk + kStageTokens - 1) / kStageTokens : 1;
+  const int64_t chunks = topk > 0 ? (topk + kChunk - 1) / kChunk : 1;
+  const int64_t min_splits = (chunks + kMaxChunks - 1) / kMaxChunks;
   int64_t splits = min_splits;
   const int64_t sm_count = sms > 0 ? sms : 148;
   if (units > 0 && units < sm_count) splits = (sm_count + units - 1) / units;
-  if (splits > max_splits) splits = max_splits;
+  if (splits > chunks) splits = chunks;
   if (splits < min_splits) splits = min_splits;
-  int64_t range = topk > 0 ? (topk + splits - 1) / splits : kStageTokens;
-  range = (range + kStageTokens - 1) / kStageTokens * kStageTokens;
-  if (range > kMaxRange) range = kMaxRange;
-  pl.range = (int)range;
-  pl.splits = (int)(topk > 0 ? (topk + range - 1) / range : 1);
+  pl.splits = (int)splits;
   return pl;
 }
 
@@ -905,7 +908,6 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.token_to_request = token_to_request;
   p.rows = rows;
   p.splits = pl.splits;
-  p.range = pl.range;
   p.vec_q = (aligned_to(query, 16) && q_stride_row % 8 == 0 && q_stride_head % 8 == 0) ? 1 : 0;
   p.vec_o = (!partial_mode && aligned_to(output, 16) && o_stride_row % 8 == 0 && o_stride_head % 8 == 0) ? 1 : 0;
   p.out = static_cast<__nv_bfloat16*>(output);
@@ -938,7 +940,8 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   if (pl.splits > 1) {
     const int64_t items = rows * query_heads;
     const int64_t blocks = (items * 32 + 255) / 256;
-    merge_kernel<<<(unsigned)blocks, 256, 0, s>>>(ws_out, ws_lse, pl.splits, rows, query_heads, partial_mode ? 1 : 0,
+    merge_kernel<<<(unsigned)blocks, 256, 0, s>>>(ws_out, ws_lse, pl.splits, items * kHeadDim, items, rows, query_heads,
+                                                  partial_mode ? 1 : 0,
                                                   p.out, o_stride_row, o_stride_head, p.vec_o, partial_out, partial_lse);
     if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
   }
@@ -1026,21 +1029,33 @@ extern "C" int nvqsa_sparse_attention_partial(
                        head_dim, workspace, workspace_bytes, stream);
 }
 
-extern "C" int nvqsa_merge_partials(const float* partial_out, const float* partial_lse, int32_t splits, void* output,
-                                    int64_t o_stride_row, int64_t o_stride_head, int64_t rows, int32_t query_heads,
-                                    int32_t head_dim, void* stream) {
+extern "C" int nvqsa_merge_partials_strided(const float* partial_out, int64_t out_split_stride,
+                                            const float* partial_lse, int64_t lse_split_stride, int32_t splits,
+                                            void* output, int64_t o_stride_row, int64_t o_stride_head, int64_t rows,
+                                            int32_t query_heads, int32_t head_dim, void* stream) {
   if (splits < 1 || rows < 0 || query_heads < 1) return NVQSA_ERR_BAD_SHAPE;
   if (head_dim != kHeadDim) return NVQSA_ERR_HEAD_DIM;
   if (rows == 0) return NVQSA_OK;
   if (!partial_out || !partial_lse || !output) return NVQSA_ERR_NULL_POINTER;
-  if (!aligned_to(partial_out, 16) || !aligned_to(output, 2)) return NVQSA_ERR_MISALIGNED;
-  const int vec_o = (aligned_to(output, 16) && o_stride_row % 8 == 0 && o_stride_head % 8 == 0) ? 1 : 0;
   const int64_t items = rows * query_heads;
+  if (splits > 1 && (out_split_stride < items * kHeadDim || lse_split_stride < items)) return NVQSA_ERR_BAD_SHAPE;
+  if (!aligned_to(partial_out, 16) || out_split_stride % 4 || !aligned_to(partial_lse, 4) || !aligned_to(output, 2))
+    return NVQSA_ERR_MISALIGNED;
+  const int vec_o = (aligned_to(output, 16) && o_stride_row % 8 == 0 && o_stride_head % 8 == 0) ? 1 : 0;
   const int64_t blocks = (items * 32 + 255) / 256;
-  merge_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(partial_out, partial_lse, splits, rows, query_heads, 0,
+  merge_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(partial_out, partial_lse, splits, out_split_stride,
+                                                                lse_split_stride, rows, query_heads, 0,
                                                                 static_cast<__nv_bfloat16*>(output), o_stride_row,
                                                                 o_stride_head, vec_o, nullptr, nullptr);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
+}
+
+extern "C" int nvqsa_merge_partials(const float* partial_out, const float* partial_lse, int32_t splits, void* output,
+                                    int64_t o_stride_row, int64_t o_stride_head, int64_t rows, int32_t query_heads,
+                                    int32_t head_dim, void* stream) {
+  const int64_t items = rows * (int64_t)query_heads;
+  return nvqsa_merge_partials_strided(partial_out, items * kHeadDim, partial_lse, items, splits, output, o_stride_row,
+                                      o_stride_head, rows, query_heads, head_dim, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -88,6 +88,7 @@ _SIGNATURES = {
         _I64, _I32, _I32,
         _P]),
     "nvqsa_merge_partials": (c_int, [_P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
+    "nvqsa_merge_partials_strided": (c_int, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "nvqsa_encode_rows": (c_int, [_P, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P]),
     "nvqsa_decode_rows": (c_int, [_P, _P, _I64, _I64, _I32, _P, _P, _P]),
 }

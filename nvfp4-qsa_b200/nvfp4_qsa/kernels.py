@@ -26,6 +26,7 @@ __all__ = [
     "qsa_write_cache_nvfp4",
     "qsa_sparse_paged_attention_nvfp4_partial",
     "qsa_merge_partials",
+    "qsa_merge_partials_strided",
     "attention_workspace_bytes",
 ]
 
@@ -293,3 +294,33 @@ def qsa_merge_partials(partial_out, partial_lse, output):
                                           output.data_ptr(), output.stride(0), output.stride(1),
                                           rows, query_heads, head_dim, _stream_ptr(device))
     _native.check(status, "qsa_merge_partials")
+
+
+def qsa_merge_partials_strided(partial_out, partial_lse, output):
+    """``qsa_merge_partials`` for partials whose splits are not adjacent.
+
+    ``partial_out`` [splits, rows, heads, dim] and ``partial_lse`` [splits, rows, heads]
+    fp32 may have any stride on the split dimension (e.g. views of one gathered
+    buffer that packs each rank's outputs and lse together); each split itself
+    must be dense.
+    """
+    if partial_out.dim() != 4 or partial_out.dtype != torch.float32:
+        raise ValueError("partial_out must be fp32 [splits, rows, heads, dim]")
+    splits, rows, query_heads, head_dim = partial_out.shape
+    if partial_lse.dtype != torch.float32 or tuple(partial_lse.shape) != (splits, rows, query_heads):
+        raise ValueError("partial_lse must be fp32 [splits, rows, heads]")
+    if (partial_out.stride()[1:] != (query_heads * head_dim, head_dim, 1)
+            or partial_lse.stride()[1:] != (query_heads, 1)):
+        raise ValueError("each split of partial_out / partial_lse must be dense")
+    if tuple(output.shape) != (rows, query_heads, head_dim) or output.dtype != torch.bfloat16 or output.stride(-1) != 1:
+        raise ValueError("output must be bf16 [rows, heads, dim] with contiguous last dim")
+    device = output.device
+    _check_same_device((partial_out, partial_lse), device)
+    if rows == 0:
+        return
+    lib = _native.load()
+    with _device_ctx(device):
+        status = lib.nvqsa_merge_partials_strided(
+            partial_out.data_ptr(), partial_out.stride(0), partial_lse.data_ptr(), partial_lse.stride(0), splits,
+            output.data_ptr(), output.stride(0), output.stride(1), rows, query_heads, head_dim, _stream_ptr(device))
+    _native.check(status, "qsa_merge_partials_strided")

@@ -77,7 +77,7 @@ def _load():
                                              P, I64, I64, I64, P, I64, I64, I64,
                                              P, I64, I64, I64, P, I64, I64, I64,
                                              I64, I64, I32, F, F,
-                                             P, I64, P, I64, I64, P, P, I64, I32, I32]
+                                             P, I64, P, I64, I64, P, P, I64, I32, I32, P]
         lib.orc_set_threads.restype = None
         lib.orc_set_threads.argtypes = [c_int]
         lib.orc_get_threads.restype = c_int
@@ -169,8 +169,13 @@ def write_cache(key_bits: np.ndarray, value_bits: np.ndarray, storage: np.ndarra
 
 def sparse_attention(q_bits: np.ndarray, storage: np.ndarray, indices: np.ndarray, block_table: np.ndarray,
                      token_to_request: np.ndarray, key_global_scale: float = 1.0,
-                     value_global_scale: float = 1.0) -> np.ndarray:
-    """Reader contract (kernels.py:168-345) in float64; returns fp32 [rows, qh, hd]."""
+                     value_global_scale: float = 1.0, return_lse: bool = False):
+    """Reader contract (kernels.py:168-345) in float64; returns fp32 [rows, qh, hd].
+
+    With ``return_lse`` also returns each head's base-2 log-sum-exp of the scaled
+    scores (fp32 [rows, qh], -inf where no selection is valid): the split-KV
+    partial format (src/qsa_fp8_harness.py:183-208) that merge_partials combines.
+    """
     q_bits = np.ascontiguousarray(q_bits, dtype=np.uint16)
     indices = np.ascontiguousarray(indices, dtype=np.int32)
     block_table = np.ascontiguousarray(block_table, dtype=np.int32)
@@ -179,6 +184,7 @@ def sparse_attention(q_bits: np.ndarray, storage: np.ndarray, indices: np.ndarra
     rows, qh, hd = q_bits.shape
     blocks, kvh, page, _ = storage.shape
     out = np.zeros((rows, qh, hd), np.float32)
+    lse = np.full((rows, qh), -np.inf, np.float32)
     regs = cache_regions(storage, hd)
     base = _ptr(storage)
     args = []
@@ -188,5 +194,22 @@ def sparse_attention(q_bits: np.ndarray, storage: np.ndarray, indices: np.ndarra
     _load().orc_sparse_attention(_ptr(q_bits), qh * hd, hd, *args, blocks, page, kvh, float(key_global_scale),
                                  float(value_global_scale), _ptr(indices), topk, _ptr(block_table),
                                  block_table.shape[0], block_table.shape[1], _ptr(token_to_request), _ptr(out),
-                                 rows, qh, hd)
-    return out
+                                 rows, qh, hd, _ptr(lse) if return_lse else None)
+    return (out, lse) if return_lse else out
+
+
+def merge_partials(part_out: np.ndarray, part_lse: np.ndarray) -> np.ndarray:
+    """Log-sum-exp merge of split partials (src/qsa_fp8_harness.py:308-321 semantics).
+
+    part_out: [splits, rows, qh, hd] normalised outputs; part_lse: [splits, rows, qh]
+    base-2 lse (-inf for empty splits).  Returns float64 [rows, qh, hd]; rows whose
+    splits are all empty are zero.
+    """
+    o = np.asarray(part_out, np.float64)
+    l = np.asarray(part_lse, np.float64)
+    m = l.max(axis=0)
+    safe_m = np.where(np.isfinite(m), m, 0.0)
+    w = np.where(np.isfinite(l), np.exp2(l - safe_m[None]), 0.0)
+    den = w.sum(axis=0)
+    num = (w[..., None] * o).sum(axis=0)
+    return np.where(den[..., None] > 0, num / np.where(den > 0, den, 1.0)[..., None], 0.0)

@@ -197,7 +197,8 @@ void orc_write_cache(const uint16_t* key, int64_t key_st, int64_t key_sh, const 
 
 /* Sparse paged GQA decode attention (kernels.py:168-345 masking; math in
  * float64 as src/qsa_ref.py:12-52).  out: fp32 [rows, query_heads, head_dim]
- * contiguous.  K/V are dequantised exactly (e2m1 * e4m3); the score scale is
+ * contiguous; lse_out (optional, fp32 [rows, query_heads]) receives each
+ * head's base-2 log-sum-exp, or -inf when no selection is valid.  K/V are dequantised exactly (e2m1 * e4m3); the score scale is
  * head_dim^-0.5 / gk and the output is divided by gv. */
 void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kd, int64_t kd_sb,
                           int64_t kd_st, int64_t kd_sh, const uint8_t* ks, int64_t ks_sb, int64_t ks_st,
@@ -206,7 +207,7 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
                           int64_t page_size, int32_t kv_heads, float gk, float gv, const int32_t* indices,
                           int64_t topk, const int32_t* block_table, int64_t num_requests, int64_t table_width,
                           const int32_t* token_to_request, float* out, int64_t rows, int32_t query_heads,
-                          int32_t head_dim) {
+                          int32_t head_dim, float* lse_out) {
   const int G = query_heads / kv_heads;
   const double scale = 1.0 / sqrt((double)head_dim) / (double)gk;
 #pragma omp parallel for collapse(2) schedule(dynamic)
@@ -253,6 +254,7 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
         float* orow = out + (r * query_heads + qh) * head_dim;
         if (nv == 0) { /* kernels.py:333-337: no valid selection -> zeros */
           for (int d = 0; d < head_dim; ++d) orow[d] = 0.0f;
+          if (lse_out) lse_out[r * query_heads + qh] = -INFINITY;
           continue;
         }
         double mx = -INFINITY;
@@ -272,6 +274,9 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
           for (int64_t t = 0; t < nv; ++t) acc += s[t] * V[t * head_dim + d];
           orow[d] = (float)(acc / den / (double)gv);
         }
+        /* base-2 log-sum-exp of the scaled scores, the split-KV partial format of
+         * src/qsa_fp8_harness.py:183-208 (lse = m + log2 l in log2 units) */
+        if (lse_out) lse_out[r * query_heads + qh] = (float)(mx / log(2.0) + log2(den));
       }
       free(sel_blk);
       free(sel_off);

@@ -1,0 +1,93 @@
+"""GPU: split-KV decode of one sequence across ranks, the kernels of nvfp4_qsa.distributed.
+
+On one GPU the ranks are emulated in turn: rank r writes only its own pages
+into its own cache (``SplitKV.slot_mapping`` gives -1 elsewhere and the writer
+skips those slots), computes its un-merged partial over its masked block table
+(``SplitKV.block_table``), the packed partials are stacked as the all_gather
+would leave them, and the strided log-sum-exp merge kernel combines them.  The
+result must match the oracle's unsplit attention within the reader tolerance
+and the single-GPU reader's output.  The NCCL exchange itself is covered by the
+gloo tests in tests/test_distributed_cpu.py and by ``bench.py --gpus N``.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from gpu_util import assert_attention_close
+from nvfp4_qsa import distributed as D
+from nvfp4_qsa import kernels
+from nvfp4_qsa import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _regions(storage):
+    parts = storage.transpose(1, 2).split(144, dim=-1)
+    kd, ks = parts[0].split((128, 16), dim=-1)
+    vd, vs = parts[1].split((128, 16), dim=-1)
+    return kd, ks, vd, vs
+
+
+@pytest.mark.parametrize("world,context,topk,page,rows", [
+    (2, 9000, 1024, 3136, 1),     # pages split 2/1
+    (4, 20000, 2048, 3136, 2),    # 7 pages over 4 ranks, two rows
+    (8, 30000, 4096, 256, 1),     # many small pages, 8 ranks
+    (3, 700, 96, 16, 3),          # a rank may own no selection of a row
+])
+def test_split_kv_ranks_merge_to_the_unsplit_result(world, context, topk, page, rows):
+    dev = torch.device("cuda")
+    case = W.decode_config(seed=50 + world, context=context, topk=topk, page=page, rows=rows)
+    pages = (context + page - 1) // page
+    key, value = _bits(case.key, dev), _bits(case.value, dev)
+    q = _bits(case.query, dev)
+    idx = torch.from_numpy(case.indices).to(dev)
+    t2r = torch.from_numpy(case.token_to_request).to(dev)
+    qh, hd = q.shape[1], q.shape[2]
+
+    bufs = []
+    for r in range(world):
+        sk = D.SplitKV(pages, page, world, r,
+                       block_order=torch.randperm(D.page_range(pages, world, r)[1] - D.page_range(pages, world, r)[0],
+                                                  generator=torch.Generator().manual_seed(r)))
+        storage = torch.zeros(max(sk.local_blocks, 1), 2, page, 288, dtype=torch.uint8, device=dev)
+        kd, ks, vd, vs = _regions(storage)
+        slots = sk.slot_mapping(torch.arange(context, device=dev))
+        kernels.qsa_write_cache_nvfp4(key, value, kd, ks, vd, vs, slots, 1.0, 1.0)
+        buf = sk.partial_buffer(rows, qh, hd, dev)
+        pout, plse = sk.unpack(buf, rows, qh, hd)
+        kernels.qsa_sparse_paged_attention_nvfp4_partial(q, kd, ks, vd, vs, 1.0, 1.0, idx, sk.block_table(dev), t2r,
+                                                         pout, plse)
+        bufs.append(buf)
+    gathered = torch.stack(bufs)  # what all_gather_into_tensor leaves, viewed [world, buffer]
+    outs, lses = D.SplitKV.unpack(gathered, rows, qh, hd)
+    merged = torch.empty_like(q)
+    kernels.qsa_merge_partials_strided(outs, lses, merged)
+    torch.cuda.synchronize()
+
+    storage_all = np.zeros((case.blocks, 2, page, 288), np.uint8)
+    oracle.write_cache(case.key, case.value, storage_all, case.slots)
+    expected = oracle.sparse_attention(case.query, storage_all, case.indices, case.block_table, case.token_to_request)
+    assert_attention_close(merged, expected, "split-kv")
+
+    # and the same as the one-GPU reader on the whole cache
+    full = torch.from_numpy(storage_all).to(dev)
+    single = torch.empty_like(q)
+    kernels.qsa_sparse_paged_attention_nvfp4(q, *_regions(full), 1.0, 1.0, idx,
+                                             torch.from_numpy(case.block_table).to(dev), t2r, single)
+    torch.cuda.synchronize()
+    assert (merged.float() - single.float()).abs().max().item() <= 2e-2
+
+
+def test_strided_merge_rejects_overlapping_splits():
+    dev = torch.device("cuda")
+    outs = torch.zeros(2, 1, 24, 256, device=dev)
+    lses = torch.zeros(2, 1, 24, device=dev)
+    out = torch.empty(1, 24, 256, dtype=torch.bfloat16, device=dev)
+    overlapping = outs.view(-1)[: 24 * 256 + 16].as_strided((2, 1, 24, 256), (16, 24 * 256, 256, 1))
+    with pytest.raises(ValueError):
+        kernels.qsa_merge_partials_strided(overlapping, lses, out)
