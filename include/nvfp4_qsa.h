@@ -120,7 +120,11 @@ int nvqsa_sparse_attention_workspace_size(
  * finite and positive (NVQSA_ERR_BAD_SHAPE otherwise).
  * workspace : device memory of at least nvqsa_sparse_attention_workspace_size
  *             bytes (may be NULL when that size is 0); contents need no
- *             initialisation and are dead after the call.
+ *             initialisation and are dead after the call.  It holds the
+ *             split-KV partials and one arrival counter per (row, kv head),
+ *             which the call zeroes on `stream` (a memset node when captured)
+ *             before its one kernel launch; the last CTA of each (row, kv
+ *             head) merges that unit's partials.
  */
 int nvqsa_sparse_attention(
     const void* query, int64_t q_stride_row, int64_t q_stride_head,
@@ -241,8 +245,9 @@ int nvqsa_decode_rows(
  * that first call outside any stream capture.  All calls on a device share
  * the one buffer, so calls that may overlap on the GPU (different streams
  * without ordering between them) race and must be serialised by the caller.
- * Nothing in the buffer needs to start at zero: each call writes every
- * partial it later reads.  No counterpart in the reference.
+ * Nothing in the buffer needs to start at zero: each call zeroes its
+ * arrival counters on its stream and writes every partial it later reads.
+ * No counterpart in the reference.
  */
 #define NVQSA_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -94,6 +94,12 @@ struct AttnParams {
   int64_t rows;
   int32_t splits;                // CTAs per (row, kv head); CTA s takes chunks s, s + splits, ...
   int32_t mode;                  // 0: bf16 output; 1: fp32 partial (normalised O, lse)
+  int32_t cluster;               // > 1: the splits of a (row, kv head) form one thread-block cluster of this size
+  int32_t fuse;                  // splits > cluster limit: the last CTA of each (row, kv head) merges the splits
+  int32_t final_mode;            // merged result: 0 -> bf16 `out`; 1 -> fp32 final_out / final_lse
+  unsigned int* counters;        // [rows * kv_heads] arrival counters (zeroed before the launch)
+  float* final_out;              // [rows][query_heads][256]
+  float* final_lse;              // [rows][query_heads]
   int32_t vec_q;                 // 16-byte aligned query rows
   int32_t vec_o;                 // 16-byte aligned output rows
   __nv_bfloat16* out;
@@ -107,11 +113,11 @@ struct __align__(128) Smem {
   uint4 qfrag[16][32];                             // Q A-fragments: [k-step][lane] -> {a0a1,a2a3,a4a5,a6a7}
   int2 sel[kMaxRange];                             // (physical block, token in page) of valid selections
   unsigned long long full_bar[kWarps][kWarpStages];
-  float qmul[16];
   float smul[16];
   int cnt[kCompactIters][kWarps];
   int total;
   int abort;
+  int last;
 };
 
 __device__ unsigned int g_error_flags;       // bit 0: an mbarrier wait ran out
@@ -166,6 +172,30 @@ __device__ __forceinline__ void gather4_g2s(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Distributed shared memory of a thread-block cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float4 cluster_ld_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ int cluster_ld_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// Every thread of every CTA of the cluster arrives; shared-memory writes before it are visible after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
@@ -200,9 +230,96 @@ __device__ __forceinline__ int group_token(int g, int j) {
 
 // Head dimensions covered by fragment k-step s (0..15) for mma thread-in-group c:
 // k-steps 0..7 walk 16-byte chunk c of the 128 K bytes, 8..15 walk chunk 4+c, so
-// each lane's K bytes are two 16-byte loads.  Returns the first of 4 dims;
-// a0a1 / b0b1 hold dims +0,+1 and a4a5 / b2b3 hold +2,+3.
-__device__ __forceinline__ int frag_dim(int s, int c) { return (s < 8) ? 32 * c + 4 * s : 128 + 32 * c + 4 * (s - 8); }
+// each lane's K bytes are two 16-byte loads.  The first of the k-step's 4 dims is
+// d = (s < 8) ? 32c + 4s : 128 + 32c + 4(s - 8); a0a1 / b0b1 hold dims d, d+1
+// and a4a5 / b2b3 hold d+2, d+3.  Inverse, used to place Q: c = (d % 128) / 32,
+// s = (d % 32) / 4 + 8 * (d / 128).
+
+// Log-sum-exp merge of `splits` partials of one (row, query head) by one warp;
+// lane L covers dims [8L, 8L + 8).  Split s of the outputs starts at
+// part_out + s * out_split_stride ([rows][heads][256] dense), of the lse at
+// part_lse + s * lse_split_stride ([rows][heads] dense).  Loads go through L2
+// (ld.global.cg): inside the attention kernel the partials were written by
+// other CTAs of the same launch.
+struct MergeArgs {
+  const float* part_out;
+  const float* part_lse;
+  int splits;
+  int64_t out_split_stride, lse_split_stride;
+  int mode;                       // 0: bf16 out; 1: fp32 out_f32 + out_lse
+  __nv_bfloat16* out;
+  int64_t o_stride_row, o_stride_head;
+  int vec_o;
+  float* out_f32;
+  float* out_lse;
+};
+
+__device__ __forceinline__ void merge_item(const MergeArgs& a, int64_t row, int head, int64_t w, int lane) {
+  // Four splits per round, every load of a round issued before any is used.
+  float M = -INFINITY;
+  for (int s0 = 0; s0 < a.splits; s0 += 4) {
+    float l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      l[u] = s0 + u < a.splits ? __ldcg(a.part_lse + (int64_t)(s0 + u) * a.lse_split_stride + w) : -INFINITY;
+    M = fmaxf(M, fmaxf(fmaxf(l[0], l[1]), fmaxf(l[2], l[3])));
+  }
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float den = 0.0f;
+  if (M != -INFINITY) {
+    for (int s0 = 0; s0 < a.splits; s0 += 4) {
+      float l[4];
+      float4 x[4], y[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        l[u] = -INFINITY;
+        x[u] = y[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s0 + u < a.splits) {
+          const int64_t s = s0 + u;
+          l[u] = __ldcg(a.part_lse + s * a.lse_split_stride + w);
+          const float4* po = reinterpret_cast<const float4*>(a.part_out + s * a.out_split_stride + w * kHeadDim +
+                                                             lane * 8);
+          x[u] = __ldcg(po);
+          y[u] = __ldcg(po + 1);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float wt = l[u] == -INFINITY ? 0.0f : exp2f(l[u] - M);  // empty partials weigh 0
+        den += wt;
+        acc[0] += wt * x[u].x; acc[1] += wt * x[u].y; acc[2] += wt * x[u].z; acc[3] += wt * x[u].w;
+        acc[4] += wt * y[u].x; acc[5] += wt * y[u].y; acc[6] += wt * y[u].z; acc[7] += wt * y[u].w;
+      }
+    }
+  }
+  const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] *= inv;
+  if (a.mode == 0) {
+    __nv_bfloat16* op = a.out + row * a.o_stride_row + (int64_t)head * a.o_stride_head + lane * 8;
+    uint32_t u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+      u[i] = *reinterpret_cast<uint32_t*>(&b);
+    }
+    if (a.vec_o) {
+      *reinterpret_cast<uint4*>(op) = make_uint4(u[0], u[1], u[2], u[3]);
+    } else {
+      unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        os[2 * i] = (unsigned short)(u[i] & 0xffffu);
+        os[2 * i + 1] = (unsigned short)(u[i] >> 16);
+      }
+    }
+  } else {
+    float4* op = reinterpret_cast<float4*>(a.out_f32 + w * kHeadDim + lane * 8);
+    op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    if (lane == 0) a.out_lse[w] = den > 0.0f ? M + log2f(den) : -INFINITY;
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -232,66 +349,103 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   }
   if (tid == 0) sm.abort = 0;
 
-  // ---------------- Q pre-scale: per-head power of two (exact), folded into the score scale ----------------
-  for (int j = warp; j < 16; j += kWarps) {
-    int e = 0;
+  // ---------------- prologue: all independent global loads first ----------------
+  // Selection indices of this CTA's chunks (chunk split + lc * splits, lc = it * kWarps + warp).
+  const int32_t req = __ldg(p.token_to_request + row);
+  const int32_t* idx_row = p.indices + row * p.topk;
+  const int iters = (my_chunks + kWarps - 1) / kWarps;
+  int32_t iv[kCompactIters];
+#pragma unroll
+  for (int it = 0; it < kCompactIters; ++it) {
+    const int lc = it * kWarps + warp;
+    const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
+    iv[it] = (lc < my_chunks && pos < p.topk) ? __ldg(idx_row + pos) : -1;
+  }
+  // Query heads warp, warp + 4, warp + 8, warp + 12 of this kv head; lane L holds dims [8L, 8L + 8).
+  uint32_t qw[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int j = warp + kWarps * i;
+    qw[i][0] = qw[i][1] = qw[i][2] = qw[i][3] = 0u;
     if (j < G) {
-      const unsigned short* qs =
-          reinterpret_cast<const unsigned short*>(p.q + row * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head) +
-          lane * 8;
-      uint32_t amax = 0;
+      const __nv_bfloat16* qrow = p.q + row * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
+      if (p.vec_q) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
+        qw[i][0] = v.x; qw[i][1] = v.y; qw[i][2] = v.z; qw[i][3] = v.w;
+      } else {
+        const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) amax = max(amax, ((uint32_t)__ldg(qs + i) << 16) & 0x7fffffffu);
-#pragma unroll
-      for (int m = 16; m; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
-      if (amax != 0 && amax < 0x7f800000u) {
-        e = 14 - ilogbf(__uint_as_float(amax));
-        e = max(-126, min(126, e));
+        for (int t = 0; t < 4; ++t) qw[i][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
       }
     }
-    if (lane == 0) {
-      sm.qmul[j] = ldexpf(1.0f, e);
-      sm.smul[j] = ldexpf(p.score_scale, -e);
+  }
+  // Block-table entries of the selections (kernels.py:236-257 masking).
+  const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
+  const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
+  // 0 <= idx < 2^31: a 32-bit division (a page larger than that holds every index in page 0)
+  const bool huge_page = p.page_size > 0x7fffffffLL;
+  int32_t phys[kCompactIters], offs[kCompactIters];
+#pragma unroll
+  for (int it = 0; it < kCompactIters; ++it) {
+    phys[it] = -1;
+    offs[it] = 0;
+    const int32_t idx = iv[it];
+    if (req_ok && idx >= 0) {
+      const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
+      if ((int64_t)lpage < p.table_width) {
+        phys[it] = __ldg(bt_row + lpage);
+        offs[it] = huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size);
+      }
     }
   }
 
-  // ---------------- resolve + compact the CTA's selections ----------------
-  const int32_t req = __ldg(p.token_to_request + row);
-  const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
-  const int32_t* idx_row = p.indices + row * p.topk;
-  const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
-  const int iters = (my_chunks + kWarps - 1) / kWarps;
+  // ---------------- Q: per-head power-of-two pre-scale (exact) into f16 mma fragments ----------------
+  // Fragment k-step ks, lane (r, c): a0a1 = Q[r][d, d+1], a2a3 = Q[r+8][d, d+1], a4a5 = Q[r][d+2, d+3],
+  // a6a7 = Q[r+8][d+2, d+3] with d the first dim of k-step ks for thread-in-group c; heads >= G stay zero.
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int j = warp + kWarps * i;
+    uint32_t amax = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      amax = max(amax, max((qw[i][t] << 16) & 0x7fffffffu, qw[i][t] & 0x7fff0000u));
+#pragma unroll
+    for (int m = 16; m; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    int e = 0;
+    if (amax != 0 && amax < 0x7f800000u) {
+      e = 14 - ilogbf(__uint_as_float(amax));
+      e = max(-126, min(126, e));
+    }
+    if (lane == 0) sm.smul[j] = ldexpf(p.score_scale, -e);
+    const float mul = ldexpf(1.0f, e);
+    const int hh = j >> 3, rr = j & 7;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int d = 8 * lane + 4 * g;
+      const int cc = (d & 127) >> 5;
+      const int ks = ((d & 31) >> 2) + ((d >> 7) << 3);
+      uint32_t* f = reinterpret_cast<uint32_t*>(&sm.qfrag[ks][4 * rr + cc]);
+      const uint32_t x0 = qw[i][2 * g], x1 = qw[i][2 * g + 1];
+      f[hh] = pack_half2(bf16_lo(x0) * mul, bf16_hi(x0) * mul);
+      f[2 + hh] = pack_half2(bf16_lo(x1) * mul, bf16_hi(x1) * mul);
+    }
+  }
+
+  // ---------------- compact the valid selections ----------------
   uint32_t vmask = 0;
-  int2 ent[kCompactIters];
   int pre[kCompactIters];
 #pragma unroll
   for (int it = 0; it < kCompactIters; ++it) {
-    ent[it] = make_int2(0, 0);
     pre[it] = 0;
     if (it < iters) {
-      const int lc = it * kWarps + warp;  // local chunk: global chunk split + lc * splits
-      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
-      bool valid = false;
-      if (lc < my_chunks && pos < p.topk && req_ok) {
-        const int32_t idx = __ldg(idx_row + pos);
-        if (idx >= 0) {
-          // 0 <= idx < 2^31: a 32-bit division (a page larger than that holds every index in page 0)
-          const bool huge_page = p.page_size > 0x7fffffffLL;
-          const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
-          if ((int64_t)lpage < p.table_width) {
-            const int32_t phys = __ldg(bt_row + lpage);
-            valid = phys >= 0 && (int64_t)phys < p.num_blocks;
-            ent[it] = make_int2(phys, huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size));
-          }
-        }
-      }
+      const bool valid = phys[it] >= 0 && (int64_t)phys[it] < p.num_blocks;
       const uint32_t b = __ballot_sync(0xffffffffu, valid);
       pre[it] = __popc(b & ((1u << lane) - 1u));
       if (valid) vmask |= 1u << it;
       if (lane == 0) sm.cnt[it][warp] = __popc(b);
     }
   }
-  __syncthreads();  // exponents and per-warp counts visible
+  __syncthreads();  // exponents, fragments and per-warp counts visible
   {
     int base_all = 0;
 #pragma unroll
@@ -299,43 +453,12 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       if (it < iters) {
         int base = base_all;
         for (int w = 0; w < warp; ++w) base += sm.cnt[it][w];
-        if (vmask & (1u << it)) sm.sel[base + pre[it]] = ent[it];
+        if (vmask & (1u << it)) sm.sel[base + pre[it]] = make_int2(phys[it], offs[it]);
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) base_all += sm.cnt[it][w];
       }
     }
     if (tid == 0) sm.total = base_all;
-  }
-  // Q fragments in shared memory, k-steps 4w..4w+3 built by warp w:
-  // a0a1 = Q[r][d, d+1], a2a3 = Q[r+8][d, d+1], a4a5 = Q[r][d+2, d+3], a6a7 = Q[r+8][d+2, d+3].
-#pragma unroll
-  for (int ks = 4 * warp; ks < 4 * warp + 4; ++ks) {
-    const int d = frag_dim(ks, c);
-    uint32_t w4[4];
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      const int j = r + 8 * hh;
-      uint32_t lo = 0, hi = 0;
-      if (j < G) {
-        const uint32_t* qp = reinterpret_cast<const uint32_t*>(p.q + row * p.q_stride_row +
-                                                               (int64_t)(kvh * G + j) * p.q_stride_head + d);
-        const float mul = sm.qmul[j];
-        uint32_t x0, x1;
-        if (p.vec_q) {
-          x0 = __ldg(qp);
-          x1 = __ldg(qp + 1);
-        } else {
-          const unsigned short* qs = reinterpret_cast<const unsigned short*>(qp);
-          x0 = (uint32_t)__ldg(qs) | ((uint32_t)__ldg(qs + 1) << 16);
-          x1 = (uint32_t)__ldg(qs + 2) | ((uint32_t)__ldg(qs + 3) << 16);
-        }
-        lo = pack_half2(bf16_lo(x0) * mul, bf16_hi(x0) * mul);
-        hi = pack_half2(bf16_lo(x1) * mul, bf16_hi(x1) * mul);
-      }
-      w4[hh] = lo;
-      w4[2 + hh] = hi;
-    }
-    sm.qfrag[ks][lane] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
   }
   __syncthreads();
   const int n = sm.total;
@@ -575,25 +698,27 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       mbar_wait(smem_u32(&sm.full_bar[warp][k2 % kWarpStages]), (uint32_t)((k2 / kWarpStages) & 1), kDrainSpinLimit);
   }
   __syncthreads();  // every warp left its loop: no bulk copy is in flight, the rings are free
-  if (sm.abort) return;
+  const bool aborted = sm.abort != 0;
+  if (aborted && p.cluster <= 1) return;  // a cluster CTA still takes the cluster barriers below
 
-  // Two rounds over shared memory: warps 2,3 -> 0,1, then warp 1 -> 0.
-  float* comb_o = reinterpret_cast<float*>(&sm.rec[0][0][0]);    // [2][lane][128]
-  float* comb_ml = comb_o + 2 * 32 * 128;                         // [2][lane][4]
+  // Two rounds over shared memory: warps 2,3 -> 0,1, then warp 1 -> 0.  Slot q = sender * 32 + lane;
+  // float4 i of slot q at comb[i * 64 + q], so that a warp's stores and loads are contiguous.
+  float4* comb = reinterpret_cast<float4*>(&sm.rec[0][0][0]);   // [32][64] float4 + [64] (m, m8, l, l8)
+  float4* comb_ml = comb + 32 * 64;
 #pragma unroll
   for (int round = 0; round < 2; ++round) {
+    if (aborted) break;  // CTA-uniform
     const int senders = round == 0 ? 2 : 1;  // warps [senders, 2*senders) send to warp - senders
     if (warp >= senders && warp < 2 * senders) {
-      float* o = comb_o + ((warp - senders) * 32 + lane) * 128;
+      const int q = (warp - senders) * 32 + lane;
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        reinterpret_cast<float4*>(o)[i] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
-      reinterpret_cast<float4*>(comb_ml)[(warp - senders) * 32 + lane] = make_float4(m_r, m_r8, l_r, l_r8);
+      for (int i = 0; i < 32; ++i) comb[i * 64 + q] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
+      comb_ml[q] = make_float4(m_r, m_r8, l_r, l_r8);
     }
     __syncthreads();
     if (warp < senders) {
-      const float* o = comb_o + (warp * 32 + lane) * 128;
-      const float4 ml = reinterpret_cast<const float4*>(comb_ml)[warp * 32 + lane];
+      const int q = warp * 32 + lane;
+      const float4 ml = comb_ml[q];
       const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
       const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
       const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
@@ -603,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       m_r8 = M_r8;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float4 v = reinterpret_cast<const float4*>(o)[i];
+        const float4 v = comb[i * 64 + q];
         oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
         oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
         oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
@@ -612,56 +737,126 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     }
     __syncthreads();
   }
-  if (warp != 0) return;
 
-  // lane (r, c) holds dims 128*h + 32c + i (oacc[16h + i][2hh]) and +16 (oacc[16h + i][2hh + 1]).
+  if (p.cluster > 1) {
+    // Split-KV inside a thread-block cluster (the CTA's rank is its split): every CTA publishes
+    // warp 0's (O, m, l) in its own shared memory, rank 0 merges the other ranks' over distributed
+    // shared memory and stores the result; no global workspace, no counters.
+    if (warp == 0 && !aborted) {
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    const int j = r + 8 * hh;
-    if (j >= G) continue;
-    const float l = hh ? l_r8 : l_r;
-    const float m = hh ? m_r8 : m_r;
-    // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
-    const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
-    const int head = kvh * G + j;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        v[i] = oacc[16 * h + i][2 * hh] * inv;
-        v[16 + i] = oacc[16 * h + i][2 * hh + 1] * inv;
-      }
-      const int d0 = 128 * h + 32 * c;
-      if (p.mode == 0) {
-        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d0;
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-          w[i] = *reinterpret_cast<uint32_t*>(&b);
+      for (int i = 0; i < 32; ++i) comb[i * 64 + lane] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
+      comb_ml[lane] = make_float4(m_r, m_r8, l_r, l_r8);
+    }
+    cluster_sync();
+    bool ok = !aborted;
+    if (split == 0 && warp == 0 && ok) {
+      for (int rk = 1; rk < p.cluster; ++rk) {
+        if (cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk))) {
+          ok = false;
+          continue;
         }
-        if (p.vec_o) {
+        const uint32_t cb = cluster_map(smem_u32(comb), (uint32_t)rk);
+        const float4 ml = cluster_ld_f4(cb + (uint32_t)(32 * 64 + lane) * 16u);
+        const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
+        const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
+        const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
+        l_r = l_r * a0 + ml.z * b0;
+        l_r8 = l_r8 * a1 + ml.w * b1;
+        m_r = M_r;
+        m_r8 = M_r8;
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            reinterpret_cast<uint4*>(op)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-        } else {
-          unsigned short* os = reinterpret_cast<unsigned short*>(op);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            os[2 * i] = (unsigned short)(w[i] & 0xffffu);
-            os[2 * i + 1] = (unsigned short)(w[i] >> 16);
-          }
+        for (int i = 0; i < 32; ++i) {
+          const float4 v = cluster_ld_f4(cb + (uint32_t)(i * 64 + lane) * 16u);
+          oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
+          oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
+          oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
+          oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
         }
-      } else {
-        const int64_t slot = ((int64_t)split * p.rows + row) * p.query_heads + head;
-        float* op = p.part_out + slot * kHeadDim + d0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          reinterpret_cast<float4*>(op)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        if (h == 0 && c == 0) p.part_lse[slot] = l > 0.0f ? m + log2f(fmaxf(l, 1.0e-20f)) : -INFINITY;
       }
     }
+    cluster_sync();  // ranks > 0 keep their shared memory until rank 0 has read it
+    if (split != 0 || !ok) return;
+  }
+
+  if (warp == 0) {
+    // lane (r, c) holds dims 128*h + 32c + i (oacc[16h + i][2hh]) and +16 (oacc[16h + i][2hh + 1]).
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = r + 8 * hh;
+      if (j >= G) continue;
+      const float l = hh ? l_r8 : l_r;
+      const float m = hh ? m_r8 : m_r;
+      // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
+      const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
+      const int head = kvh * G + j;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          v[i] = oacc[16 * h + i][2 * hh] * inv;
+          v[16 + i] = oacc[16 * h + i][2 * hh + 1] * inv;
+        }
+        const int d0 = 128 * h + 32 * c;
+        if (p.mode == 0) {
+          __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d0;
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&b);
+          }
+          if (p.vec_o) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              reinterpret_cast<uint4*>(op)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          } else {
+            unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              os[2 * i] = (unsigned short)(w[i] & 0xffffu);
+              os[2 * i + 1] = (unsigned short)(w[i] >> 16);
+            }
+          }
+        } else {
+          const int64_t slot = ((int64_t)split * p.rows + row) * p.query_heads + head;
+          float* op = p.part_out + slot * kHeadDim + d0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(op)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          if (h == 0 && c == 0) p.part_lse[slot] = l > 0.0f ? m + log2f(fmaxf(l, 1.0e-20f)) : -INFINITY;
+        }
+      }
+    }
+  }
+
+  // ---------------- split-KV: the last CTA of this (row, kv head) merges the splits ----------------
+  if (!p.fuse) return;
+  if (warp == 0) {
+    __threadfence();  // this CTA's partial is visible device-wide before its arrival is counted
+    __syncwarp();
+    if (lane == 0)
+      sm.last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(p.splits - 1);
+  }
+  __syncthreads();
+  if (!sm.last) return;
+  __threadfence();  // the other CTAs' partials, counted before ours, are visible
+  MergeArgs a;
+  a.part_out = p.part_out;
+  a.part_lse = p.part_lse;
+  a.splits = p.splits;
+  a.out_split_stride = p.rows * p.query_heads * kHeadDim;
+  a.lse_split_stride = p.rows * p.query_heads;
+  a.mode = p.final_mode;
+  a.out = p.out;
+  a.o_stride_row = p.o_stride_row;
+  a.o_stride_head = p.o_stride_head;
+  a.vec_o = p.vec_o;
+  a.out_f32 = p.final_out;
+  a.out_lse = p.final_lse;
+  for (int j = warp; j < G; j += kWarps) {
+    const int head = kvh * G + j;
+    merge_item(a, row, head, row * p.query_heads + head, lane);
   }
 }
 
@@ -669,61 +864,12 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
 // at part_out + s * out_split_stride ([rows][heads][256] dense) and
 // part_lse + s * lse_split_stride ([rows][heads] dense).
 // mode 0 -> bf16 output; mode 1 -> fp32 normalised output + merged lse.
-__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ part_out, const float* __restrict__ part_lse,
-                                                    int splits, int64_t out_split_stride, int64_t lse_split_stride,
-                                                    int64_t rows, int query_heads, int mode,
-                                                    __nv_bfloat16* out, int64_t o_stride_row, int64_t o_stride_head,
-                                                    int vec_o, float* out_f32, float* out_lse) {
+__global__ void __launch_bounds__(256) merge_kernel(MergeArgs a, int64_t rows, int query_heads) {
   const int lane = threadIdx.x & 31;
   const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t items = rows * query_heads;
-  if (w >= items) return;
+  if (w >= rows * query_heads) return;
   const int64_t row = w / query_heads;
-  const int head = (int)(w - row * query_heads);
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldg(part_lse + (int64_t)s * lse_split_stride + w));
-  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  float den = 0.0f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < splits; ++s) {
-      const float lse = __ldg(part_lse + (int64_t)s * lse_split_stride + w);
-      const float wt = exp2f(lse - M);  // 0 for -inf partials
-      if (wt == 0.0f) continue;
-      den += wt;
-      const float4* po =
-          reinterpret_cast<const float4*>(part_out + (int64_t)s * out_split_stride + w * kHeadDim + lane * 8);
-      const float4 a = __ldg(po), b = __ldg(po + 1);
-      acc[0] += wt * a.x; acc[1] += wt * a.y; acc[2] += wt * a.z; acc[3] += wt * a.w;
-      acc[4] += wt * b.x; acc[5] += wt * b.y; acc[6] += wt * b.z; acc[7] += wt * b.w;
-    }
-  }
-  const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] *= inv;
-  if (mode == 0) {
-    __nv_bfloat16* op = out + row * o_stride_row + (int64_t)head * o_stride_head + lane * 8;
-    uint32_t u[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-      u[i] = *reinterpret_cast<uint32_t*>(&b);
-    }
-    if (vec_o) {
-      *reinterpret_cast<uint4*>(op) = make_uint4(u[0], u[1], u[2], u[3]);
-    } else {
-      unsigned short* os = reinterpret_cast<unsigned short*>(op);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        os[2 * i] = (unsigned short)(u[i] & 0xffffu);
-        os[2 * i + 1] = (unsigned short)(u[i] >> 16);
-      }
-    }
-  } else {
-    float4* op = reinterpret_cast<float4*>(out_f32 + w * kHeadDim + lane * 8);
-    op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    if (lane == 0) out_lse[w] = den > 0.0f ? M + log2f(den) : -INFINITY;
-  }
+  merge_item(a, row, (int)(w - row * query_heads), w, lane);
 }
 
 // ---------------- host-side planning ----------------
@@ -782,7 +928,9 @@ bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
 
 struct Plan {
   int splits;
+  int cluster;  // splits of one (row, kv head) merged inside a cluster of this size (1: no cluster)
 };
+constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
 
 // Split plan.  Each CTA pays a fixed prologue (selection resolution, Q
 // fragments) and epilogue (warp combine, partial write), so CTAs stay long: a
@@ -800,13 +948,27 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   if (splits > chunks) splits = chunks;
   if (splits < min_splits) splits = min_splits;
   pl.splits = (int)splits;
+  pl.cluster = (splits > 1 && splits <= kMaxClusterSplits) ? (int)splits : 1;
   return pl;
 }
 
-size_t workspace_for(const Plan& pl, int64_t rows, int query_heads) {
-  if (pl.splits <= 1) return 0;
+// Workspace of a split launch: partial outputs [splits][rows][heads][256] fp32,
+// partial lse [splits][rows][heads] fp32 (padded to 256 bytes), then one
+// arrival counter per (row, kv head), zeroed on the launch's stream.
+struct Workspace {
+  size_t lse_offset, counter_offset, bytes;
+};
+Workspace workspace_layout(const Plan& pl, int64_t rows, int query_heads, int kv_heads) {
+  Workspace w{0, 0, 0};
+  if (pl.splits <= 1 || pl.cluster > 1) return w;
   const size_t items = (size_t)pl.splits * rows * query_heads;
-  return items * kHeadDim * sizeof(float) + ((items * sizeof(float) + 255) / 256) * 256;
+  w.lse_offset = items * kHeadDim * sizeof(float);
+  w.counter_offset = w.lse_offset + ((items * sizeof(float) + 255) / 256) * 256;
+  w.bytes = w.counter_offset + (size_t)rows * kv_heads * sizeof(unsigned int);
+  return w;
+}
+size_t workspace_for(const Plan& pl, int64_t rows, int query_heads, int kv_heads) {
+  return workspace_layout(pl, rows, query_heads, kv_heads).bytes;
 }
 
 // Dynamic shared memory above 48 KB is opted into once per device.
@@ -863,7 +1025,8 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   const int sms = device_sm_count();
   if (sms <= 0) return NVQSA_ERR_CUDA;
   const Plan pl = make_plan(rows, kv_heads, topk, sms);
-  const size_t need = workspace_for(pl, rows, query_heads);
+  const Workspace wl = workspace_layout(pl, rows, query_heads, kv_heads);
+  const size_t need = wl.bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned_to(workspace, 16))) return NVQSA_ERR_WORKSPACE;
   if ((int64_t)pl.splits * rows * kv_heads > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;
 
@@ -913,14 +1076,23 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.out = static_cast<__nv_bfloat16*>(output);
   p.o_stride_row = o_stride_row;
   p.o_stride_head = o_stride_head;
-  float* ws_out = nullptr;
-  float* ws_lse = nullptr;
-  if (pl.splits > 1) {
-    ws_out = static_cast<float*>(workspace);
-    ws_lse = ws_out + (size_t)pl.splits * rows * query_heads * kHeadDim;
+  p.fuse = 0;
+  p.cluster = pl.cluster;
+  p.final_mode = partial_mode ? 1 : 0;
+  p.counters = nullptr;
+  p.final_out = partial_out;
+  p.final_lse = partial_lse;
+  if (pl.cluster > 1) {  // rank 0 of each cluster stores the merged result like an unsplit CTA
+    p.mode = partial_mode ? 1 : 0;
+    p.part_out = partial_out;
+    p.part_lse = partial_lse;
+  } else if (pl.splits > 1) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
     p.mode = 1;
-    p.part_out = ws_out;
-    p.part_lse = ws_lse;
+    p.fuse = 1;
+    p.part_out = reinterpret_cast<float*>(ws);
+    p.part_lse = reinterpret_cast<float*>(ws + wl.lse_offset);
+    p.counters = reinterpret_cast<unsigned int*>(ws + wl.counter_offset);
   } else if (partial_mode) {
     p.mode = 1;
     p.part_out = partial_out;
@@ -934,17 +1106,27 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   const size_t smem = sizeof(Smem) + 128;  // + slack for the 128-byte alignment of the base
   if (const int st = configure_smem(smem)) return st;
   cudaStream_t s = as_stream(stream);
+  if (p.fuse && cudaMemsetAsync(p.counters, 0, (size_t)rows * kv_heads * sizeof(unsigned int), s) != cudaSuccess)
+    return NVQSA_ERR_LAUNCH;
   const int64_t grid = (int64_t)pl.splits * rows * kv_heads;
-  sparse_attention_kernel<<<(unsigned)grid, kThreads, smem, s>>>(p);
-  if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
-  if (pl.splits > 1) {
-    const int64_t items = rows * query_heads;
-    const int64_t blocks = (items * 32 + 255) / 256;
-    merge_kernel<<<(unsigned)blocks, 256, 0, s>>>(ws_out, ws_lse, pl.splits, items * kHeadDim, items, rows, query_heads,
-                                                  partial_mode ? 1 : 0,
-                                                  p.out, o_stride_row, o_stride_head, p.vec_o, partial_out, partial_lse);
-    if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
+  if (pl.cluster > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)pl.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, sparse_attention_kernel, p) != cudaSuccess) return NVQSA_ERR_LAUNCH;
+  } else {
+    sparse_attention_kernel<<<(unsigned)grid, kThreads, smem, s>>>(p);
   }
+  if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
   return NVQSA_OK;
 }
 
@@ -974,7 +1156,7 @@ extern "C" int nvqsa_sparse_attention_workspace_size(int64_t rows, int32_t query
   if (rows == 0) return NVQSA_OK;
   const int sms = device_sm_count();
   if (sms <= 0) return NVQSA_ERR_CUDA;
-  *workspace_bytes = workspace_for(make_plan(rows, kv_heads, topk, sms), rows, query_heads);
+  *workspace_bytes = workspace_for(make_plan(rows, kv_heads, topk, sms), rows, query_heads, kv_heads);
   return NVQSA_OK;
 }
 
@@ -1043,10 +1225,20 @@ extern "C" int nvqsa_merge_partials_strided(const float* partial_out, int64_t ou
     return NVQSA_ERR_MISALIGNED;
   const int vec_o = (aligned_to(output, 16) && o_stride_row % 8 == 0 && o_stride_head % 8 == 0) ? 1 : 0;
   const int64_t blocks = (items * 32 + 255) / 256;
-  merge_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(partial_out, partial_lse, splits, out_split_stride,
-                                                                lse_split_stride, rows, query_heads, 0,
-                                                                static_cast<__nv_bfloat16*>(output), o_stride_row,
-                                                                o_stride_head, vec_o, nullptr, nullptr);
+  MergeArgs a;
+  a.part_out = partial_out;
+  a.part_lse = partial_lse;
+  a.splits = splits;
+  a.out_split_stride = out_split_stride;
+  a.lse_split_stride = lse_split_stride;
+  a.mode = 0;
+  a.out = static_cast<__nv_bfloat16*>(output);
+  a.o_stride_row = o_stride_row;
+  a.o_stride_head = o_stride_head;
+  a.vec_o = vec_o;
+  a.out_f32 = nullptr;
+  a.out_lse = nullptr;
+  merge_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(a, rows, query_heads);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }
 

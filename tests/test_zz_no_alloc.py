@@ -72,7 +72,7 @@ def test_noalloc_matches_regular_entry_point_on_two_calls():
 def test_noalloc_rejects_problems_beyond_its_buffer():
     lib = _native.load()
     case, regions, q, idx, bt, t2r = _storage_case(33)
-    rows, topk = 4096, 2048  # partials of ~2 splits x 4096 rows x 24 heads x 1 KiB > 16 MiB
+    rows, topk = 4096, 16384  # 16 splits (beyond a cluster) x 4096 rows x 24 heads x 1 KiB of partials > 16 MiB
     assert kernels.attention_workspace_bytes(rows, 24, 2, 256, topk) > (16 << 20)
     big_q = torch.zeros(rows, 24, 256, dtype=torch.bfloat16, device="cuda")
     big_idx = torch.zeros(rows, topk, dtype=torch.int32, device="cuda")
