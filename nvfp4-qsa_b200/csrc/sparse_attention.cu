@@ -52,6 +52,8 @@
 //    pre-scale (amax * 2^e in [2^14, 2^15)), folded back into the score scale.
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace nvqsa {
@@ -321,6 +323,10 @@ __device__ __forceinline__ void merge_item(const MergeArgs& a, int64_t row, int 
   }
 }
 
+// GMODE: how records reach shared memory (0: tile::gather4 rows; 1: one bulk copy per
+// record; 2: four bulk copies per record), fixed per launch so the hot loop carries no
+// mode branches.
+template <int GMODE>
 __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // Tensor copies need 128-byte aligned destinations: align the base explicitly.
@@ -475,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     const int count = min(kTile, n - j0);
     // The slot was last read by this warp's generic loads: order them before the async-proxy writes.
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    if (p.gather_mode == 0) {
+    if constexpr (GMODE == 0) {
       if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
       __syncwarp();
       if (lane < kTile / 4) {
@@ -499,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     if (lane < count) {
       const int2 e = sm.sel[j0 + lane];
       const uint32_t dst = smem_u32(&sm.rec[warp][slot][slot_off(lane)]);
-      if (p.gather_mode == 1) {
+      if constexpr (GMODE == 1) {
         bulk_g2s(dst, reg0 + (int64_t)e.x * sb0 + (int64_t)e.y * st0 + (int64_t)kvh * sh0, kRecordBytes, bar);
       } else {
         const uint32_t dofs[4] = {0, 128, 144, 272};
@@ -536,51 +542,54 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   float m_r = kMaskedScore, m_r8 = kMaskedScore;
   float l_r = 0.0f, l_r8 = 0.0f;
 
-  int k = 0;
-  for (; k < my_tiles; ++k) {
-    if (k + kAhead < my_tiles) issue_tile(k + kAhead);  // into the slot tile k-1 used
-    const int slot = k % kWarpStages;
-    if (!mbar_wait(smem_u32(&sm.full_bar[warp][slot]), (uint32_t)((k / kWarpStages) & 1))) {
-      if (lane == 0) sm.abort = 1;
-      break;
-    }
-    const int tok_base = (warp + kWarps * k) * kTile;  // compacted index of the tile's first token
-    const bool tail = tok_base + kTile > n;
-    const uint8_t* stage = sm.rec[warp][slot];
+  // One tile of 16 tokens at `stage`; TAIL masks tokens at or past n (only a warp's last tile can be short).
+  auto tile_body = [&](const uint8_t* stage, const int tok_base, auto tail_tag) {
+    constexpr bool TAIL = decltype(tail_tag)::value;
 
-    // ---- S = Q K^T: 2 n-tiles of 8 tokens x 16 k-steps over all 256 dims ----
+    // ---- S = Q K^T: 16 k-steps over all 256 dims, each on both n-tiles of 8 tokens ----
     float sacc[2][4];
+    uint32_t sg[2][4];  // f16x2 group scales {lo, hi} x {chunk c, chunk 4+c}, duplicated per half
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const uint8_t* rec = stage + k_off[nt];
-      const uint4 ka = *reinterpret_cast<const uint4*>(rec + 16 * c);
-      const uint4 kb = *reinterpret_cast<const uint4*>(rec + 64 + 16 * c);
-      const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
       const uint32_t sc0 = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 2 * c));
       const uint32_t sc1 = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 136 + 2 * c));
+      sg[nt][0] = dup_lo(sc0);
+      sg[nt][1] = dup_hi(sc0);
+      sg[nt][2] = dup_lo(sc1);
+      sg[nt][3] = dup_hi(sc1);
       sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+    }
 #pragma unroll
-      for (int s = 0; s < 16; ++s) {
+    for (int half = 0; half < 2; ++half) {  // k-steps 8*half .. 8*half+7: chunk c (half 0) or 4+c (half 1)
+      uint4 kq[2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) kq[nt] = *reinterpret_cast<const uint4*>(stage + k_off[nt] + 64 * half + 16 * c);
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        const int s = 8 * half + s2;
         const uint4 qa = sm.qfrag[s][lane];
-        const uint32_t word = kw[s >> 1];
-        const uint32_t scale2 = (s < 8) ? sc0 : sc1;
-        const uint32_t sg = ((s & 7) < 4) ? dup_lo(scale2) : dup_hi(scale2);
-        uint32_t b0, b1;
-        if (s & 1) {
-          b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(word), sg);
-          b1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(word), sg);
-        } else {
-          b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(word), sg);
-          b1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(word), sg);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint32_t word = (s2 >> 1) == 0 ? kq[nt].x : (s2 >> 1) == 1 ? kq[nt].y : (s2 >> 1) == 2 ? kq[nt].z : kq[nt].w;
+          const uint32_t scl = sg[nt][2 * half + (s2 >> 2)];
+          uint32_t b0, b1;
+          if (s2 & 1) {
+            b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(word), scl);
+            b1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(word), scl);
+          } else {
+            b0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(word), scl);
+            b1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(word), scl);
+          }
+          mma_f16(sacc[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
         }
-        mma_f16(sacc[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
       }
     }
 
     // ---- online softmax (base 2): p = 2^(s * smul - m) with one FFMA ----
     uint32_t pf[4];
     {
-      if (tail) {
+      if constexpr (TAIL) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const int t0 = tok_base + 8 * nt + 2 * c;
@@ -619,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
         pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
         pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
       }
-      if (tail) {  // masked scores must not count even while the running max is still -1e20
+      if constexpr (TAIL) {  // masked scores must not count even while the running max is still -1e20
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           const int t0 = tok_base + 8 * nt + 2 * c;
@@ -646,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
         vw[q] = *reinterpret_cast<const uint2*>(rec + 144 + 64 * h + 8 * r);
         vsb[q] = rec[272 + 8 * h + r];
       }
-      if (tail && p.gather_mode != 0) {  // stale slots past the last valid token: zero V so that 0 * V stays 0
+      if constexpr (TAIL && GMODE != 0) {  // stale slots past the last valid token: zero V so that 0 * V stays 0
         const int tt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -682,6 +691,22 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
 #undef NVQSA_PV_BYTE
       }
     }
+  };
+
+  int k = 0;
+  for (; k < my_tiles; ++k) {
+    if (k + kAhead < my_tiles) issue_tile(k + kAhead);  // into the slot tile k-1 used
+    const int slot = k % kWarpStages;
+    if (!mbar_wait(smem_u32(&sm.full_bar[warp][slot]), (uint32_t)((k / kWarpStages) & 1))) {
+      if (lane == 0) sm.abort = 1;
+      break;
+    }
+    const int tok_base = (warp + kWarps * k) * kTile;  // compacted index of the tile's first token
+    const uint8_t* stage = sm.rec[warp][slot];
+    if (tok_base + kTile <= n)
+      tile_body(stage, tok_base, std::false_type{});
+    else
+      tile_body(stage, tok_base, std::true_type{});
     __syncwarp();  // every lane's reads of this slot precede its refill
   }
 
@@ -979,11 +1004,13 @@ int configure_smem(size_t smem) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    if (cudaFuncSetAttribute(sparse_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(sparse_attention_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100) !=
-            cudaSuccess)
-      return NVQSA_ERR_CUDA;
+    const void* fns[3] = {reinterpret_cast<const void*>(sparse_attention_kernel<0>),
+                          reinterpret_cast<const void*>(sparse_attention_kernel<1>),
+                          reinterpret_cast<const void*>(sparse_attention_kernel<2>)};
+    for (const void* fn : fns)
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+          cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+        return NVQSA_ERR_CUDA;
     smem_configured[dev] = true;
   }
   return NVQSA_OK;
@@ -1122,9 +1149,20 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, sparse_attention_kernel, p) != cudaSuccess) return NVQSA_ERR_LAUNCH;
+    cudaError_t e;
+    if (p.gather_mode == 0)
+      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<0>, p);
+    else if (p.gather_mode == 1)
+      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<1>, p);
+    else
+      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<2>, p);
+    if (e != cudaSuccess) return NVQSA_ERR_LAUNCH;
+  } else if (p.gather_mode == 0) {
+    sparse_attention_kernel<0><<<(unsigned)grid, kThreads, smem, s>>>(p);
+  } else if (p.gather_mode == 1) {
+    sparse_attention_kernel<1><<<(unsigned)grid, kThreads, smem, s>>>(p);
   } else {
-    sparse_attention_kernel<<<(unsigned)grid, kThreads, smem, s>>>(p);
+    sparse_attention_kernel<2><<<(unsigned)grid, kThreads, smem, s>>>(p);
   }
   if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
   return NVQSA_OK;

@@ -1,0 +1,143 @@
+"""CPU: the vLLM backend hooks (nvfp4_qsa.vllm_hooks) with fake layer, metadata and kernels.
+
+Checks the reference hook behaviour (integration/snapshot/qsa.py:263-321 and
+:618-640) without a GPU: the rejections, output zeroing, the early return on
+an empty batch, the missing top-k buffer and bad cache errors, the four region
+views cut from the uint8 cache, and the exact arguments handed to the raw
+kernels (recorded by monkeypatched stand-ins; nothing is computed).
+"""
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from nvfp4_qsa import kernels, vllm_hooks
+from nvfp4_qsa.vllm_hooks import QSANVFP4AttentionHooks, split_nvfp4_kv_cache, write_nvfp4_kv
+
+
+class Impl(QSANVFP4AttentionHooks):
+    def __init__(self, **kw):
+        self.head_size = 256
+        self.alibi_slopes = None
+        self.sinks = None
+        self.sliding_window = (-1, -1)
+        self.__dict__.update(kw)
+
+
+def _inputs(num_tokens=3, max_tokens=5, blocks=4, page=16):
+    layer = SimpleNamespace(topk_indices_buffer=torch.arange(max_tokens * 8, dtype=torch.int32).view(max_tokens, 8),
+                            _qsa_nvfp4_k_global=2, _qsa_nvfp4_v_global=0.5)
+    query = torch.randn(max_tokens, 24, 256).bfloat16()
+    kv_cache = torch.zeros(blocks, 2, page, 288, dtype=torch.uint8)
+    meta = SimpleNamespace(num_actual_tokens=num_tokens, block_table=torch.zeros(2, 3, dtype=torch.int32))
+    output = torch.full((max_tokens, 24, 256), 7.0).bfloat16()
+    t2r = torch.zeros(max_tokens, dtype=torch.int32)
+    return layer, query, kv_cache, meta, output, t2r
+
+
+@pytest.fixture
+def recorded(monkeypatch):
+    calls = []
+    monkeypatch.setattr(kernels, "qsa_sparse_paged_attention_nvfp4", lambda *a: calls.append(("read", a)))
+    monkeypatch.setattr(kernels, "qsa_write_cache_nvfp4", lambda *a: calls.append(("write", a)))
+    return calls
+
+
+def test_split_matches_the_record_layout():
+    cache = torch.arange(3 * 2 * 4 * 288, dtype=torch.int64).remainder(251).to(torch.uint8).view(3, 2, 4, 288)
+    kd, ks, vd, vs = split_nvfp4_kv_cache(cache, 256)
+    assert kd.shape == (3, 4, 2, 128) and ks.shape == (3, 4, 2, 16)
+    assert vd.shape == (3, 4, 2, 128) and vs.shape == (3, 4, 2, 16)
+    for view, off in ((kd, 0), (ks, 128), (vd, 144), (vs, 272)):
+        assert view.stride() == (2 * 4 * 288, 288, 4 * 288, 1)
+        assert view.data_ptr() - cache.data_ptr() == off
+    assert torch.equal(vd[1, 2, 1], cache[1, 1, 2, 144:272])
+
+
+@pytest.mark.parametrize("bad", [torch.zeros(2, 2, 4, 288, dtype=torch.int8), torch.zeros(2, 2, 4, 256, dtype=torch.uint8)])
+def test_split_rejects_a_cache_that_is_not_nvfp4(bad):
+    with pytest.raises(RuntimeError, match="last dim 288"):
+        split_nvfp4_kv_cache(bad, 256)
+
+
+@pytest.mark.parametrize("kw,match", [
+    (dict(output_scale=torch.ones(1)), "fused output quantization"),
+    (dict(output_block_scale=torch.ones(1)), "fused output quantization"),
+])
+def test_forward_rejects_fused_output_quantisation(recorded, kw, match):
+    layer, query, cache, meta, out, t2r = _inputs()
+    with pytest.raises(NotImplementedError, match=match):
+        Impl().forward_qsa(layer, query, None, None, cache, meta, out, t2r, **kw)
+    assert not recorded
+
+
+@pytest.mark.parametrize("attrs,match", [
+    (dict(alibi_slopes=torch.ones(24)), "ALiBi"),
+    (dict(sinks=torch.ones(24)), "attention sinks"),
+    (dict(sliding_window=(128, 0)), "sliding-window"),
+])
+def test_forward_rejects_unsupported_attention_features(recorded, attrs, match):
+    layer, query, cache, meta, out, t2r = _inputs()
+    with pytest.raises(NotImplementedError, match=match):
+        Impl(**attrs).forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert not recorded
+
+
+def test_forward_zeroes_and_returns_on_an_empty_batch(recorded):
+    layer, query, cache, meta, out, t2r = _inputs(num_tokens=0)
+    res = Impl().forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert res is out and not out.float().any() and not recorded
+
+
+def test_forward_needs_the_topk_buffer(recorded):
+    layer, query, cache, meta, out, t2r = _inputs()
+    del layer.topk_indices_buffer
+    with pytest.raises(RuntimeError, match="top-k buffer"):
+        Impl().forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert not out.float().any()  # zeroed before the check, as in the reference
+
+
+def test_forward_rejects_a_bad_cache(recorded):
+    layer, query, _, meta, out, t2r = _inputs()
+    with pytest.raises(RuntimeError, match="uint8"):
+        Impl().forward_qsa(layer, query, None, None, torch.zeros(4, 2, 16, 288, dtype=torch.float16), meta, out, t2r)
+
+
+def test_forward_hands_the_reader_the_reference_arguments(recorded):
+    layer, query, cache, meta, out, t2r = _inputs(num_tokens=3)
+    res = Impl().forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert res is out
+    (kind, a), = recorded
+    assert kind == "read" and len(a) == 11
+    q, kd, ks, vd, vs, gk, gv, idx, bt, tr, o = a
+    assert q.shape[0] == 3 and q.data_ptr() == query.data_ptr()
+    assert (kd.shape, ks.shape, vd.shape, vs.shape) == ((4, 16, 2, 128), (4, 16, 2, 16), (4, 16, 2, 128), (4, 16, 2, 16))
+    assert vd.data_ptr() - cache.data_ptr() == 144
+    assert (gk, gv) == (2.0, 0.5) and type(gk) is float and type(gv) is float
+    assert torch.equal(idx, layer.topk_indices_buffer[:3]) and bt is meta.block_table and tr.shape[0] == 3
+    assert o.shape[0] == 3 and o.data_ptr() == out.data_ptr()
+    assert not out.float().any()  # zeroed; the reader writes rows [0, 3)
+
+
+def test_forward_defaults_the_global_scales_to_one(recorded):
+    layer, query, cache, meta, out, t2r = _inputs()
+    del layer._qsa_nvfp4_k_global, layer._qsa_nvfp4_v_global
+    Impl().forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert recorded[0][1][5:7] == (1.0, 1.0)
+
+
+def test_write_hook_hands_the_writer_the_reference_arguments(recorded):
+    cache = torch.zeros(4, 2, 16, 288, dtype=torch.uint8)
+    key = torch.randn(5, 2, 256).bfloat16()
+    value = torch.randn(5, 2, 256).bfloat16()
+    slots = torch.arange(5)
+    write_nvfp4_kv(cache, 256, key, value, slots, 1, 3)
+    (kind, a), = recorded
+    assert kind == "write" and len(a) == 9
+    assert a[0] is key and a[1] is value and a[6] is slots and a[7:] == (1.0, 3.0)
+    assert a[4].data_ptr() - cache.data_ptr() == 144 and a[3].shape == (4, 16, 2, 16)
+
+
+def test_hooks_module_calls_through_kernels_namespace():
+    # the hooks look the raw ops up on nvfp4_qsa.kernels at call time (monkeypatch-able, one code path)
+    assert vllm_hooks.kernels is kernels
