@@ -214,8 +214,9 @@ def test_read_inside_cuda_graph():
 
 
 def test_size_independent_properties():
-    # Full-size style checks without an oracle: selection order, duplicating every
-    # selection, and row replication leave the softmax output unchanged.
+    # Checks without an oracle at config 2's full size: selection order, duplicating every
+    # selection, masked selections (negative / past the table) and row replication leave
+    # the softmax output unchanged.
     case = W.decode_config(seed=13, context=32768, topk=2048, rows=2)
     storage, q, idx, bt, t2r = build_case_on_gpu(case)
     base = gpu_attend(storage, q, idx, bt, t2r).float()
@@ -223,6 +224,8 @@ def test_size_independent_properties():
     assert (gpu_attend(storage, q, perm, bt, t2r).float() - base).abs().max().item() < 2e-3
     doubled = torch.cat([idx, idx], dim=1).contiguous()
     assert (gpu_attend(storage, q, doubled, bt, t2r).float() - base).abs().max().item() < 2e-3
+    masked = torch.cat([torch.full_like(idx, -1), idx, torch.full_like(idx, 1 << 30)], dim=1).contiguous()
+    assert (gpu_attend(storage, q, masked, bt, t2r).float() - base).abs().max().item() < 2e-3  # masked = absent
     q_rep = q[:1].repeat(6, 1, 1).contiguous()
     rep = gpu_attend(storage, q_rep, idx[:1].repeat(6, 1).contiguous(), bt, t2r[:1].repeat(6).contiguous())
     assert torch.equal(rep, rep[:1].expand_as(rep))  # identical rows -> identical bits
