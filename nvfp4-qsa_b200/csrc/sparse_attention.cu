@@ -52,6 +52,7 @@
 //    pre-scale (amax * 2^e in [2^14, 2^15)), folded back into the score scale.
 #include <cuda.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -774,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     }
     cluster_sync();
     bool ok = !aborted;
-    if (split == 0 && warp == 0 && ok) {
+    if (split % p.cluster == 0 && warp == 0 && ok) {
       for (int rk = 1; rk < p.cluster; ++rk) {
         if (cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk))) {
           ok = false;
@@ -800,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       }
     }
     cluster_sync();  // ranks > 0 keep their shared memory until rank 0 has read it
-    if (split != 0 || !ok) return;
+    if (split % p.cluster != 0 || !ok) return;  // rank 0 carries on with the cluster's merged (O, m, l)
   }
 
   if (warp == 0) {
@@ -844,7 +845,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
             }
           }
         } else {
-          const int64_t slot = ((int64_t)split * p.rows + row) * p.query_heads + head;
+          const int64_t slot = ((int64_t)(split / p.cluster) * p.rows + row) * p.query_heads + head;
           float* op = p.part_out + slot * kHeadDim + d0;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
@@ -855,33 +856,98 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     }
   }
 
-  // ---------------- split-KV: the last CTA of this (row, kv head) merges the splits ----------------
+  // ---------------- split-KV beyond one cluster: the last part to arrive merges all parts ----------------
+  // Parts: one per CTA (cluster 1) or one per cluster (its rank 0), each a normalised partial in the workspace.
   if (!p.fuse) return;
+  const int nparts = p.splits / p.cluster;
   if (warp == 0) {
-    __threadfence();  // this CTA's partial is visible device-wide before its arrival is counted
+    __threadfence();  // this part is visible device-wide before its arrival is counted
     __syncwarp();
     if (lane == 0)
-      sm.last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(p.splits - 1);
+      sm.last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
   }
   __syncthreads();
   if (!sm.last) return;
-  __threadfence();  // the other CTAs' partials, counted before ours, are visible
-  MergeArgs a;
-  a.part_out = p.part_out;
-  a.part_lse = p.part_lse;
-  a.splits = p.splits;
-  a.out_split_stride = p.rows * p.query_heads * kHeadDim;
-  a.lse_split_stride = p.rows * p.query_heads;
-  a.mode = p.final_mode;
-  a.out = p.out;
-  a.o_stride_row = p.o_stride_row;
-  a.o_stride_head = p.o_stride_head;
-  a.vec_o = p.vec_o;
-  a.out_f32 = p.final_out;
-  a.out_lse = p.final_lse;
-  for (int j = warp; j < G; j += kWarps) {
-    const int head = kvh * G + j;
-    merge_item(a, row, head, row * p.query_heads + head, lane);
+  __threadfence();  // the other parts, counted before ours, are visible
+  {
+    // 1. every part's lse of this unit's heads into shared memory (ring space, free now)
+    float* wt = reinterpret_cast<float*>(&sm.rec[0][0][0]);   // [nparts][16]: lse, then weights
+    float* head_m = wt + nparts * 16;                         // [16]
+    float* head_den = head_m + 16;                            // [16]
+    const int64_t items = p.rows * p.query_heads;
+    const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
+    for (int i = tid; i < nparts * G; i += kThreads) {
+      const int part = i / G, j = i - part * G;
+      wt[part * 16 + j] = __ldcg(p.part_lse + (int64_t)part * items + w0 + j);
+    }
+    __syncthreads();
+    // 2. per head: max, weights 2^(lse - max) (0 for empty parts), their sum
+    if (tid < G) {
+      float M = -INFINITY;
+      for (int part = 0; part < nparts; ++part) M = fmaxf(M, wt[part * 16 + tid]);
+      float den = 0.0f;
+      for (int part = 0; part < nparts; ++part) {
+        const float l = wt[part * 16 + tid];
+        const float x = (l == -INFINITY) ? 0.0f : exp2f(l - M);
+        wt[part * 16 + tid] = x;
+        den += x;
+      }
+      head_m[tid] = M;
+      head_den[tid] = den;
+    }
+    __syncthreads();
+    // 3. outputs: item = (head j, 8 dims); loads of four parts in flight at a time (empty parts hold zeros)
+    for (int it = tid; it < G * 32; it += kThreads) {
+      const int j = it >> 5, d8 = it & 31;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
+      for (int q0 = 0; q0 < nparts; q0 += 4) {
+        float4 x[4], y[4];
+        float c[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const bool in = q0 + u < nparts;
+          const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + u : 0) * items * kHeadDim);
+          x[u] = __ldcg(po);
+          y[u] = __ldcg(po + 1);
+          c[u] = in ? wt[(q0 + u) * 16 + j] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[0] += c[u] * x[u].x; acc[1] += c[u] * x[u].y; acc[2] += c[u] * x[u].z; acc[3] += c[u] * x[u].w;
+          acc[4] += c[u] * y[u].x; acc[5] += c[u] * y[u].y; acc[6] += c[u] * y[u].z; acc[7] += c[u] * y[u].w;
+        }
+      }
+      const float den = head_den[j];
+      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= inv;
+      const int head = kvh * G + j;
+      if (p.final_mode == 0) {
+        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
+        uint32_t u4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+          u4[i] = *reinterpret_cast<uint32_t*>(&b);
+        }
+        if (p.vec_o) {
+          *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+        } else {
+          unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
+            os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
+          }
+        }
+      } else {
+        float4* op = reinterpret_cast<float4*>(p.final_out + (w0 + j) * kHeadDim + d8 * 8);
+        op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (d8 == 0) p.final_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+      }
+    }
   }
 }
 
@@ -972,8 +1038,11 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   if (units > 0 && units < sm_count) splits = (sm_count + units - 1) / units;
   if (splits > chunks) splits = chunks;
   if (splits < min_splits) splits = min_splits;
+  // Beyond one cluster: a multiple of 8 splits in clusters of 8, whose rank-0 parts merge globally
+  // (CTAs past the last chunk contribute empty parts).
+  if (splits > kMaxClusterSplits) splits = (splits + kMaxClusterSplits - 1) / kMaxClusterSplits * kMaxClusterSplits;
   pl.splits = (int)splits;
-  pl.cluster = (splits > 1 && splits <= kMaxClusterSplits) ? (int)splits : 1;
+  pl.cluster = splits > 1 ? (int)std::min<int64_t>(splits, kMaxClusterSplits) : 1;
   return pl;
 }
 
@@ -985,8 +1054,8 @@ struct Workspace {
 };
 Workspace workspace_layout(const Plan& pl, int64_t rows, int query_heads, int kv_heads) {
   Workspace w{0, 0, 0};
-  if (pl.splits <= 1 || pl.cluster > 1) return w;
-  const size_t items = (size_t)pl.splits * rows * query_heads;
+  if (pl.splits <= pl.cluster) return w;  // unsplit, or merged inside one cluster
+  const size_t items = (size_t)(pl.splits / pl.cluster) * rows * query_heads;
   w.lse_offset = items * kHeadDim * sizeof(float);
   w.counter_offset = w.lse_offset + ((items * sizeof(float) + 255) / 256) * 256;
   w.bytes = w.counter_offset + (size_t)rows * kv_heads * sizeof(unsigned int);
@@ -1056,6 +1125,8 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   const size_t need = wl.bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned_to(workspace, 16))) return NVQSA_ERR_WORKSPACE;
   if ((int64_t)pl.splits * rows * kv_heads > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;
+  // The last part's merge keeps one weight per (part, head) in the CTA's ring space.
+  if ((size_t)(pl.splits / pl.cluster) * 16 * sizeof(float) + 128 > sizeof(Smem::rec)) return NVQSA_ERR_UNSUPPORTED;
 
   AttnParams p;
   p.q = static_cast<const __nv_bfloat16*>(query);
@@ -1109,11 +1180,11 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.counters = nullptr;
   p.final_out = partial_out;
   p.final_lse = partial_lse;
-  if (pl.cluster > 1) {  // rank 0 of each cluster stores the merged result like an unsplit CTA
+  if (pl.splits > 1 && pl.splits == pl.cluster) {  // one cluster per unit: its rank 0 stores like an unsplit CTA
     p.mode = partial_mode ? 1 : 0;
     p.part_out = partial_out;
     p.part_lse = partial_lse;
-  } else if (pl.splits > 1) {
+  } else if (pl.splits > 1) {  // several parts per unit (one per cluster) merged by the last to arrive
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     p.mode = 1;
     p.fuse = 1;
