@@ -324,6 +324,100 @@ __device__ __forceinline__ void merge_item(const MergeArgs& a, int64_t row, int 
   }
 }
 
+// Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
+// normalised partial and lse to the workspace; the last part to arrive at the unit's
+// counter merges all parts into the output.  Called by every thread of the CTA.
+__device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratch, int& last, int64_t row, int kvh,
+                                              int G, int tid) {
+  const int nparts = p.splits / p.cluster;
+  __threadfence();  // this part is visible device-wide before its arrival is counted
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();  // the other parts, counted before ours, are visible
+  {
+    // 1. every part's lse of this unit's heads into shared memory (ring space, free now)
+    float* wt = scratch;                                      // [nparts][16]: lse, then weights
+    float* head_m = wt + nparts * 16;                         // [16]
+    float* head_den = head_m + 16;                            // [16]
+    const int64_t items = p.rows * p.query_heads;
+    const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
+    for (int i = tid; i < nparts * G; i += kThreads) {
+      const int part = i / G, j = i - part * G;
+      wt[part * 16 + j] = __ldcg(p.part_lse + (int64_t)part * items + w0 + j);
+    }
+    __syncthreads();
+    // 2. per head: max, weights 2^(lse - max) (0 for empty parts), their sum
+    if (tid < G) {
+      float M = -INFINITY;
+      for (int part = 0; part < nparts; ++part) M = fmaxf(M, wt[part * 16 + tid]);
+      float den = 0.0f;
+      for (int part = 0; part < nparts; ++part) {
+        const float l = wt[part * 16 + tid];
+        const float x = (l == -INFINITY) ? 0.0f : exp2f(l - M);
+        wt[part * 16 + tid] = x;
+        den += x;
+      }
+      head_m[tid] = M;
+      head_den[tid] = den;
+    }
+    __syncthreads();
+    // 3. outputs: item = (head j, 8 dims); loads of four parts in flight at a time (empty parts hold zeros)
+    for (int it = tid; it < G * 32; it += kThreads) {
+      const int j = it >> 5, d8 = it & 31;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
+      for (int q0 = 0; q0 < nparts; q0 += 4) {
+        float4 x[4], y[4];
+        float c[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const bool in = q0 + u < nparts;
+          const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + u : 0) * items * kHeadDim);
+          x[u] = __ldcg(po);
+          y[u] = __ldcg(po + 1);
+          c[u] = in ? wt[(q0 + u) * 16 + j] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          acc[0] += c[u] * x[u].x; acc[1] += c[u] * x[u].y; acc[2] += c[u] * x[u].z; acc[3] += c[u] * x[u].w;
+          acc[4] += c[u] * y[u].x; acc[5] += c[u] * y[u].y; acc[6] += c[u] * y[u].z; acc[7] += c[u] * y[u].w;
+        }
+      }
+      const float den = head_den[j];
+      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] *= inv;
+      const int head = kvh * G + j;
+      if (p.final_mode == 0) {
+        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
+        uint32_t u4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+          u4[i] = *reinterpret_cast<uint32_t*>(&b);
+        }
+        if (p.vec_o) {
+          *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+        } else {
+          unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
+            os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
+          }
+        }
+      } else {
+        float4* op = reinterpret_cast<float4*>(p.final_out + (w0 + j) * kHeadDim + d8 * 8);
+        op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (d8 == 0) p.final_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+      }
+    }
+  }
+}
+
 // GMODE: how records reach shared memory (0: tile::gather4 rows; 1: one bulk copy per
 // record; 2: four bulk copies per record), fixed per launch so the hot loop carries no
 // mode branches.
@@ -857,98 +951,8 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   }
 
   // ---------------- split-KV beyond one cluster: the last part to arrive merges all parts ----------------
-  // Parts: one per CTA (cluster 1) or one per cluster (its rank 0), each a normalised partial in the workspace.
   if (!p.fuse) return;
-  const int nparts = p.splits / p.cluster;
-  if (warp == 0) {
-    __threadfence();  // this part is visible device-wide before its arrival is counted
-    __syncwarp();
-    if (lane == 0)
-      sm.last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
-  }
-  __syncthreads();
-  if (!sm.last) return;
-  __threadfence();  // the other parts, counted before ours, are visible
-  {
-    // 1. every part's lse of this unit's heads into shared memory (ring space, free now)
-    float* wt = reinterpret_cast<float*>(&sm.rec[0][0][0]);   // [nparts][16]: lse, then weights
-    float* head_m = wt + nparts * 16;                         // [16]
-    float* head_den = head_m + 16;                            // [16]
-    const int64_t items = p.rows * p.query_heads;
-    const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
-    for (int i = tid; i < nparts * G; i += kThreads) {
-      const int part = i / G, j = i - part * G;
-      wt[part * 16 + j] = __ldcg(p.part_lse + (int64_t)part * items + w0 + j);
-    }
-    __syncthreads();
-    // 2. per head: max, weights 2^(lse - max) (0 for empty parts), their sum
-    if (tid < G) {
-      float M = -INFINITY;
-      for (int part = 0; part < nparts; ++part) M = fmaxf(M, wt[part * 16 + tid]);
-      float den = 0.0f;
-      for (int part = 0; part < nparts; ++part) {
-        const float l = wt[part * 16 + tid];
-        const float x = (l == -INFINITY) ? 0.0f : exp2f(l - M);
-        wt[part * 16 + tid] = x;
-        den += x;
-      }
-      head_m[tid] = M;
-      head_den[tid] = den;
-    }
-    __syncthreads();
-    // 3. outputs: item = (head j, 8 dims); loads of four parts in flight at a time (empty parts hold zeros)
-    for (int it = tid; it < G * 32; it += kThreads) {
-      const int j = it >> 5, d8 = it & 31;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
-      for (int q0 = 0; q0 < nparts; q0 += 4) {
-        float4 x[4], y[4];
-        float c[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const bool in = q0 + u < nparts;
-          const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + u : 0) * items * kHeadDim);
-          x[u] = __ldcg(po);
-          y[u] = __ldcg(po + 1);
-          c[u] = in ? wt[(q0 + u) * 16 + j] : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          acc[0] += c[u] * x[u].x; acc[1] += c[u] * x[u].y; acc[2] += c[u] * x[u].z; acc[3] += c[u] * x[u].w;
-          acc[4] += c[u] * y[u].x; acc[5] += c[u] * y[u].y; acc[6] += c[u] * y[u].z; acc[7] += c[u] * y[u].w;
-        }
-      }
-      const float den = head_den[j];
-      const float inv = den > 0.0f ? 1.0f / den : 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] *= inv;
-      const int head = kvh * G + j;
-      if (p.final_mode == 0) {
-        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
-        uint32_t u4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-          u4[i] = *reinterpret_cast<uint32_t*>(&b);
-        }
-        if (p.vec_o) {
-          *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
-        } else {
-          unsigned short* os = reinterpret_cast<unsigned short*>(op);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
-            os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
-          }
-        }
-      } else {
-        float4* op = reinterpret_cast<float4*>(p.final_out + (w0 + j) * kHeadDim + d8 * 8);
-        op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-        if (d8 == 0) p.final_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
-      }
-    }
-  }
+  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
 }
 
 // One warp per (row, query head): log-sum-exp merge of `splits` partials, split s
@@ -962,6 +966,8 @@ __global__ void __launch_bounds__(256) merge_kernel(MergeArgs a, int64_t rows, i
   const int64_t row = w / query_heads;
   merge_item(a, row, (int)(w - row * query_heads), w, lane);
 }
+
+#include "sparse_attention_tc.cuh"
 
 // ---------------- host-side planning ----------------
 // 2D tensor map viewing the cache records as rows [rows, 144] of u16 (288 bytes),
@@ -1069,17 +1075,40 @@ size_t workspace_for(const Plan& pl, int64_t rows, int query_heads, int kv_heads
 constexpr int kMaxDevices = 64;
 bool smem_configured[kMaxDevices] = {};
 
-int configure_smem(size_t smem) {
+// The reader kernel of a launch: P.V on tcgen05 (sparse_attention_tc_kernel) or on
+// mma.sync (sparse_attention_kernel), per gather mode, with its shared-memory size.
+constexpr bool kTensorMemoryReader = false;
+
+struct ReaderKernel {
+  const void* fn;
+  size_t smem;  // + slack for the 128-byte alignment of the base
+};
+ReaderKernel reader_kernel(int gather_mode) {
+  if (kTensorMemoryReader) {
+    switch (gather_mode) {
+      case 0: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<0>), sizeof(SmemTc<0>) + 128};
+      case 1: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<1>), sizeof(SmemTc<1>) + 128};
+      default: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<2>), sizeof(SmemTc<2>) + 128};
+    }
+  }
+  switch (gather_mode) {
+    case 0: return {reinterpret_cast<const void*>(sparse_attention_kernel<0>), sizeof(Smem) + 128};
+    case 1: return {reinterpret_cast<const void*>(sparse_attention_kernel<1>), sizeof(Smem) + 128};
+    default: return {reinterpret_cast<const void*>(sparse_attention_kernel<2>), sizeof(Smem) + 128};
+  }
+}
+
+// Dynamic shared memory above 48 KB is opted into once per device and kernel.
+int configure_smem() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    const void* fns[3] = {reinterpret_cast<const void*>(sparse_attention_kernel<0>),
-                          reinterpret_cast<const void*>(sparse_attention_kernel<1>),
-                          reinterpret_cast<const void*>(sparse_attention_kernel<2>)};
-    for (const void* fn : fns)
-      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-          cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    for (int mode = 0; mode < 3; ++mode) {
+      const ReaderKernel rk = reader_kernel(mode);
+      if (cudaFuncSetAttribute(rk.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rk.smem) != cudaSuccess ||
+          cudaFuncSetAttribute(rk.fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return NVQSA_ERR_CUDA;
+    }
     smem_configured[dev] = true;
   }
   return NVQSA_OK;
@@ -1201,40 +1230,26 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     p.part_lse = nullptr;
   }
 
-  const size_t smem = sizeof(Smem) + 128;  // + slack for the 128-byte alignment of the base
-  if (const int st = configure_smem(smem)) return st;
+  if (const int st = configure_smem()) return st;
+  const ReaderKernel rk = reader_kernel(p.gather_mode);
   cudaStream_t s = as_stream(stream);
   if (p.fuse && cudaMemsetAsync(p.counters, 0, (size_t)rows * kv_heads * sizeof(unsigned int), s) != cudaSuccess)
     return NVQSA_ERR_LAUNCH;
   const int64_t grid = (int64_t)pl.splits * rows * kv_heads;
-  if (pl.cluster > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)pl.cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e;
-    if (p.gather_mode == 0)
-      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<0>, p);
-    else if (p.gather_mode == 1)
-      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<1>, p);
-    else
-      e = cudaLaunchKernelEx(&cfg, sparse_attention_kernel<2>, p);
-    if (e != cudaSuccess) return NVQSA_ERR_LAUNCH;
-  } else if (p.gather_mode == 0) {
-    sparse_attention_kernel<0><<<(unsigned)grid, kThreads, smem, s>>>(p);
-  } else if (p.gather_mode == 1) {
-    sparse_attention_kernel<1><<<(unsigned)grid, kThreads, smem, s>>>(p);
-  } else {
-    sparse_attention_kernel<2><<<(unsigned)grid, kThreads, smem, s>>>(p);
-  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = rk.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)pl.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.cluster > 1 ? 1 : 0;
+  void* args[1] = {&p};
+  if (cudaLaunchKernelExC(&cfg, rk.fn, args) != cudaSuccess) return NVQSA_ERR_LAUNCH;
   if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
   return NVQSA_OK;
 }
