@@ -294,15 +294,21 @@ def bench_split_kv(args, device, world, rank, steps):
         L.append(dict(regions=(kd, ks, vd, vs), idx=idx, q=q, table=table, out=torch.empty_like(q),
                       buf=sk.partial_buffer(1, QUERY_HEADS, HEAD_DIM, device)))
     t2r = torch.zeros(1, device=device, dtype=torch.int32)
+    exchange = D.PeerExchange(1, QUERY_HEADS, KV_HEADS) if world > 1 else None
 
-    def step():
+    def step():  # fused: the exchange over NVLink peer memory inside the reader kernel
         for d in L:
             if world > 1:
-                sk.attend(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], block_table=d["table"],
-                          buffer=d["buf"])
+                sk.attend_fused(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], exchange,
+                                block_table=d["table"])
             else:
                 kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
                                                          d["out"])
+
+    def step_nccl():  # partial kernel, NCCL all_gather of the packed partials, merge kernel
+        for d in L:
+            sk.attend(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], block_table=d["table"],
+                      buffer=d["buf"])
 
     for _ in range(3):
         step()
@@ -325,21 +331,32 @@ def bench_split_kv(args, device, world, rank, steps):
     n = max(10, steps // 4)
     secs = timed(graph.replay if graph is not None else step, n, device)
     del graph
+    nccl_secs = None
     if world > 1:
-        t = torch.tensor([secs], device=device, dtype=torch.float64)
+        for _ in range(3):
+            step_nccl()
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        nccl_secs = timed(step_nccl, n, device)
+        t = torch.tensor([secs, nccl_secs], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs = float(t.item())
+        secs, nccl_secs = float(t[0].item()), float(t[1].item())
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        exchange.close()
     per_layer_bytes = KV_HEADS * topk * RECORD + topk * 4 + 2 * QUERY_HEADS * HEAD_DIM * 2
     return {
         "config": {"workload": f"split-KV decode (config 5b): one sequence of {ctx} tokens, {topk} selected per row, "
                                f"{layers} layers, page {page}, pages split contiguously over {world} GPU(s); "
-                               "per layer: partial + one NCCL all_gather of packed (O, lse) + merge (eager launches); "
+                               "per layer one reader launch whose last CTA per (row, kv head) pushes its partial "
+                               "into every rank's exchange buffer over NVLink and merges (eager launches); "
                                "one GPU: the plain reader, 12 layers replayed from a CUDA graph",
                    "scaling": "strong"},
         "ms_per_step": secs / n * 1e3,
         "us_per_layer": secs / n / layers * 1e6,
         "gb_per_s": per_layer_bytes * layers * n / secs / 1e9,
         "exchange_bytes_per_rank_per_layer": L[0]["buf"].numel() * 4 if world > 1 else 0,
+        "nccl_us_per_layer": nccl_secs / n / layers * 1e6 if nccl_secs is not None else None,
     }
 
 

@@ -50,7 +50,7 @@ int nvqsa_abi_version(void);
 /*
  * Device error flags raised by the kernels on the current device (bit 0: a
  * bounded wait on a shared-memory barrier ran out, the affected CTA skipped
- * its output).  Kernels never trap; this synchronous query (it copies one
+ * its output; bit 1: a split-KV peer's slot did not arrive within 2 s).  Kernels never trap; this synchronous query (it copies one
  * word from the device) is for tests and diagnostics.  clear != 0 resets the
  * flags after reading.  No counterpart in the reference.
  */
@@ -170,6 +170,54 @@ int nvqsa_sparse_attention_partial(
     float* partial_out, float* partial_lse,
     int64_t rows, int32_t query_heads, int32_t head_dim,
     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Split-KV decode of one sequence across GPUs, the exchange fused into the
+ * reader kernel: each rank runs this call on its own cache pages (its block
+ * table holds -1 on pages other ranks own, so its share of the selections is
+ * implicit).  The CTA that finishes this rank's merged (O, lse) of a (row,
+ * kv head) stores it into slot `rank` of every rank's exchange buffer over
+ * NVLink, raises that rank's flag (release), waits for the flags of all
+ * other ranks (acquire; bounded at 2 s, after which bit 1 of the device error
+ * flags is raised and the output is left unwritten) and merges the `world`
+ * slots into `output` (bf16).  Every rank gets the full result.  This
+ * replaces the reference's split-K merge (src/qsa_fp8_harness.py:308-321)
+ * done after an all_gather; there is no reference counterpart for the
+ * peer-memory exchange itself.
+ *
+ * exchange : [world] pointers, rank r's exchange buffer as mapped in this
+ *            process (own buffer included; peers via nvqsa_ipc_open_handle),
+ *            each nvqsa_split_kv_exchange_bytes(rows, ...) bytes, allocated
+ *            by nvqsa_exchange_alloc (zeroed).  The same `rows` on every call.
+ * parity   : 0 or 1, alternating from call to call on this exchange buffer
+ *            (every rank the same sequence), so a fast rank's next call never
+ *            meets flags of the previous one.
+ * All ranks must make the same calls in the same order; calls are not
+ * capture-safe across ranks (eager use).
+ */
+int nvqsa_split_kv_exchange_bytes(int64_t rows, int32_t query_heads, int32_t kv_heads, int32_t world,
+                                  size_t* bytes);
+int nvqsa_exchange_alloc(size_t bytes, void** ptr);
+int nvqsa_exchange_free(void* ptr);
+/* CUDA IPC handle (64 bytes) of an exchange buffer, and mapping a peer's handle into this process. */
+int nvqsa_ipc_get_handle(const void* ptr, void* handle);
+int nvqsa_ipc_open_handle(const void* handle, void** ptr);
+int nvqsa_ipc_close_handle(void* ptr);
+int nvqsa_sparse_attention_split_kv(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes,
+    void* const* exchange, int32_t world, int32_t rank, int32_t parity, void* stream);
 
 /*
  * Log-sum-exp merge of `splits` partials into the bf16 output: for each

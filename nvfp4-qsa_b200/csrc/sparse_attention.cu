@@ -53,6 +53,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
@@ -103,6 +104,10 @@ struct AttnParams {
   unsigned int* counters;        // [rows * kv_heads] arrival counters (zeroed before the launch)
   float* final_out;              // [rows][query_heads][256]
   float* final_lse;              // [rows][query_heads]
+  // Split-KV across GPUs (xworld > 0): this rank's merged (O, lse) goes into slot xrank of every rank's
+  // exchange buffer over NVLink, then the unit's final CTA waits for every rank's slot and merges them.
+  int32_t xworld, xrank, xparity;
+  float* xpeer[8];               // exchange buffer of every rank, as mapped in this process
   int32_t vec_q;                 // 16-byte aligned query rows
   int32_t vec_o;                 // 16-byte aligned output rows
   __nv_bfloat16* out;
@@ -125,6 +130,8 @@ struct __align__(128) Smem {
 
 __device__ unsigned int g_error_flags;       // bit 0: an mbarrier wait ran out
 constexpr unsigned int kErrWaitTimeout = 1u;
+constexpr unsigned int kErrPeerTimeout = 2u;            // bit 1: another GPU's split-KV slot never arrived
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
@@ -327,15 +334,13 @@ __device__ __forceinline__ void merge_item(const MergeArgs& a, int64_t row, int 
 // Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
 // normalised partial and lse to the workspace; the last part to arrive at the unit's
 // counter merges all parts into the output.  Called by every thread of the CTA.
-__device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratch, int& last, int64_t row, int kvh,
-                                              int G, int tid) {
-  const int nparts = p.splits / p.cluster;
-  __threadfence();  // this part is visible device-wide before its arrival is counted
-  __syncthreads();
-  if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
-  __syncthreads();
-  if (!last) return;
-  __threadfence();  // the other parts, counted before ours, are visible
+// Log-sum-exp merge of `nparts` normalised partials of one (row, kv head) unit, part q at
+// part_out + q * rows * heads * 256 and part_lse + q * rows * heads, into the bf16 output
+// (out_mode 0) or fp32 f32_out / f32_lse (out_mode 1).  Called by every thread of the CTA;
+// `scratch` holds nparts * 16 + 32 floats of shared memory.
+__device__ __noinline__ void merge_unit_parts(const AttnParams& p, float* scratch, int64_t row, int kvh, int G, int tid,
+                                              const float* part_out, const float* part_lse, int nparts, int out_mode,
+                                              float* f32_out, float* f32_lse) {
   {
     // 1. every part's lse of this unit's heads into shared memory (ring space, free now)
     float* wt = scratch;                                      // [nparts][16]: lse, then weights
@@ -345,7 +350,7 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
     const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
     for (int i = tid; i < nparts * G; i += kThreads) {
       const int part = i / G, j = i - part * G;
-      wt[part * 16 + j] = __ldcg(p.part_lse + (int64_t)part * items + w0 + j);
+      wt[part * 16 + j] = __ldcg(part_lse + (int64_t)part * items + w0 + j);
     }
     __syncthreads();
     // 2. per head: max, weights 2^(lse - max) (0 for empty parts), their sum
@@ -367,7 +372,7 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
     for (int it = tid; it < G * 32; it += kThreads) {
       const int j = it >> 5, d8 = it & 31;
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
+      const float* base = part_out + (w0 + j) * kHeadDim + d8 * 8;
       for (int q0 = 0; q0 < nparts; q0 += 4) {
         float4 x[4], y[4];
         float c[4];
@@ -390,7 +395,7 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] *= inv;
       const int head = kvh * G + j;
-      if (p.final_mode == 0) {
+      if (out_mode == 0) {
         __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
         uint32_t u4[4];
 #pragma unroll
@@ -409,13 +414,93 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
           }
         }
       } else {
-        float4* op = reinterpret_cast<float4*>(p.final_out + (w0 + j) * kHeadDim + d8 * 8);
+        float4* op = reinterpret_cast<float4*>(f32_out + (w0 + j) * kHeadDim + d8 * 8);
         op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-        if (d8 == 0) p.final_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+        if (d8 == 0) f32_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
       }
     }
   }
+}
+
+// Split-KV across GPUs: this rank's merged (O, lse) of the unit sits in slot xrank of its own
+// exchange buffer.  Push it into slot xrank of every other rank's buffer (NVLink stores), publish
+// a flag per destination (release), wait for every other rank's flag (acquire, bounded by time),
+// then merge the ranks' slots into the bf16 output and re-arm the flags of this parity.
+__device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch, int& status, int64_t row, int kvh,
+                                            int G, int tid) {
+  const int64_t items = p.rows * p.query_heads;
+  const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
+  const int64_t unit = row * p.kv_heads + kvh;
+  const int64_t units = p.rows * p.kv_heads;
+  const int world = p.xworld, me = p.xrank;
+  auto lse_of = [&](float* base) { return base + (int64_t)world * items * kHeadDim; };
+  auto flag_of = [&](float* base, int src) {
+    return reinterpret_cast<unsigned int*>(lse_of(base) + (int64_t)world * items) +
+           ((int64_t)p.xparity * units + unit) * world + src;
+  };
+  __syncthreads();  // this unit's slot-me stores by the CTA are complete
+  float* mine = p.xpeer[me];
+  const float4* src_o = reinterpret_cast<const float4*>(mine + ((int64_t)me * items + w0) * kHeadDim);
+  const float* src_l = lse_of(mine) + (int64_t)me * items + w0;
+  for (int r = 0; r < world; ++r) {
+    if (r == me) continue;
+    float4* dst_o = reinterpret_cast<float4*>(p.xpeer[r] + ((int64_t)me * items + w0) * kHeadDim);
+    for (int i = tid; i < G * (kHeadDim / 4); i += kThreads) dst_o[i] = __ldcg(src_o + i);
+    if (tid < G) lse_of(p.xpeer[r])[(int64_t)me * items + w0 + tid] = __ldcg(src_l + tid);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    for (int r = 0; r < world; ++r) {
+      if (r == me) continue;
+      asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(flag_of(p.xpeer[r], me)), "r"(1u) : "memory");
+    }
+    // Wait for every other rank's slot: bounded by time, so a rank that never arrives cannot hang the GPU.
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    int ok = 1;
+    for (int r = 0; r < world && ok; ++r) {
+      if (r == me) continue;
+      unsigned int* f = flag_of(mine, r);
+      while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(f) : "memory");
+        if (v) break;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > kPeerWaitNs) {
+          ok = 0;
+          atomicOr(&g_error_flags, kErrPeerTimeout);
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+    status = ok;
+  }
+  __syncthreads();
+  if (!status) return;
+  merge_unit_parts(p, scratch, row, kvh, G, tid, mine, lse_of(mine), world, 0, nullptr, nullptr);
+  __syncthreads();
+  if (tid < world) *flag_of(mine, tid) = 0u;  // re-arm this parity for the call after next
+}
+
+// Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
+// normalised partial and lse to the workspace; the last part to arrive at the unit's
+// counter merges all parts.  Called by every thread of the CTA.
+__device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratch, int& last, int64_t row, int kvh,
+                                              int G, int tid) {
+  const int nparts = p.splits / p.cluster;
+  __threadfence();  // this part is visible device-wide before its arrival is counted
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();  // the other parts, counted before ours, are visible
+  merge_unit_parts(p, scratch, row, kvh, G, tid, p.part_out, p.part_lse, nparts, p.final_mode, p.final_out,
+                   p.final_lse);
+  if (p.xworld > 0) xrank_exchange(p, scratch, last, row, kvh, G, tid);
 }
 
 // GMODE: how records reach shared memory (0: tile::gather4 rows; 1: one bulk copy per
@@ -951,7 +1036,10 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   }
 
   // ---------------- split-KV beyond one cluster: the last part to arrive merges all parts ----------------
-  if (!p.fuse) return;
+  if (!p.fuse) {
+    if (p.xworld > 0) xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+    return;
+  }
   fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
 }
 
@@ -1120,7 +1208,8 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
                   const int32_t* block_table, int64_t num_requests, int64_t table_width,
                   const int32_t* token_to_request, void* output, int64_t o_stride_row, int64_t o_stride_head,
                   float* partial_out, float* partial_lse, int64_t rows, int32_t query_heads, int32_t head_dim,
-                  void* workspace, size_t workspace_bytes, void* stream) {
+                  void* workspace, size_t workspace_bytes, void* stream, float* const* xpeers = nullptr,
+                  int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0) {
   if (rows < 0 || topk < 0 || kv_heads < 1 || query_heads < 1 || num_blocks < 0 || page_size < 1 ||
       num_requests < 0 || table_width < 0)
     return NVQSA_ERR_BAD_SHAPE;
@@ -1205,12 +1294,23 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.o_stride_head = o_stride_head;
   p.fuse = 0;
   p.cluster = pl.cluster;
-  p.final_mode = partial_mode ? 1 : 0;
+  p.xworld = xworld;
+  p.xrank = xrank;
+  p.xparity = xparity;
+  for (int r = 0; r < 8; ++r) p.xpeer[r] = (xpeers && r < xworld) ? xpeers[r] : nullptr;
+  if (xworld > 0) {
+    // This rank's merged (O, lse) goes to slot xrank of its own exchange buffer first.
+    const int64_t items = rows * query_heads;
+    partial_out = p.xpeer[xrank] + (int64_t)xrank * items * kHeadDim;
+    partial_lse = p.xpeer[xrank] + (int64_t)xworld * items * kHeadDim + (int64_t)xrank * items;
+  }
+  const bool to_f32 = partial_mode || xworld > 0;
+  p.final_mode = to_f32 ? 1 : 0;
   p.counters = nullptr;
   p.final_out = partial_out;
   p.final_lse = partial_lse;
   if (pl.splits > 1 && pl.splits == pl.cluster) {  // one cluster per unit: its rank 0 stores like an unsplit CTA
-    p.mode = partial_mode ? 1 : 0;
+    p.mode = to_f32 ? 1 : 0;
     p.part_out = partial_out;
     p.part_lse = partial_lse;
   } else if (pl.splits > 1) {  // several parts per unit (one per cluster) merged by the last to arrive
@@ -1220,7 +1320,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     p.part_out = reinterpret_cast<float*>(ws);
     p.part_lse = reinterpret_cast<float*>(ws + wl.lse_offset);
     p.counters = reinterpret_cast<unsigned int*>(ws + wl.counter_offset);
-  } else if (partial_mode) {
+  } else if (to_f32) {
     p.mode = 1;
     p.part_out = partial_out;
     p.part_lse = partial_lse;
@@ -1333,6 +1433,90 @@ extern "C" int nvqsa_sparse_attention_partial(
                        key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
                        table_width, token_to_request, nullptr, 0, 0, partial_out, partial_lse, rows, query_heads,
                        head_dim, workspace, workspace_bytes, stream);
+}
+
+extern "C" int nvqsa_split_kv_exchange_bytes(int64_t rows, int32_t query_heads, int32_t kv_heads, int32_t world,
+                                             size_t* bytes) {
+  if (!bytes) return NVQSA_ERR_NULL_POINTER;
+  *bytes = 0;
+  if (rows < 1 || query_heads < 1 || kv_heads < 1 || world < 1 || world > 8) return NVQSA_ERR_BAD_SHAPE;
+  const size_t items = (size_t)rows * query_heads;
+  *bytes = (size_t)world * items * (kHeadDim + 1) * sizeof(float) +
+           (size_t)2 * rows * kv_heads * world * sizeof(unsigned int);
+  return NVQSA_OK;
+}
+
+extern "C" int nvqsa_exchange_alloc(size_t bytes, void** ptr) {
+  if (!ptr) return NVQSA_ERR_NULL_POINTER;
+  *ptr = nullptr;
+  if (bytes == 0) return NVQSA_ERR_BAD_SHAPE;
+  // A dedicated allocation (its own IPC handle, offset 0), zeroed: every flag starts disarmed.
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return NVQSA_ERR_CUDA;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return NVQSA_ERR_CUDA;
+  }
+  return NVQSA_OK;
+}
+
+extern "C" int nvqsa_exchange_free(void* ptr) {
+  if (!ptr) return NVQSA_OK;
+  return cudaFree(ptr) == cudaSuccess ? NVQSA_OK : NVQSA_ERR_CUDA;
+}
+
+extern "C" int nvqsa_ipc_get_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return NVQSA_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return NVQSA_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return NVQSA_OK;
+}
+
+extern "C" int nvqsa_ipc_open_handle(const void* handle, void** ptr) {
+  if (!handle || !ptr) return NVQSA_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? NVQSA_OK : NVQSA_ERR_CUDA;
+}
+
+extern "C" int nvqsa_ipc_close_handle(void* ptr) {
+  if (!ptr) return NVQSA_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? NVQSA_OK : NVQSA_ERR_CUDA;
+}
+
+extern "C" int nvqsa_sparse_attention_split_kv(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes,
+    void* const* exchange, int32_t world, int32_t rank, int32_t parity, void* stream) {
+  if (!exchange || !output) return NVQSA_ERR_NULL_POINTER;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || (parity != 0 && parity != 1)) return NVQSA_ERR_BAD_SHAPE;
+  float* peers[8];
+  for (int r = 0; r < world; ++r) {
+    if (!exchange[r]) return NVQSA_ERR_NULL_POINTER;
+    if (!aligned_to(exchange[r], 16)) return NVQSA_ERR_MISALIGNED;
+    peers[r] = static_cast<float*>(exchange[r]);
+  }
+  const void* region[4] = {key_data, key_scale, value_data, value_scale};
+  const int64_t strides[4][3] = {{kd_stride_block, kd_stride_token, kd_stride_head},
+                                 {ks_stride_block, ks_stride_token, ks_stride_head},
+                                 {vd_stride_block, vd_stride_token, vd_stride_head},
+                                 {vs_stride_block, vs_stride_token, vs_stride_head}};
+  return run_attention(query, q_stride_row, q_stride_head, region, strides, num_blocks, page_size, kv_heads,
+                       key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
+                       table_width, token_to_request, output, o_stride_row, o_stride_head, nullptr, nullptr, rows,
+                       query_heads, head_dim, workspace, workspace_bytes, stream, peers, world, rank, parity);
 }
 
 extern "C" int nvqsa_merge_partials_strided(const float* partial_out, int64_t out_split_stride,

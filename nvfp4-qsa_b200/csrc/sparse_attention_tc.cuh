@@ -605,6 +605,9 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_tc_kernel(const 
   }
 
   // ---------------- split-KV beyond one cluster: the last part to arrive merges all parts ----------------
-  if (!p.fuse) return;
+  if (!p.fuse) {
+    if (p.xworld > 0) xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+    return;
+  }
   fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
 }

@@ -87,6 +87,27 @@ _SIGNATURES = {
         _P, _I64, _I64,
         _I64, _I32, _I32,
         _P]),
+    "nvqsa_split_kv_exchange_bytes": (c_int, [_I64, _I32, _I32, _I32, POINTER(c_size_t)]),
+    "nvqsa_exchange_alloc": (c_int, [c_size_t, POINTER(_P)]),
+    "nvqsa_exchange_free": (c_int, [_P]),
+    "nvqsa_ipc_get_handle": (c_int, [_P, _P]),
+    "nvqsa_ipc_open_handle": (c_int, [_P, POINTER(_P)]),
+    "nvqsa_ipc_close_handle": (c_int, [_P]),
+    "nvqsa_sparse_attention_split_kv": (c_int, [
+        _P, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _I64, _I64, _I32,
+        _F, _F,
+        _P, _I64,
+        _P, _I64, _I64,
+        _P,
+        _P, _I64, _I64,
+        _I64, _I32, _I32,
+        _P, c_size_t,
+        _P, _I32, _I32, _I32, _P]),
     "nvqsa_merge_partials": (c_int, [_P, _P, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "nvqsa_merge_partials_strided": (c_int, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     "nvqsa_encode_rows": (c_int, [_P, _I64, _I64, _I32, _P, _P, _P, _P, _P, _P]),

@@ -26,17 +26,27 @@ Two ways to spread the QSA decode over GPUs:
 
 Every rank takes the same collective steps in the same order; the exchange is
 the only collective on the data path.
+
+``SplitKV.attend`` exchanges the partials with NCCL (all_gather) and merges in
+a second kernel.  ``SplitKV.attend_fused`` does the exchange inside the reader
+kernel itself over NVLink peer memory: the CTA that finishes this rank's
+partial of a (row, kv head) stores it into every rank's exchange buffer
+(``PeerExchange``: one buffer per rank, mapped into every process through CUDA
+IPC handles exchanged once over the process group), raises a flag there, waits
+for the other ranks' flags and merges -- one launch per layer, no NCCL call.
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
-from . import kernels
+from . import _native, kernels
 
-__all__ = ["page_range", "shard_requests", "SplitKV"]
+__all__ = ["page_range", "shard_requests", "SplitKV", "PeerExchange"]
 
 
 def page_range(num_pages: int, world: int, rank: int) -> tuple[int, int]:
@@ -147,3 +157,80 @@ class SplitKV:
         outs, lses = self.unpack(gathered, rows, query_heads, head_dim)
         kernels.qsa_merge_partials_strided(outs, lses, output)
         return output
+
+    def attend_fused(self, query, key_data, key_scale, value_data, value_scale, key_global_scale, value_global_scale,
+                      logical_indices, token_to_request, output, exchange: "PeerExchange", block_table=None):
+        """Split-KV decode with the exchange and merge fused into the reader kernel (no NCCL call).
+
+        Every rank calls it with the same ``logical_indices`` and its own cache pages; all get ``output``.
+        """
+        if query.shape[0] != exchange.rows:
+            raise ValueError("the exchange buffers were sized for a different number of rows")
+        if block_table is None:
+            block_table = self.block_table(query.device)
+        kernels.qsa_sparse_paged_attention_nvfp4_split_kv(
+            query, key_data, key_scale, value_data, value_scale, key_global_scale, value_global_scale,
+            logical_indices, block_table, token_to_request, output, exchange.ptrs, exchange.world, exchange.rank,
+            exchange.next_parity())
+        return output
+
+
+class PeerExchange:
+    """Per-rank exchange buffers for ``SplitKV.attend_fused``, mapped on every rank.
+
+    Collective (every rank of ``group`` constructs it with the same ``rows``).  Holds this
+    rank's buffer (``nvqsa_exchange_alloc``) and the peers' buffers opened from their CUDA IPC
+    handles, plus the parity that alternates from call to call.  ``close()`` unmaps and frees.
+    """
+
+    def __init__(self, rows: int, query_heads: int, kv_heads: int, group=None, device=None):
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("the fused split-KV exchange supports at most 8 ranks")
+        self.rows = rows
+        self.lib = _native.load()
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.device = device
+        with torch.cuda.device(device):
+            size = ctypes.c_size_t()
+            _native.check(self.lib.nvqsa_split_kv_exchange_bytes(rows, query_heads, kv_heads, self.world,
+                                                                ctypes.byref(size)), "exchange size")
+            local = ctypes.c_void_p()
+            _native.check(self.lib.nvqsa_exchange_alloc(size.value, ctypes.byref(local)), "exchange alloc")
+            self._local = local.value
+            handle = (ctypes.c_ubyte * 64)()
+            _native.check(self.lib.nvqsa_ipc_get_handle(ctypes.c_void_p(self._local), handle), "ipc handle")
+            handles = [bytes(handle)]
+            if self.world > 1:
+                gathered = [None] * self.world
+                dist.all_gather_object(gathered, bytes(handle), group=group)
+                handles = gathered
+            self._opened = []
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._local)
+                    continue
+                buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+                peer = ctypes.c_void_p()
+                _native.check(self.lib.nvqsa_ipc_open_handle(buf, ctypes.byref(peer)), "ipc open")
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+            self.ptrs = ptrs
+        self.parity = 0
+
+    def next_parity(self) -> int:
+        p = self.parity
+        self.parity ^= 1
+        return p
+
+    def close(self):
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            for ptr in self._opened:
+                self.lib.nvqsa_ipc_close_handle(ctypes.c_void_p(ptr))
+            self._opened = []
+            if self._local:
+                self.lib.nvqsa_exchange_free(ctypes.c_void_p(self._local))
+                self._local = None

@@ -15,6 +15,7 @@ The global K/V scales are fixed for the lifetime of a cache.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 from functools import lru_cache
 
 import torch
@@ -27,6 +28,7 @@ __all__ = [
     "qsa_sparse_paged_attention_nvfp4_partial",
     "qsa_merge_partials",
     "qsa_merge_partials_strided",
+    "qsa_sparse_paged_attention_nvfp4_split_kv",
     "attention_workspace_bytes",
 ]
 
@@ -324,3 +326,59 @@ def qsa_merge_partials_strided(partial_out, partial_lse, output):
             partial_out.data_ptr(), partial_out.stride(0), partial_lse.data_ptr(), partial_lse.stride(0), splits,
             output.data_ptr(), output.stride(0), output.stride(1), rows, query_heads, head_dim, _stream_ptr(device))
     _native.check(status, "qsa_merge_partials_strided")
+
+
+def qsa_sparse_paged_attention_nvfp4_split_kv(
+    query,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    key_global_scale,
+    value_global_scale,
+    logical_indices,
+    block_table,
+    token_to_request,
+    output,
+    exchange_ptrs,
+    world,
+    rank,
+    parity,
+):
+    """Split-KV decode of one sequence across GPUs with the exchange fused into the kernel.
+
+    ``exchange_ptrs``: the ``world`` exchange buffers (this rank's and its peers' as mapped here,
+    see ``nvfp4_qsa.distributed.PeerExchange``).  Every rank makes the same call with its own cache
+    pages and block table and gets the merged bf16 ``output``.
+    """
+    _check_read(query, key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                token_to_request)
+    if output.shape != query.shape or output.dtype != torch.bfloat16 or output.stride(-1) != 1:
+        raise ValueError("NVFP4 QSA output must be bf16 shaped like query with contiguous last dim")
+    device = query.device
+    _check_same_device((key_data, key_scale, value_data, value_scale, logical_indices, block_table,
+                        token_to_request, output), device)
+    rows, query_heads, head_dim = query.shape
+    if rows == 0:
+        return
+    if len(exchange_ptrs) != world:
+        raise ValueError("one exchange buffer per rank is required")
+    topk = logical_indices.shape[1]
+    kv_heads = key_data.shape[2]
+    lib = _native.load()
+    ptrs = (ctypes.c_void_p * world)(*exchange_ptrs)
+    with _device_ctx(device):
+        ws_bytes = _workspace_bytes(torch.cuda.current_device(), rows, query_heads, kv_heads, head_dim, topk)
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+        status = lib.nvqsa_sparse_attention_split_kv(
+            query.data_ptr(), query.stride(0), query.stride(1),
+            *_cache_args(key_data, key_scale, value_data, value_scale),
+            float(key_global_scale), float(value_global_scale),
+            logical_indices.data_ptr(), topk,
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            token_to_request.data_ptr(),
+            output.data_ptr(), output.stride(0), output.stride(1),
+            rows, query_heads, head_dim,
+            workspace.data_ptr() if workspace is not None else None, ws_bytes,
+            ctypes.cast(ptrs, ctypes.c_void_p), int(world), int(rank), int(parity), _stream_ptr(device))
+    _native.check(status, "qsa_sparse_paged_attention_nvfp4_split_kv")

@@ -91,3 +91,36 @@ def test_strided_merge_rejects_overlapping_splits():
     overlapping = outs.view(-1)[: 24 * 256 + 16].as_strided((2, 1, 24, 256), (16, 24 * 256, 256, 1))
     with pytest.raises(ValueError):
         kernels.qsa_merge_partials_strided(overlapping, lses, out)
+
+
+@pytest.mark.parametrize("rows,topk", [(1, 8192), (1, 2048), (3, 4096), (40, 2048)])
+def test_fused_exchange_single_rank_matches_the_reader(rows, topk):
+    # world = 1: the fused path stores this rank's slot, waits for no peer and merges one slot;
+    # called three times so that both flag parities are used and re-armed.
+    dev = torch.device("cuda")
+    context = topk + 1000
+    case = W.decode_config(seed=70 + rows, context=context, topk=topk, page=3136, rows=rows)
+    storage = torch.zeros(case.blocks, 2, case.page, 288, dtype=torch.uint8, device=dev)
+    regs = _regions(storage)
+    kernels.qsa_write_cache_nvfp4(_bits(case.key, dev), _bits(case.value, dev), *regs,
+                                  torch.from_numpy(case.slots).to(dev), 1.0, 1.0)
+    q = _bits(case.query, dev)
+    idx = torch.from_numpy(case.indices).to(dev)
+    bt = torch.from_numpy(case.block_table).to(dev)
+    t2r = torch.from_numpy(case.token_to_request).to(dev)
+    expected = torch.empty_like(q)
+    kernels.qsa_sparse_paged_attention_nvfp4(q, *regs, 1.0, 1.0, idx, bt, t2r, expected)
+    pages = (context + case.page - 1) // case.page
+    sk = D.SplitKV(pages, case.page, 1, 0)
+    ex = D.PeerExchange(rows, 24, 2)
+    try:
+        for _ in range(3):
+            out = torch.full_like(q, float("nan"))
+            sk.attend_fused(q, *regs, 1.0, 1.0, idx, t2r, out, ex, block_table=bt)
+            torch.cuda.synchronize()
+            assert torch.isfinite(out.float()).all()
+            assert (out.float() - expected.float()).abs().max().item() <= 2e-2
+    finally:
+        ex.close()
+    from nvfp4_qsa import _native
+    assert _native.read_error_flags() == 0
