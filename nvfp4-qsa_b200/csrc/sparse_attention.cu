@@ -1056,6 +1056,7 @@ __global__ void __launch_bounds__(256) merge_kernel(MergeArgs a, int64_t rows, i
 }
 
 #include "sparse_attention_tc.cuh"
+#include "sparse_attention_pair.cuh"
 
 // ---------------- host-side planning ----------------
 // 2D tensor map viewing the cache records as rows [rows, 144] of u16 (288 bytes),
@@ -1111,8 +1112,14 @@ bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
   return true;
 }
 
+// The reader kernel of a launch: P.V on tcgen05 (sparse_attention_tc_kernel) or on
+// mma.sync (sparse_attention_kernel), per gather mode, with its shared-memory size.
+constexpr bool kTensorMemoryReader = false;
+constexpr int kReaderCtasPerSm = 3;  // resident CTAs per SM of the full-width reader (registers and shared memory)
+
 struct Plan {
   int splits;
+  bool pair;    // fewer (row, kv head) units than SMs: the warp-pair reader (lower latency per tile)
   int cluster;  // splits of one (row, kv head) merged inside a cluster of this size (1: no cluster)
 };
 constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
@@ -1129,7 +1136,14 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   const int64_t min_splits = (chunks + kMaxChunks - 1) / kMaxChunks;
   int64_t splits = min_splits;
   const int64_t sm_count = sms > 0 ? sms : 148;
-  if (units > 0 && units < sm_count) splits = (sm_count + units - 1) / units;
+  if (units > 0 && units < sm_count) {
+    splits = (sm_count + units - 1) / units;
+  } else if (units > 0) {
+    // Enough splits for every SM to hold the kernel's resident CTAs in one wave (3 splits at 96 rows x 2 kv heads
+    // with 4 CTAs per SM), which also evens out the work per SM.
+    const int64_t fill = (kReaderCtasPerSm * sm_count) / units;
+    if (fill > splits) splits = fill;
+  }
   if (splits > chunks) splits = chunks;
   if (splits < min_splits) splits = min_splits;
   // Beyond one cluster: a multiple of 8 splits in clusters of 8, whose rank-0 parts merge globally
@@ -1137,6 +1151,7 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   if (splits > kMaxClusterSplits) splits = (splits + kMaxClusterSplits - 1) / kMaxClusterSplits * kMaxClusterSplits;
   pl.splits = (int)splits;
   pl.cluster = splits > 1 ? (int)std::min<int64_t>(splits, kMaxClusterSplits) : 1;
+  pl.pair = units > 0 && units < sm_count;
   return pl;
 }
 
@@ -1163,15 +1178,18 @@ size_t workspace_for(const Plan& pl, int64_t rows, int query_heads, int kv_heads
 constexpr int kMaxDevices = 64;
 bool smem_configured[kMaxDevices] = {};
 
-// The reader kernel of a launch: P.V on tcgen05 (sparse_attention_tc_kernel) or on
-// mma.sync (sparse_attention_kernel), per gather mode, with its shared-memory size.
-constexpr bool kTensorMemoryReader = false;
-
 struct ReaderKernel {
   const void* fn;
   size_t smem;  // + slack for the 128-byte alignment of the base
 };
-ReaderKernel reader_kernel(int gather_mode) {
+ReaderKernel reader_kernel(int gather_mode, bool pair) {
+  if (pair && !kTensorMemoryReader) {
+    switch (gather_mode) {
+      case 0: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<0>), sizeof(SmemPair<0>) + 128};
+      case 1: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<1>), sizeof(SmemPair<1>) + 128};
+      default: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<2>), sizeof(SmemPair<2>) + 128};
+    }
+  }
   if (kTensorMemoryReader) {
     switch (gather_mode) {
       case 0: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<0>), sizeof(SmemTc<0>) + 128};
@@ -1191,8 +1209,8 @@ int configure_smem() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    for (int mode = 0; mode < 3; ++mode) {
-      const ReaderKernel rk = reader_kernel(mode);
+    for (int k = 0; k < 6; ++k) {
+      const ReaderKernel rk = reader_kernel(k % 3, k >= 3);
       if (cudaFuncSetAttribute(rk.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rk.smem) != cudaSuccess ||
           cudaFuncSetAttribute(rk.fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return NVQSA_ERR_CUDA;
@@ -1331,7 +1349,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   }
 
   if (const int st = configure_smem()) return st;
-  const ReaderKernel rk = reader_kernel(p.gather_mode);
+  const ReaderKernel rk = reader_kernel(p.gather_mode, pl.pair);
   cudaStream_t s = as_stream(stream);
   if (p.fuse && cudaMemsetAsync(p.counters, 0, (size_t)rows * kv_heads * sizeof(unsigned int), s) != cudaSuccess)
     return NVQSA_ERR_LAUNCH;
