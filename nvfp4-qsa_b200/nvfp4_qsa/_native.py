@@ -143,7 +143,8 @@ def status_text(status: int) -> str:
 
 
 def read_error_flags(clear: bool = True) -> int:
-    """Device error flags of the current device (bit 0: a bounded barrier wait ran out)."""
+    """Device error flags of the current device (bit 0: a bounded barrier wait ran out; bit 1: a split-KV
+    peer's slot did not arrive in time)."""
     flags = ctypes.c_uint32(0)
     check(load().nvqsa_read_error_flags(ctypes.byref(flags), 1 if clear else 0), "nvqsa_read_error_flags")
     return int(flags.value)

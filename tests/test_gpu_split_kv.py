@@ -124,3 +124,47 @@ def test_fused_exchange_single_rank_matches_the_reader(rows, topk):
         ex.close()
     from nvfp4_qsa import _native
     assert _native.read_error_flags() == 0
+
+
+def test_peer_wait_times_out_and_reports_without_a_fault():
+    # Failure detection without a GPU fault: a two-rank exchange where rank 1 never runs.  Rank 0's
+    # kernel stores its slot, raises its flag in the (local stand-in) peer buffer, waits for rank 1's
+    # flag that nothing sets, gives up after its 2 s limit, raises device error bit 1 and leaves the
+    # output untouched; the context stays usable.
+    import ctypes
+    from nvfp4_qsa import _native
+
+    dev = torch.device("cuda")
+    lib = _native.load()
+    case = W.decode_config(seed=90, context=4000, topk=512, page=256, rows=1)
+    storage = torch.zeros(case.blocks, 2, case.page, 288, dtype=torch.uint8, device=dev)
+    regs = _regions(storage)
+    kernels.qsa_write_cache_nvfp4(_bits(case.key, dev), _bits(case.value, dev), *regs,
+                                  torch.from_numpy(case.slots).to(dev), 1.0, 1.0)
+    q = _bits(case.query, dev)
+    idx = torch.from_numpy(case.indices).to(dev)
+    bt = torch.from_numpy(case.block_table).to(dev)
+    t2r = torch.from_numpy(case.token_to_request).to(dev)
+    size = ctypes.c_size_t()
+    _native.check(lib.nvqsa_split_kv_exchange_bytes(1, 24, 2, 2, ctypes.byref(size)), "size")
+    bufs = []
+    for _ in range(2):
+        ptr = ctypes.c_void_p()
+        _native.check(lib.nvqsa_exchange_alloc(size.value, ctypes.byref(ptr)), "alloc")
+        bufs.append(ptr.value)
+    try:
+        _native.read_error_flags(clear=True)
+        out = torch.full_like(q, 7.0)
+        kernels.qsa_sparse_paged_attention_nvfp4_split_kv(q, *regs, 1.0, 1.0, idx, bt, t2r, out, bufs, 2, 0, 0)
+        torch.cuda.synchronize()
+        assert _native.read_error_flags(clear=True) & 2
+        assert (out.float() == 7.0).all()  # nothing stored after the timeout
+        # the context is still usable: an ordinary call afterwards is correct
+        ok = torch.empty_like(q)
+        kernels.qsa_sparse_paged_attention_nvfp4(q, *regs, 1.0, 1.0, idx, bt, t2r, ok)
+        torch.cuda.synchronize()
+        assert torch.isfinite(ok.float()).all()
+        assert _native.read_error_flags() == 0
+    finally:
+        for b in bufs:
+            lib.nvqsa_exchange_free(ctypes.c_void_p(b))
