@@ -200,3 +200,118 @@ def test_raw_op_type_errors():
         kernels.qsa_write_cache_nvfp4(k, k, kd, ks, vd, vs, slots.int(), 1.0, 1.0)
     with pytest.raises(ValueError, match="group-scale"):
         kernels.qsa_write_cache_nvfp4(k, k, kd, ks[..., :8], vd, vs, slots, 1.0, 1.0)
+
+
+def test_division_by_six_matches_ieee_for_every_float(tmp_path):
+    # The writer's group scale g * amax / 6 (oracle.py:54) uses an FMA-corrected
+    # product with RN(1/6); it must equal the IEEE division for all 2^32 inputs.
+    import ctypes
+    import os
+    import subprocess
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    so = tmp_path / "div6_check.so"
+    subprocess.run(["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-shared", "-Xcompiler", "-fPIC",
+                    "-I", os.path.join(root, "include"), "-I", os.path.join(root, "nvfp4-qsa_b200", "csrc"),
+                    os.path.join(root, "tests", "cuda", "div6_check.cu"), "-o", str(so)], check=True)
+    lib = ctypes.CDLL(str(so))
+    bad = ctypes.c_ulonglong(0)
+    first = (ctypes.c_uint * 8)()
+    assert lib.div6_check(ctypes.byref(bad), first) == 0
+    assert bad.value == 0, [hex(v) for v in first]
+
+
+def _scale_sweep_inputs(rng, g, tokens=96, infinities=True):
+    # group amplitudes log-uniform so that g * amax / 6 sweeps the E4M3 range
+    # [2^-12, 2^10] (every scale byte, subnormals and saturation included),
+    # plus all-zero groups, +-inf and NaN inputs
+    x = rng.standard_normal((tokens, 2, 256)).astype(np.float32)
+    x /= np.maximum(np.abs(x).reshape(tokens, 2, 16, 16).max(-1, keepdims=True), 1e-30).repeat(16, -1).reshape(x.shape)
+    amp = 6.0 * np.exp2(rng.uniform(-12, 10, (tokens, 2, 16))) / abs(g)
+    x *= np.minimum(amp, 1e38).astype(np.float32).repeat(16, -1)
+    x[::7, 0, :16] = 0.0
+    if infinities:
+        x[3, 1, 20] = np.inf
+        x[5, 0, 100] = -np.inf
+    x[9, 1, 200] = np.nan
+    return W.f32_to_bf16_bits(x)
+
+
+@pytest.mark.parametrize("gk,gv", [(1.0, 1.0), (0.37, 3e-5), (1e4, 2.0 ** -117), (2.0 ** -118, 1e30), (-2.0, 5e8),
+                                   (2.0 ** 100, 2.0 ** 101), (-(2.0 ** -117), 1.5), (3e38, 0.0)])
+def test_global_scales_across_the_scale_table_paths(gk, gv):
+    # The per-CTA table g / max(e4m3(b), 1e-30) is built from g / k by exact
+    # power-of-two scaling when 2^-117 <= |g| <= 2^100 and by direct division
+    # otherwise; both must give the oracle's bytes, including groups whose
+    # out_scale overflows to inf (zero groups with g >= 3.4e8 -> NaN -> code 0).
+    # g = 0 gets no infinite inputs: 0 * inf is a NaN scale whose sign IEEE
+    # leaves open (x86 gives 0xff, the GPU 0x7f; both decode to NaN).
+    rng = np.random.default_rng(abs(hash((gk, gv))) % 2 ** 32)
+    kb = _scale_sweep_inputs(rng, gk if gk != 0 else 1.0, infinities=gk != 0)
+    vb = _scale_sweep_inputs(rng, gv if gv != 0 else 1.0, infinities=gv != 0)
+    slots = rng.permutation(128)[:96].astype(np.int64)
+    st = torch.zeros(8, 2, 16, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(kb), bits_to_cuda(vb), torch.from_numpy(slots).cuda(), gk, gv)
+    np.testing.assert_array_equal(st.cpu().numpy(), oracle_storage(kb, vb, slots, 8, 16, gk, gv))
+
+
+@pytest.mark.parametrize("page", [1, 3, 7, 16, 1000, 3136, 65537])
+def test_page_sizes_and_slot_edges(page):
+    # slot -> (block, offset) is a multiply-shift division by the page size;
+    # the last valid slot, one past it and negative slots at every page size
+    rng = np.random.default_rng(page)
+    blocks = max(2, 64 // page + 1)
+    n = blocks * page
+    tokens = 40
+    src = W.f32_to_bf16_bits(rng.standard_normal((tokens, 2, 256), dtype=np.float32))
+    # distinct slots below the last one, then the last valid slot, one past the cache and a negative slot
+    slots = np.concatenate([rng.permutation(n - 1)[:tokens - 4], [n - 1, n, n + page, -1]]).astype(np.int64)
+    slots = slots[rng.permutation(tokens)]
+    st = torch.zeros(blocks, 2, page, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(st, bits_to_cuda(src), bits_to_cuda(src), torch.from_numpy(slots).cuda())
+    np.testing.assert_array_equal(st.cpu().numpy(), oracle_storage(src, src, slots, blocks, page))
+
+
+def test_block_stride_above_two_gib_takes_the_64_bit_path():
+    # one block of 3.8M tokens: the block stride (2 x 3.8M x 288 B) exceeds 2^31,
+    # so the writer uses 64-bit index arithmetic and the 64-bit slot division
+    page = 3_800_000
+    st = torch.zeros(1, 2, page, 288, dtype=torch.uint8, device="cuda")
+    assert st.stride(0) > 2 ** 31
+    rng = np.random.default_rng(17)
+    tokens = 48
+    src = W.f32_to_bf16_bits(rng.standard_normal((tokens, 2, 256), dtype=np.float32))
+    slots = rng.choice(page, tokens, replace=False).astype(np.int64)
+    slots[0], slots[1] = page - 1, page  # the last slot, and one past the cache (skipped)
+    gpu_write(st, bits_to_cuda(src), bits_to_cuda(src), torch.from_numpy(slots).cuda())
+    exp = oracle_storage(src, src, np.arange(tokens, dtype=np.int64), (tokens + 15) // 16, 16)
+    exp = exp.transpose(0, 2, 1, 3).reshape(-1, 2, 288)[:tokens]
+    valid = slots < page
+    got = st[0].transpose(0, 1)[torch.from_numpy(slots[valid]).cuda()].cpu().numpy()
+    np.testing.assert_array_equal(got, exp[valid])
+    del st
+    torch.cuda.empty_cache()
+
+
+def test_negative_products_that_underflow_to_zero_get_code_zero():
+    # y = x * out_scale rounds to -0 for a tiny negative x in a group whose
+    # out_scale is tiny (small g, saturated scale): the oracle's sign is y < 0,
+    # so the code is +0 (0x0), not -0 (0x8).  A fused x * s + 0 would keep the
+    # sign of the exact product and write 0x8.
+    x = np.zeros((4, 2, 256), np.float32)
+    x[:, :, 0] = 2.0 ** 32  # amax: g * amax / 6 saturates the scale to 448
+    x[:, :, 1] = -(2.0 ** -133)  # bf16 subnormal
+    x[:, :, 2] = -(2.0 ** -126)
+    x[:, :, 3] = -(2.0 ** -120)
+    x[:, :, 4] = 2.0 ** -133
+    x[:, :, 5] = -0.0
+    x[:, :, 16:] = np.random.default_rng(3).standard_normal((4, 2, 240))
+    bits = W.f32_to_bf16_bits(x)
+    slots = np.arange(4, dtype=np.int64)
+    for g in (2.0 ** -20, 2.0 ** -118):  # table by scaling and by division
+        st = torch.zeros(1, 2, 16, 288, dtype=torch.uint8, device="cuda")
+        gpu_write(st, bits_to_cuda(bits), bits_to_cuda(bits), torch.from_numpy(slots).cuda(), g, g)
+        exp = oracle_storage(bits, bits, slots, 1, 16, g, g)
+        if g == 2.0 ** -20:  # x0 -> +6 (code 7), x1, x2 underflow to -0 -> code 0, x3 rounds to -2^-149 -> 0x8
+            assert exp[0, 0, 0, 0] == 0x07 and exp[0, 0, 0, 1] == 0x80 and exp[0, 0, 0, 2] == 0x00
+        np.testing.assert_array_equal(st.cpu().numpy(), exp, err_msg=f"g={g}")
