@@ -11,7 +11,7 @@ namespace {
 __global__ void encode_rows_kernel(const float* __restrict__ x, int64_t groups, int block_size,
                                    const float* __restrict__ gptr, uint8_t* __restrict__ nibbles,
                                    uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
-                                   int64_t* __restrict__ counts) {
+                                   int64_t* __restrict__ counts, float zero) {
   const float g = __ldg(gptr);
   unsigned long long clip = 0, sat = 0;
   for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups;
@@ -31,7 +31,7 @@ __global__ void encode_rows_kernel(const float* __restrict__ x, int64_t groups, 
       const float y0 = __fmul_rn(__ldg(xp + i), out_scale);
       const float y1 = __fmul_rn(__ldg(xp + i + 1), out_scale);
       clip += (fabsf(y0) > 6.0f) + (fabsf(y1) > 6.0f);  // oracle.py:59 clip6_rate
-      const uint32_t byte = cvt_e2m1x2(e2m1_prepare(y1), e2m1_prepare(y0));
+      const uint32_t byte = cvt_e2m1x2(e2m1_prepare(y1, zero), e2m1_prepare(y0, zero));
       packed[(gi * block_size + i) >> 1] = (uint8_t)byte;
       if (nibbles) {
         nibbles[gi * block_size + i] = (uint8_t)(byte & 0xfu);
@@ -85,7 +85,8 @@ extern "C" int nvqsa_encode_rows(const float* x, int64_t m, int64_t n, int32_t b
   if (!x || !global_scale || !packed || !scales) return NVQSA_ERR_NULL_POINTER;
   const int64_t groups = m * (n / block_size);
   encode_rows_kernel<<<grid_for(groups, 128), 128, 0, as_stream(stream)>>>(x, groups, block_size, global_scale,
-                                                                            nibbles, packed, scales, counts);
+                                                                            nibbles, packed, scales, counts,
+                                                                            0.0f);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }
 

@@ -50,9 +50,12 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&y)[8]) {
 
 // The reference takes sign = (y < 0) and maps NaN to code 0 (all its threshold
 // comparisons are false).  Hardware cvt keeps the sign of -0 and saturates NaN,
-// so normalise first: -0 + 0 = +0 under round-to-nearest, NaN -> 0.
-__device__ __forceinline__ float e2m1_prepare(float y) {
-  float z = __fadd_rn(y, 0.0f);
+// so normalise first: -0 + 0 = +0 under round-to-nearest, NaN -> 0.  `zero`
+// must be a +0.0f the compiler cannot see (a kernel parameter): an add of a
+// literal zero whose only use is the E2M1 conversion is dropped, and -0 then
+// converts to code 8.
+__device__ __forceinline__ float e2m1_prepare(float y, float zero) {
+  float z = __fadd_rn(y, zero);
   return (z != z) ? 0.0f : z;
 }
 

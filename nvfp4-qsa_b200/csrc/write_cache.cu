@@ -56,6 +56,8 @@ struct WriteParams {
   // the compiler drops when the addend is a literal zero feeding the E2M1
   // conversion (that conversion writes code 8 for -0).
   float zero;
+  // 1: both global scales in [2^-6, 2^28] (see the encoder's fast path)
+  int32_t plain;
   int32_t lut_by_scaling;  // 1: scale table by power-of-two scaling of g / k (see build_out_scale_lut)
 };
 
@@ -108,29 +110,41 @@ __device__ __forceinline__ uint32_t group_amax_bits(const uint32_t (&w)[EPL / 2]
 }
 
 // E2M1 codes of the lane's values scaled by out_scale (oracle.py:58-63),
-// EPL/2 bytes with element 2i in the low nibble of byte i.  y = x * s + 0,
-// the product two lanes at a time (f32x2), each step rounded on its own: the + 0 turns an exact -0 (a -0 input, or a tiny
-// negative product that underflows) into +0, as the oracle's sign is y < 0
-// while the hardware conversion keeps the sign of -0; a tiny negative y that
-// rounds to a nonzero value keeps its sign.  `zero` is +0 from a kernel
-// parameter (see WriteParams::zero).  The add stays scalar: a packed f32x2
-// multiply followed by a packed add was contracted into one FMA, which keeps
-// the sign of an underflowing product.  `slow` (warp-uniform) maps NaN to code 0,
-// needed only when an input is NaN or inf or out_scale is NaN or inf (every
-// threshold test of the oracle is false for NaN; the hardware conversion
-// would saturate it).
+// EPL/2 bytes with element 2i in the low nibble of byte i.  The oracle rounds
+// y = x * s and takes sign = y < 0, so an exact -0 (a -0 input, or a negative
+// product that underflows) must give code 0 while a tiny negative y that
+// rounds to a nonzero value keeps code 8; the hardware conversion keeps the
+// sign of -0, hence y = x * s + 0 with +0 from a kernel parameter (see
+// WriteParams::zero).  In the slow path the product (f32x2) and the add are
+// rounded separately -- a packed multiply followed by a packed add was
+// contracted into one FMA, which keeps the sign of an underflowing product --
+// and NaN maps to code 0 (every threshold test of the oracle is false for
+// NaN; the hardware conversion would saturate it).  `slow` is warp-uniform.
 template <int EPL>
 __device__ __forceinline__ void encode_row(const uint32_t (&w)[EPL / 2], float s, float zero, bool slow,
                                            uint32_t (&packed)[(EPL + 7) / 8]) {
+  const float2 s2 = make_float2(s, s);
   float y[EPL];
+  if (!slow) {
+    // Fast path (plain global scales, no NaN or inf in the group): no product
+    // of a nonzero bf16 value underflows to zero (|x| >= 2^-133 and
+    // |s| >= 2^-6 / 448), so one rounding of x * s + 0 equals the two, and an
+    // exact zero product gives +0.
+    const float2 z2 = make_float2(zero, zero);
 #pragma unroll
-  for (int i = 0; i < EPL / 2; ++i) {
-    const float2 m2 = __fmul2_rn(make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u)),
-                                 make_float2(s, s));
-    y[2 * i] = __fadd_rn(m2.x, zero);
-    y[2 * i + 1] = __fadd_rn(m2.y, zero);
-  }
-  if (slow) {
+    for (int i = 0; i < EPL / 2; ++i) {
+      const float2 y2 =
+          __ffma2_rn(make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u)), s2, z2);
+      y[2 * i] = y2.x;
+      y[2 * i + 1] = y2.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL / 2; ++i) {
+      const float2 m2 = __fmul2_rn(make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u)), s2);
+      y[2 * i] = __fadd_rn(m2.x, zero);
+      y[2 * i + 1] = __fadd_rn(m2.y, zero);
+    }
 #pragma unroll
     for (int i = 0; i < EPL; ++i) y[i] = (y[i] != y[i]) ? 0.0f : y[i];
   }
@@ -264,14 +278,16 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
       offset = slot - block * p.page_size;
     }
     const bool two = h0 + 1 < p.kv_heads;
-    // Group scales of the four rows (oracle.py:54-57).  The fast division and
-    // the no-NaN encode hold for finite, non-tiny g * amax and a finite
-    // out_scale; otherwise (one warp vote) every row is redone with the IEEE
-    // division and the encode maps NaN to code 0.  The satfinite E4M3
-    // conversion clamps to +-448 as the oracle's clamp does.
+    // Group scales of the four rows (oracle.py:54-57).  With plain global
+    // scales every table entry a finite non-negative g * amax / 6 can reach is
+    // finite, so the fast division is the only check: it fails for NaN / inf
+    // inputs and tiny or huge g * amax.  Otherwise (one warp vote), or when
+    // the scales are not plain, every row is redone with the IEEE division and
+    // encoded on the slow path.  The satfinite E4M3 conversion clamps to
+    // +-448 as the oracle's clamp does.
     uint32_t amax_bits[4], sb[4];
     float os[4];
-    bool rare = false;
+    bool rare = !p.plain;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       bool exact;
@@ -279,7 +295,7 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
       const float bs = div6_fast(__fmul_rn(p.global_scale[q & 1], __uint_as_float(amax_bits[q])), exact);
       sb[q] = cvt_e4m3(bs);
       os[q] = out_scale_lut[q & 1][sb[q]];
-      rare |= !(exact && amax_bits[q] < 0x7f800000u && (__float_as_uint(os[q]) & 0x7fffffffu) < 0x7f800000u);
+      rare |= !exact;
     }
     const bool slow = __any_sync(0xffffffffu, rare);
     if (slow) {
@@ -440,6 +456,8 @@ extern "C" int nvqsa_write_cache(
   // Scale table by exact power-of-two scaling of g / k when both global scales are in range.
   auto scalable = [](float g) { return std::isfinite(g) && std::fabs(g) >= 0x1p-117f && std::fabs(g) <= 0x1p100f; };
   p.zero = 0.0f;
+  auto plain = [](float g) { return g >= 0x1p-6f && g <= 0x1p28f; };
+  p.plain = (plain(key_global_scale) && plain(value_global_scale)) ? 1 : 0;
   p.lut_by_scaling = (scalable(key_global_scale) && scalable(value_global_scale)) ? 1 : 0;
 
   // Packed-row stores are (head_dim/64)-byte words: rows and strides must be

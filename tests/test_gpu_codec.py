@@ -46,3 +46,23 @@ def test_quant_dequant_and_block_size_32():
     _, p32, s32, _ = nvfp4_qsa.encode(x, torch.tensor(g), block_size=32)
     assert s32.shape == (64, 16) and p32.shape == (64, 256)
     assert nvfp4_qsa.global_scale_for(x).item() == pytest.approx(2688.0 / x.abs().max().item(), rel=1e-6)
+
+
+@pytest.mark.parametrize("g", [1.0, 2.0 ** -10])
+def test_signed_zeros_and_underflowing_products(g):
+    # -0 inputs and negative products that underflow to -0 get code 0 (the
+    # oracle's sign is y < 0); tiny negative products that round to a nonzero
+    # subnormal keep code 8
+    import oracle
+    x = np.zeros((2, 32), np.float32)
+    x[:, 0] = 2688.0 / g  # group scale saturates at 448
+    x[:, 1:6] = [-1e-45, -0.0, -1e-40, -(2.0 ** -140), -(2.0 ** -126)]
+    x[1, 16:] = -0.0  # an all -0 group
+    x[0, 16:] = np.random.default_rng(2).standard_normal(16)
+    nib, packed, scales, _ = nvfp4_qsa.encode(torch.from_numpy(x).cuda(), torch.tensor(g))
+    enib, epacked, escales, _ = oracle.encode(x, g)
+    assert enib[0, 1] == 0 and enib[0, 2] == 0  # -1e-45 underflows, -0 stays zero
+    assert enib[0, 5] == 8  # -2^-126 * s rounds to a nonzero subnormal at both g
+    np.testing.assert_array_equal(scales.cpu().numpy(), escales)
+    np.testing.assert_array_equal(packed.cpu().numpy(), epacked)
+    np.testing.assert_array_equal(nib.cpu().numpy(), enib)

@@ -308,7 +308,7 @@ def test_negative_products_that_underflow_to_zero_get_code_zero():
     x[:, :, 16:] = np.random.default_rng(3).standard_normal((4, 2, 240))
     bits = W.f32_to_bf16_bits(x)
     slots = np.arange(4, dtype=np.int64)
-    for g in (2.0 ** -20, 2.0 ** -118):  # table by scaling and by division
+    for g in (2.0 ** -20, 2.0 ** -118, 1.0):  # slow path (table by scaling, by division); fast path with -0
         st = torch.zeros(1, 2, 16, 288, dtype=torch.uint8, device="cuda")
         gpu_write(st, bits_to_cuda(bits), bits_to_cuda(bits), torch.from_numpy(slots).cuda(), g, g)
         exp = oracle_storage(bits, bits, slots, 1, 16, g, g)
