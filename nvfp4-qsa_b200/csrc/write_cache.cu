@@ -20,6 +20,7 @@
 // a zero scale, so it writes code 0 where the oracle saturates to +-6 for
 // groups whose scale rounds to zero; this kernel follows the oracle.
 #include <cmath>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -119,13 +120,13 @@ __device__ __forceinline__ uint32_t group_amax_bits(const uint32_t (&w)[EPL / 2]
 // rounded separately -- a packed multiply followed by a packed add was
 // contracted into one FMA, which keeps the sign of an underflowing product --
 // and NaN maps to code 0 (every threshold test of the oracle is false for
-// NaN; the hardware conversion would saturate it).  `slow` is warp-uniform.
-template <int EPL>
-__device__ __forceinline__ void encode_row(const uint32_t (&w)[EPL / 2], float s, float zero, bool slow,
+// NaN; the hardware conversion would saturate it).
+template <int EPL, bool SLOW>
+__device__ __forceinline__ void encode_row(const uint32_t (&w)[EPL / 2], float s, float zero,
                                            uint32_t (&packed)[(EPL + 7) / 8]) {
   const float2 s2 = make_float2(s, s);
   float y[EPL];
-  if (!slow) {
+  if constexpr (!SLOW) {
     // Fast path (plain global scales, no NaN or inf in the group): no product
     // of a nonzero bf16 value underflows to zero (|x| >= 2^-133 and
     // |s| >= 2^-6 / 448), so one rounding of x * s + 0 equals the two, and an
@@ -210,16 +211,119 @@ __device__ __forceinline__ void build_out_scale_lut(const WriteParams& p, float 
   }
 }
 
-// One warp per (token, pair of kv heads); grid-stride over all items.  A
-// warp issues every global load of its first item (the slot and the K and V
-// rows of both heads) before the CTA builds its scale table, so the table is
-// built while the loads are in flight; each later item again issues all its
-// loads before the first use.
+// slot -> (block, offset); false for a slot that is negative or past the
+// cache, which the writer skips (kernels.py:71-77).
+template <bool RECORD>
+__device__ __forceinline__ bool slot_position(const WriteParams& p, int64_t slot, int64_t& block, int64_t& offset) {
+  if (slot < 0) return false;
+  if constexpr (RECORD) {  // slot < num_blocks * page_size < 2^31: multiply-shift division
+    if (slot >= p.num_slots) return false;
+    const uint32_t b32 = (uint32_t)(((uint64_t)(uint32_t)slot * p.page_magic) >> p.page_shift);
+    block = b32;
+    offset = (int64_t)((uint32_t)slot - b32 * (uint32_t)p.page_size);
+  } else {
+    block = slot / p.page_size;
+    if (block >= p.num_blocks) return false;
+    offset = slot - block * p.page_size;
+  }
+  return true;
+}
+
+// Encode and store one item: the K and V rows of kv heads h0 and h0 + 1
+// (x = K h0, V h0, K h1, V h1; the h1 rows are ignored when h0 is the last
+// head) into the slot's records.
+template <int EPL, bool RECORD>
+__device__ __forceinline__ void write_item(const WriteParams& p, const float (*out_scale_lut)[256], int lane,
+                                           int64_t block, int64_t offset, int h0, const uint32_t (&x)[4][EPL / 2]) {
+  constexpr int LPG = 16 / EPL;
+  const bool two = h0 + 1 < p.kv_heads;
+  // Group scales of the four rows (oracle.py:54-57).  With plain global
+  // scales every table entry a finite non-negative g * amax / 6 can reach is
+  // finite, so the fast division is the only check: it fails for NaN / inf
+  // inputs and tiny or huge g * amax.  Otherwise (one warp vote), or when the
+  // scales are not plain, every row is redone with the IEEE division and
+  // encoded on the slow path.  The satfinite E4M3 conversion clamps to +-448
+  // as the oracle's clamp does.
+  uint32_t amax_bits[4], sb[4];
+  float os[4];
+  bool rare = !p.plain;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    bool exact;
+    amax_bits[q] = group_amax_bits<EPL>(x[q]);
+    const float bs = div6_fast(__fmul_rn(p.global_scale[q & 1], __uint_as_float(amax_bits[q])), exact);
+    sb[q] = cvt_e4m3(bs);
+    os[q] = out_scale_lut[q & 1][sb[q]];
+    rare |= !exact;
+  }
+  const bool slow = __any_sync(0xffffffffu, rare);
+  if (slow) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      sb[q] = cvt_e4m3(__fdiv_rn(__fmul_rn(p.global_scale[q & 1], __uint_as_float(amax_bits[q])), 6.0f));
+      os[q] = out_scale_lut[q & 1][sb[q]];
+    }
+  }
+  uint8_t* drow[2];
+  uint8_t* srow[2];
+  if constexpr (RECORD) {
+    uint8_t* rec = p.data[0] + ((int64_t)(int32_t)block * p.rec_block32 +
+                                (int32_t)((int32_t)offset * p.rec_token32 + h0 * p.rec_head32));
+    drow[0] = rec;
+    srow[0] = rec + p.off_ks;
+    drow[1] = rec + p.off_vd;
+    srow[1] = rec + p.off_vs;
+  } else {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      drow[r] = p.data[r] + block * p.data_stride[r][0] + offset * p.data_stride[r][1] + h0 * p.data_stride[r][2];
+      srow[r] = p.scale[r] + block * p.scale_stride[r][0] + offset * p.scale_stride[r][1] + h0 * p.scale_stride[r][2];
+    }
+  }
+  // the fast / slow choice is warp-uniform: one branch for the four rows
+  auto encode_store = [&](auto slow_tag) {
+    constexpr bool SLOW = decltype(slow_tag)::value;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      if (hh == 1 && !two) break;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int q = 2 * hh + r;
+        uint32_t packed[(EPL + 7) / 8];
+        encode_row<EPL, SLOW>(x[q], os[q], p.zero, packed);
+        const int64_t hstep_d = RECORD ? (int64_t)p.rec_head32 : p.data_stride[r][2];
+        const int64_t hstep_s = RECORD ? (int64_t)p.rec_head32 : p.scale_stride[r][2];
+        store_lane<EPL>(drow[r] + (hh ? hstep_d : 0), lane, packed);
+        if ((lane % LPG) == 0) (srow[r] + (hh ? hstep_s : 0))[lane / LPG] = (uint8_t)sb[q];
+      }
+    }
+  };
+  if (slow)
+    encode_store(std::true_type{});
+  else
+    encode_store(std::false_type{});
+}
+
+// Item w -> (token, first kv head of its pair).
+template <bool RECORD>
+__device__ __forceinline__ void item_token(int64_t w, int head_pairs, int64_t& token, int& h0) {
+  if constexpr (RECORD) {
+    token = head_pairs == 1 ? w : (int64_t)((uint32_t)w / (uint32_t)head_pairs);
+  } else {
+    token = head_pairs == 1 ? w : w / head_pairs;
+  }
+  h0 = 2 * (int)(w - token * head_pairs);
+}
+
+// One warp per item (token, pair of kv heads), grid-stride over all items,
+// rows loaded into registers.  Any head_dim and layout.  A warp issues every
+// global load of its first item (the slot and the K and V rows of both heads)
+// before the CTA builds its scale table, so the table is built while the
+// loads are in flight.
 template <int HEAD_DIM, bool VEC, bool RECORD>
 __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kernel(const WriteParams p) {
   constexpr int EPL = HEAD_DIM / 32;
   constexpr int NW = EPL / 2;
-  constexpr int LPG = 16 / EPL;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int head_pairs = (p.kv_heads + 1) >> 1;
@@ -227,17 +331,11 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
   __shared__ float out_scale_lut[2][256];
   __shared__ float quot[2][16];
 
-  int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int64_t token = 0, slot = -1;
   int h0 = 0;
   uint32_t x[4][NW];  // K h0, V h0, K h1, V h1
-  auto load_item = [&]() {
-    if constexpr (RECORD) {
-      token = head_pairs == 1 ? w : (int64_t)((uint32_t)w / (uint32_t)head_pairs);
-    } else {
-      token = head_pairs == 1 ? w : w / head_pairs;
-    }
-    h0 = 2 * (int)(w - token * head_pairs);
+  auto load_item = [&](int64_t w) {
+    item_token<RECORD>(w, head_pairs, token, h0);
     slot = __ldg(p.slots + token);
     const bool two = h0 + 1 < p.kv_heads;
     if constexpr (RECORD) {
@@ -259,83 +357,16 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
       }
     }
   };
-  if (w < items) load_item();
+
+  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w0 < items) load_item(w0);
   build_out_scale_lut(p, out_scale_lut, quot);
   __syncthreads();
-
-  for (; w < items; w += warps) {
-    if (w != (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) load_item();
-    if (slot < 0) continue;  // kernels.py:71-77: negative slots are skipped
+  for (int64_t w = w0; w < items; w += warps) {
+    if (w != w0) load_item(w);
     int64_t block, offset;
-    if constexpr (RECORD) {  // slot < num_blocks * page_size < 2^31: multiply-shift division
-      if (slot >= p.num_slots) continue;
-      const uint32_t b32 = (uint32_t)(((uint64_t)(uint32_t)slot * p.page_magic) >> p.page_shift);
-      block = b32;
-      offset = (int64_t)((uint32_t)slot - b32 * (uint32_t)p.page_size);
-    } else {
-      block = slot / p.page_size;
-      if (block >= p.num_blocks) continue;
-      offset = slot - block * p.page_size;
-    }
-    const bool two = h0 + 1 < p.kv_heads;
-    // Group scales of the four rows (oracle.py:54-57).  With plain global
-    // scales every table entry a finite non-negative g * amax / 6 can reach is
-    // finite, so the fast division is the only check: it fails for NaN / inf
-    // inputs and tiny or huge g * amax.  Otherwise (one warp vote), or when
-    // the scales are not plain, every row is redone with the IEEE division and
-    // encoded on the slow path.  The satfinite E4M3 conversion clamps to
-    // +-448 as the oracle's clamp does.
-    uint32_t amax_bits[4], sb[4];
-    float os[4];
-    bool rare = !p.plain;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      bool exact;
-      amax_bits[q] = group_amax_bits<EPL>(x[q]);
-      const float bs = div6_fast(__fmul_rn(p.global_scale[q & 1], __uint_as_float(amax_bits[q])), exact);
-      sb[q] = cvt_e4m3(bs);
-      os[q] = out_scale_lut[q & 1][sb[q]];
-      rare |= !exact;
-    }
-    const bool slow = __any_sync(0xffffffffu, rare);
-    if (slow) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        sb[q] = cvt_e4m3(__fdiv_rn(__fmul_rn(p.global_scale[q & 1], __uint_as_float(amax_bits[q])), 6.0f));
-        os[q] = out_scale_lut[q & 1][sb[q]];
-      }
-    }
-    uint8_t* drow[2];
-    uint8_t* srow[2];
-    if constexpr (RECORD) {
-      uint8_t* rec = p.data[0] + ((int64_t)(int32_t)block * p.rec_block32 +
-                                  (int32_t)((int32_t)offset * p.rec_token32 + h0 * p.rec_head32));
-      drow[0] = rec;
-      srow[0] = rec + p.off_ks;
-      drow[1] = rec + p.off_vd;
-      srow[1] = rec + p.off_vs;
-    } else {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        drow[r] = p.data[r] + block * p.data_stride[r][0] + offset * p.data_stride[r][1] + h0 * p.data_stride[r][2];
-        srow[r] = p.scale[r] + block * p.scale_stride[r][0] + offset * p.scale_stride[r][1] +
-                  h0 * p.scale_stride[r][2];
-      }
-    }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      if (hh == 1 && !two) break;
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int q = 2 * hh + r;
-        uint32_t packed[(EPL + 7) / 8];
-        encode_row<EPL>(x[q], os[q], p.zero, slow, packed);
-        const int64_t hstep_d = RECORD ? (int64_t)p.rec_head32 : p.data_stride[r][2];
-        const int64_t hstep_s = RECORD ? (int64_t)p.rec_head32 : p.scale_stride[r][2];
-        store_lane<EPL>(drow[r] + (hh ? hstep_d : 0), lane, packed);
-        if ((lane % LPG) == 0) (srow[r] + (hh ? hstep_s : 0))[lane / LPG] = (uint8_t)sb[q];
-      }
-    }
+    if (slot_position<RECORD>(p, slot, block, offset))
+      write_item<EPL, RECORD>(p, out_scale_lut, lane, block, offset, h0, x);
   }
 }
 
