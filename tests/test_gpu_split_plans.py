@@ -30,6 +30,11 @@ def _expected_splits(rows, topk, sms):
     splits = min_splits
     if units < sms:
         splits = -(-sms // units)
+    else:
+        fill = 3 * sms // units
+        while fill & (fill - 1):
+            fill &= fill - 1
+        splits = max(splits, fill)
     return max(min(splits, chunks), min_splits)
 
 
@@ -59,6 +64,8 @@ PLANS = [  # (rows, topk): the split count on a 148-SM B200 in the comment
     (80, 8192),   # 8 splits from the 1024-per-CTA limit: cluster of 8
     (3, 4096),    # units 6 -> 25 splits: global workspace, last CTA merges
     (1, 2048),    # units 2 -> 64 splits (one 32-index chunk each): global workspace
+    (74, 2048),   # units 148 = SMs: 3 splits would be clusters of 3; 2 splits, cluster of 2
+    (96, 3072),   # 96 chunks: 3 splits without a cluster (big batch), merged through the workspace
 ]
 
 
