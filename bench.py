@@ -54,6 +54,7 @@ def parse_args():
     ap.add_argument("--split-context", type=int, default=169984, help="split-KV section: one sequence of this length")
     ap.add_argument("--split-topk", type=int, default=8192, help="split-KV section: selected tokens per row")
     ap.add_argument("--skip-split", action="store_true", help="skip the split-KV section")
+    ap.add_argument("--skip-mtp", action="store_true", help="skip the MTP (config 4) section")
     return ap.parse_args()
 
 
@@ -254,6 +255,95 @@ def bench_write(device, steps):
                      "algorithmic_bytes_per_launch": algo,
                      "traffic": profile_traffic("write_cache_prefill.md")},
         "gpu_launches": launches,
+    }
+
+
+def bench_mtp(args, device, steps):
+    """Config 4: MTP=3 decode batch, 12 sequences x 4 rows sharing each sequence's 2,048 selections.
+
+    Contexts U[8,192, 169,984] (seeded), page 3,136, random block tables, 12 layers (one cache each) replayed
+    from one CUDA graph per step.  The grouped reader (rows_per_group=4: one gather and dequantisation per record
+    for the four rows) and the per-row reader run on the same inputs; bytes are the unique records of the step.
+    """
+    import numpy as np
+    import torch
+    from nvfp4_qsa import kernels
+
+    seqs, rows_per_seq, topk, page, layers = 12, 4, 2048, args.page, args.layers
+    rng = np.random.default_rng(2024)
+    contexts = rng.integers(8192, 169984 + 1, size=seqs)
+    widths = [(int(cx) + page - 1) // page for cx in contexts]
+    width = max(widths)
+    blocks = sum(widths)
+    gen = torch.Generator(device=device).manual_seed(4)
+    rows = seqs * rows_per_seq
+    L = []
+    for layer in range(layers):
+        storage = torch.empty(blocks, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        total, chunk = blocks * page, 1 << 20
+        for s0 in range(0, total, chunk):
+            n = min(chunk, total - s0)
+            kv = torch.randn(2, n, KV_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+            kernels.qsa_write_cache_nvfp4(kv[0], kv[1], kd, ks, vd, vs,
+                                          torch.arange(s0, s0 + n, device=device, dtype=torch.int64), 1.0, 1.0)
+        perm = torch.randperm(blocks, device=device, generator=gen).to(torch.int32)
+        table = torch.full((seqs, width), -1, dtype=torch.int32, device=device)
+        b0 = 0
+        for i, w in enumerate(widths):
+            table[i, :w] = perm[b0:b0 + w]
+            b0 += w
+        sel = []
+        for cx in contexts:
+            sel.append(torch.rand(int(cx), device=device, generator=gen).topk(topk).indices.sort().values)
+        idx = torch.stack(sel).to(torch.int32).repeat_interleave(rows_per_seq, dim=0).contiguous()
+        q = torch.randn(rows, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+        L.append(dict(regions=(kd, ks, vd, vs), table=table, idx=idx, q=q, out=torch.empty_like(q)))
+    t2r = torch.arange(seqs, device=device, dtype=torch.int32).repeat_interleave(rows_per_seq).contiguous()
+    torch.cuda.synchronize(device)
+
+    def step(group):
+        for d in L:
+            kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
+                                                     d["out"], rows_per_group=group)
+
+    times = {}
+    for group in (4, 1):
+        step(group)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            step(group)
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(group)
+        for _ in range(3):
+            graph.replay()
+        reps = max(20, steps)
+        times[group] = timed(graph.replay, reps, device) / reps / layers
+        del graph
+    records = seqs * KV_HEADS * topk * RECORD
+    algo = records + rows * topk * 4 + 2 * rows * QUERY_HEADS * HEAD_DIM * 2
+    peak, kind = measured_peaks()
+    g4, g1 = times[4], times[1]
+    return {
+        "config": {"workload": "MTP=3 decode (config 4): 12 sequences x 4 rows sharing 2048 sorted selections per "
+                               "sequence, contexts U[8192, 169984], page 3136, 24 query heads over 2 KV heads, "
+                               f"{layers} layers (one cache each) in one CUDA graph per step",
+                   "l2": f"inputs larger than L2 over a step: {layers} layers x {records / 1e6:.1f} MB of records"},
+        "us_per_layer": g4 * 1e6,
+        "gb_per_s": algo / g4 / 1e9,
+        "per_row_us_per_layer": g1 * 1e6,
+        "per_row_gb_per_s": algo / g1 / 1e9,
+        "speedup_vs_per_row": g1 / g4,
+        "roofline": {"bound": "hbm", "achieved": algo / g4 / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algo / g4 / 1e9 / peak, "peak_kind": kind,
+                     "kernel": "sparse_attention_mtp_kernel (one layer, splits merged in a cluster)",
+                     "algorithmic_bytes_per_launch": algo},
+        "gpu_launches": 2 * (max(20, steps) + 5) * layers,
     }
 
 
@@ -523,6 +613,7 @@ def main_ours(args):
 
     split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
+    mtp = bench_mtp(args, device, args.steps) if rank == 0 and not args.skip_mtp else None
     del graph
     result = None
     if rank == 0:
@@ -557,6 +648,8 @@ def main_ours(args):
         }
         if split is not None:
             result["split_kv"] = split
+        if mtp is not None:
+            result["mtp"] = mtp
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
         print(json.dumps(result), flush=True)

@@ -142,6 +142,38 @@ int nvqsa_sparse_attention(
     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Grouped variant for multi-token-prediction (MTP) decode batches, where the
+ * draft rows of a sequence attend to one shared selection list: rows
+ * [g * rows_per_group, (g + 1) * rows_per_group) form group g.  Same
+ * arguments, masking and result as nvqsa_sparse_attention (the reference
+ * interface it extends is qsa_sparse_paged_attention_nvfp4,
+ * python/nvfp4_qsa/kernels.py:348-403); rows_per_group is a hint only.  When
+ * rows_per_group * G <= 48, rows_per_group is 2..4 and the cache is the
+ * canonical [blocks, kv_heads, page, 288] storage, each selected record is
+ * gathered and dequantised once per group instead of once per row; every CTA
+ * verifies on the device that the group's rows have the same request and the
+ * same selections for its share of the index positions, and processes a
+ * group that does not share row by row.  Otherwise (or with rows_per_group
+ * 1) the call is nvqsa_sparse_attention.  The grouped kernel needs no
+ * workspace; pass the one nvqsa_sparse_attention_workspace_size gives.
+ * rows_per_group outside 1..4 -> NVQSA_ERR_BAD_SHAPE.
+ */
+int nvqsa_sparse_attention_grouped(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, int32_t rows_per_group,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Partial (un-merged) variant for split-KV across devices: writes, for every
  * (row, query head), the softmax-normalized output of the selections this
  * device holds, already divided by value_global_scale, and its base-2

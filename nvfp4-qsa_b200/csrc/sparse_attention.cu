@@ -108,6 +108,7 @@ struct AttnParams {
   // exchange buffer over NVLink, then the unit's final CTA waits for every rank's slot and merges them.
   int32_t xworld, xrank, xparity;
   float* xpeer[8];               // exchange buffer of every rank, as mapped in this process
+  int32_t group_rows;            // grouped reader: consecutive rows per group that may share their selections
   int32_t vec_q;                 // 16-byte aligned query rows
   int32_t vec_o;                 // 16-byte aligned output rows
   __nv_bfloat16* out;
@@ -1057,6 +1058,7 @@ __global__ void __launch_bounds__(256) merge_kernel(MergeArgs a, int64_t rows, i
 
 #include "sparse_attention_tc.cuh"
 #include "sparse_attention_pair.cuh"
+#include "sparse_attention_mtp.cuh"
 
 // ---------------- host-side planning ----------------
 // 2D tensor map viewing the cache records as rows [rows, 144] of u16 (288 bytes),
@@ -1160,6 +1162,31 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
   return pl;
 }
 
+// Grouped (MTP) reader plan: groups of rows_per_group consecutive rows, power-of-two splits (one cluster
+// of at most 16 per group, each CTA at most 1024 selections) until the launch fills the SMs' three
+// resident CTAs: a group's tiles are processed in order by its CTA, so more splits mean shorter chains.
+struct MtpPlan {
+  bool use;
+  int splits;
+  int64_t grid;
+};
+MtpPlan make_mtp_plan(int64_t rows, int kv_heads, int64_t topk, int G, int rows_per_group, int sms) {
+  MtpPlan mp{false, 1, 0};
+  if (rows_per_group < 2 || rows_per_group * G > kMtpHeads || topk < 1) return mp;
+  const int64_t units = (rows + rows_per_group - 1) / rows_per_group * kv_heads;
+  const int64_t chunks = (topk + kChunk - 1) / kChunk;
+  int64_t splits = 1;
+  while (splits * kMaxChunks < chunks) splits *= 2;
+  if (splits > kMtpMaxCluster) return mp;
+  const int64_t target = 3 * (int64_t)(sms > 0 ? sms : 148);
+  while (splits < kMtpMaxCluster && splits * 2 <= chunks && units * splits * 2 <= target) splits *= 2;
+  if (units * splits > 0x7fffffffLL) return mp;
+  mp.use = true;
+  mp.splits = (int)splits;
+  mp.grid = units * splits;
+  return mp;
+}
+
 // Workspace of a split launch: partial outputs [splits][rows][heads][256] fp32,
 // partial lse [splits][rows][heads] fp32 (padded to 256 bytes), then one
 // arrival counter per (row, kv head), zeroed on the launch's stream.
@@ -1220,6 +1247,13 @@ int configure_smem() {
           cudaFuncSetAttribute(rk.fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return NVQSA_ERR_CUDA;
     }
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(sparse_attention_mtp_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sizeof(SmemMtp) + 128)) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(sparse_attention_mtp_kernel),
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(sparse_attention_mtp_kernel),
+                             cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return NVQSA_ERR_CUDA;
     smem_configured[dev] = true;
   }
   return NVQSA_OK;
@@ -1232,7 +1266,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
                   const int32_t* token_to_request, void* output, int64_t o_stride_row, int64_t o_stride_head,
                   float* partial_out, float* partial_lse, int64_t rows, int32_t query_heads, int32_t head_dim,
                   void* workspace, size_t workspace_bytes, void* stream, float* const* xpeers = nullptr,
-                  int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0) {
+                  int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0, int32_t rows_per_group = 1) {
   if (rows < 0 || topk < 0 || kv_heads < 1 || query_heads < 1 || num_blocks < 0 || page_size < 1 ||
       num_requests < 0 || table_width < 0)
     return NVQSA_ERR_BAD_SHAPE;
@@ -1261,13 +1295,16 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
 
   const int sms = device_sm_count();
   if (sms <= 0) return NVQSA_ERR_CUDA;
-  const Plan pl = make_plan(rows, kv_heads, topk, sms);
-  const Workspace wl = workspace_layout(pl, rows, query_heads, kv_heads);
+  if (rows_per_group < 1 || rows_per_group > kMtpRows) return NVQSA_ERR_BAD_SHAPE;
+  const MtpPlan mp = make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
+  const Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms);
+  const Workspace wl = mp.use ? Workspace{0, 0, 0} : workspace_layout(pl, rows, query_heads, kv_heads);
   const size_t need = wl.bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned_to(workspace, 16))) return NVQSA_ERR_WORKSPACE;
-  if ((int64_t)pl.splits * rows * kv_heads > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;
+  if (!mp.use && (int64_t)pl.splits * rows * kv_heads > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;
   // The last part's merge keeps one weight per (part, head) in the CTA's ring space.
-  if ((size_t)(pl.splits / pl.cluster) * 16 * sizeof(float) + 128 > sizeof(Smem::rec)) return NVQSA_ERR_UNSUPPORTED;
+  if (!mp.use && (size_t)(pl.splits / pl.cluster) * 16 * sizeof(float) + 128 > sizeof(Smem::rec))
+    return NVQSA_ERR_UNSUPPORTED;
 
   AttnParams p;
   p.q = static_cast<const __nv_bfloat16*>(query);
@@ -1310,6 +1347,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.token_to_request = token_to_request;
   p.rows = rows;
   p.splits = pl.splits;
+  p.group_rows = 1;
   p.vec_q = (aligned_to(query, 16) && q_stride_row % 8 == 0 && q_stride_head % 8 == 0) ? 1 : 0;
   p.vec_o = (!partial_mode && aligned_to(output, 16) && o_stride_row % 8 == 0 && o_stride_head % 8 == 0) ? 1 : 0;
   p.out = static_cast<__nv_bfloat16*>(output);
@@ -1354,6 +1392,37 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   }
 
   if (const int st = configure_smem()) return st;
+  if (mp.use && p.gather_mode == 0 && p.mode == 0 && xworld == 0 && !p.fuse) {
+    // grouped reader: the splits of a group form one cluster, merged in shared memory
+    p.splits = mp.splits;
+    p.cluster = mp.splits;
+    p.group_rows = rows_per_group;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)mp.grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = sizeof(SmemMtp) + 128;
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)mp.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = mp.splits > 1 ? 1 : 0;
+    void* args[1] = {&p};
+    if (cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(sparse_attention_mtp_kernel), args) != cudaSuccess)
+      return NVQSA_ERR_LAUNCH;
+    if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;
+    return NVQSA_OK;
+  }
+  if (mp.use) {
+    // not eligible after all (layout, output mode): the per-row reader with its own plan
+    return run_attention(query, q_stride_row, q_stride_head, region, strides, num_blocks, page_size, kv_heads,
+                         key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
+                         table_width, token_to_request, output, o_stride_row, o_stride_head, partial_out, partial_lse,
+                         rows, query_heads, head_dim, workspace, workspace_bytes, stream, xpeers, xworld, xrank,
+                         xparity, 1);
+  }
   const ReaderKernel rk = reader_kernel(p.gather_mode, pl.pair);
   cudaStream_t s = as_stream(stream);
   if (p.fuse && cudaMemsetAsync(p.counters, 0, (size_t)rows * kv_heads * sizeof(unsigned int), s) != cudaSuccess)
@@ -1430,6 +1499,31 @@ extern "C" int nvqsa_sparse_attention(
                        key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
                        table_width, token_to_request, output, o_stride_row, o_stride_head, nullptr, nullptr, rows,
                        query_heads, head_dim, workspace, workspace_bytes, stream);
+}
+
+extern "C" int nvqsa_sparse_attention_grouped(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    const void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    const void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    const void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    float key_global_scale, float value_global_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim, int32_t rows_per_group,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const void* region[4] = {key_data, key_scale, value_data, value_scale};
+  const int64_t strides[4][3] = {{kd_stride_block, kd_stride_token, kd_stride_head},
+                                 {ks_stride_block, ks_stride_token, ks_stride_head},
+                                 {vd_stride_block, vd_stride_token, vd_stride_head},
+                                 {vs_stride_block, vs_stride_token, vs_stride_head}};
+  return run_attention(query, q_stride_row, q_stride_head, region, strides, num_blocks, page_size, kv_heads,
+                       key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
+                       table_width, token_to_request, output, o_stride_row, o_stride_head, nullptr, nullptr, rows,
+                       query_heads, head_dim, workspace, workspace_bytes, stream, nullptr, 0, 0, 0, rows_per_group);
 }
 
 extern "C" int nvqsa_sparse_attention_partial(

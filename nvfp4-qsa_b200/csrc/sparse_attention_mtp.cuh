@@ -1,0 +1,585 @@
+// QSA sparse decode reader for groups of query rows that share one selection
+// list: the MTP (multi-token prediction) decode batch, where the draft tokens
+// of a sequence attend to the same selected cache tokens (config 4: 12
+// sequences x 4 rows, 12 query heads per kv head).  Included by
+// sparse_attention.cu inside namespace nvqsa::{anonymous}; uses its parameter
+// block, barrier, copy, conversion and cluster helpers.
+//
+// One CTA = (group of up to 4 consecutive rows, kv head, split); the CTA
+// gathers each selected record ONCE into a CTA-wide ring (tile::gather4) and
+// all four warps use it:
+//   * K: warp w dequantises dims [64w, 64w + 64) of the tile's 16 records into
+//     a shared f16 tile (exact: e2m1 x e4m3);
+//   * S = Q K^T: warp w computes the scores of row w of the group (its query
+//     heads in one m16 tile) over all 256 dims, K fragments by ldmatrix, and
+//     runs that row's online softmax; P goes to a shared tile of the group's
+//     packed heads (row-major, up to 48 = 3 m16 tiles);
+//   * O += P V: warp w accumulates dims [64w, 64w + 64) of every packed head
+//     (96 fp32 registers), V dequantised in registers once per tile.
+// So the gather and the dequantisation are paid once per record for all rows
+// of the group instead of once per row.
+//
+// Sharing is verified on the device, never assumed: each CTA compares the
+// rows' request and the index positions of its chunks against the group's
+// first row, and the CTAs of a cluster agree on the result.  A group that does
+// not share is processed row by row (one pass per row, one active S warp).
+//
+// Splits of a group form one thread-block cluster (1, 2, 4, 8 or 16 CTAs):
+// every rank publishes its (O, m, l) in shared memory, then every rank merges
+// one slice of the output fragments of all ranks over distributed shared
+// memory and stores it.
+
+constexpr int kMtpStages = 3;     // ring stages of 16 records
+constexpr int kMtpHeads = 48;     // packed query heads of a group (rows x group size)
+constexpr int kMtpMTiles = 3;     // m16 tiles of packed heads
+constexpr int kKhStride = 264;    // halfs per token row of the dequantised K tile (256 + 8: ldmatrix conflict-free)
+constexpr int kPhStride = 24;     // halfs per head row of the P tile (16 + 8: ldmatrix conflict-free)
+constexpr int kMtpRows = 4;       // rows per group (one S warp each)
+constexpr int kMtpMaxCluster = 8;   // splits of a group: one portable cluster
+
+struct __align__(128) SmemMtp {
+  // rec, kh and qf are contiguous: after the last tile they hold the cluster merge's published O.
+  uint8_t rec[kMtpStages][kStageBytes];   // gather ring, CTA-wide
+  __half kh[2][kTile][kKhStride];         // dequantised K of a tile, double-buffered
+  uint4 qf[kMtpRows][16][33];             // Q A-fragments of each row: [row][k-step][lane] (+1: conflict-free stores)
+  __half ph[2][kMtpHeads][kPhStride];     // P of a tile (packed heads x tokens), double-buffered
+  int32_t sel[kMaxRange];                 // record rows (gather4) of the valid shared selections
+  float alpha[2][kMtpHeads];              // rescale factor of each packed head (read only when its row rescaled)
+  int resc[2][kMtpRows];                  // row rescaled its running max in this tile
+  float smul[kMtpHeads];
+  float m_s[kMtpHeads];
+  float l_s[kMtpHeads];
+  unsigned long long full_bar[kMtpStages];
+  int cnt[kCompactIters][kWarps];
+  int total;
+  int abort;
+  int shared_ok;
+};
+static_assert(sizeof(float4) * kWarps * 24 * 32 <=
+                  sizeof(SmemMtp::rec) + sizeof(SmemMtp::kh) + sizeof(SmemMtp::qf),
+              "published O must fit the ring, K and Q space");
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+               : "r"(addr));
+}
+
+__global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  SmemMtp& sm = *reinterpret_cast<SmemMtp*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int r = lane >> 2;  // mma group row
+  const int c = lane & 3;   // mma thread-in-group
+  const int G = p.group;
+
+  int64_t bid = blockIdx.x;
+  const int split = (int)(bid % p.splits);
+  bid /= p.splits;
+  const int kvh = (int)(bid % p.kv_heads);
+  const int64_t grp = bid / p.kv_heads;
+  const int64_t row_lo = grp * p.group_rows;
+  const int nrows = (int)min((int64_t)p.group_rows, p.rows - row_lo);
+
+  const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
+  const int my_chunks = split < chunks ? (int)((chunks - 1 - split) / p.splits + 1) : 0;  // <= kMaxChunks
+  const int iters = (my_chunks + kWarps - 1) / kWarps;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int b = 0; b < kMtpStages; ++b) mbar_init(smem_u32(&sm.full_bar[b]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    sm.abort = 0;
+  }
+
+  // ---------------- do the group's rows share request and selections (this CTA's chunks)? ----------------
+  bool same = true;
+  {
+    const int32_t req0 = __ldg(p.token_to_request + row_lo);
+    for (int i = 1; i < nrows; ++i) same &= __ldg(p.token_to_request + row_lo + i) == req0;
+    const int32_t* idx0 = p.indices + row_lo * p.topk;
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      const int lc = it * kWarps + warp;
+      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
+      if (lc < my_chunks && pos < p.topk) {
+        const int32_t v0 = __ldg(idx0 + pos);
+        int32_t vi[kMtpRows - 1];
+#pragma unroll
+        for (int i = 1; i < kMtpRows; ++i) vi[i - 1] = i < nrows ? __ldg(idx0 + (int64_t)i * p.topk + pos) : v0;
+#pragma unroll
+        for (int i = 1; i < kMtpRows; ++i) same &= vi[i - 1] == v0;
+      }
+    }
+  }
+  same = __syncthreads_and(same) != 0;
+  if (p.cluster > 1) {
+    // every rank of the cluster takes the same passes
+    if (tid == 0) sm.shared_ok = same ? 1 : 0;
+    cluster_sync();
+    if (tid == 0) {
+      int all = 1;
+      for (int rk = 0; rk < p.cluster; ++rk) all &= cluster_ld_s32(cluster_map(smem_u32(&sm.shared_ok), (uint32_t)rk));
+      sm.total = all;
+    }
+    cluster_sync();  // no rank rewrites shared_ok before every rank has read it
+    same = sm.total != 0;
+  }
+  const int passes = same ? 1 : nrows;
+  int tiles_done = 0;  // tiles consumed in earlier passes: ring stage and phase carry over
+
+  for (int pass = 0; pass < passes; ++pass) {
+    const int64_t prow = same ? row_lo : row_lo + pass;  // row whose selections the gather follows
+    const int act = same ? nrows : 1;                    // active S warps (rows) of this pass
+    bool aborted = sm.abort != 0;
+
+    // ---------------- prologue: selections, block table, Q of the active rows ----------------
+    const int32_t req = __ldg(p.token_to_request + prow);
+    const int32_t* idx_row = p.indices + prow * p.topk;
+    int32_t iv[kCompactIters];
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      const int lc = it * kWarps + warp;
+      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
+      iv[it] = (lc < my_chunks && pos < p.topk) ? __ldg(idx_row + pos) : -1;
+    }
+    // warp w loads row w's heads: lane L holds dims [8L, 8L + 8) of each head
+    uint32_t qw[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
+      if (warp < act && j < G) {
+        const __nv_bfloat16* qrow =
+            p.q + (prow + warp) * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
+        if (p.vec_q) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
+          qw[j][0] = v.x; qw[j][1] = v.y; qw[j][2] = v.z; qw[j][3] = v.w;
+        } else {
+          const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) qw[j][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
+        }
+      }
+    }
+    const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
+    const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
+    const bool huge_page = p.page_size > 0x7fffffffLL;
+    int32_t rowid[kCompactIters];
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      rowid[it] = -1;
+      const int32_t idx = iv[it];
+      if (req_ok && idx >= 0) {
+        const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
+        if ((int64_t)lpage < p.table_width) {
+          const int32_t phys = __ldg(bt_row + lpage);
+          const int32_t off = huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size);
+          if (phys >= 0 && (int64_t)phys < p.num_blocks) rowid[it] = (phys * p.kv_heads + kvh) * (int32_t)p.page_size + off;
+        }
+      }
+    }
+
+    // Q: per-head power-of-two pre-scale (exact) into f16 A-fragments of the row's m16 tile (natural
+    // dim order: k-step s covers dims [16s, 16s + 16)); heads >= G stay zero.
+    if (warp < kMtpRows) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        uint32_t amax = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) amax = max(amax, max((qw[j][t] << 16) & 0x7fffffffu, qw[j][t] & 0x7fff0000u));
+#pragma unroll
+        for (int m = 16; m; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        // scale 2^e brings the head's amax to [2^14, 2^15); |e| <= 100 keeps both products exact
+        int e = 0;
+        if (amax >= 0x00800000u && amax < 0x7f800000u) e = max(-100, min(100, 14 - ((int)(amax >> 23) - 127)));
+        if (lane == 0 && j < G && warp < act)
+          sm.smul[warp * G + j] = p.score_scale * __int_as_float((127 - e) << 23);
+        const float mul = __int_as_float((127 + e) << 23);
+        // lane L holds dims 8L..8L+7 = k-step L/2, columns 8(L%2)..+7: pairs (2cc, 2cc+1) of half L%2
+        const int s = lane >> 1, hi = lane & 1;
+        uint32_t* f = reinterpret_cast<uint32_t*>(&sm.qf[warp][s][0]);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const uint32_t x = qw[j][cc];
+          // register 2*hi + (j >= 8) of lane (j % 8) * 4 + cc
+          f[((j & 7) * 4 + cc) * 4 + 2 * hi + (j >> 3)] = pack_half2(bf16_lo(x) * mul, bf16_hi(x) * mul);
+        }
+      }
+    }
+
+    // compact the valid selections
+    uint32_t vmask = 0;
+    int pre[kCompactIters];
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      pre[it] = 0;
+      if (it < iters) {
+        const bool valid = rowid[it] >= 0;
+        const uint32_t b = __ballot_sync(0xffffffffu, valid);
+        pre[it] = __popc(b & ((1u << lane) - 1u));
+        if (valid) vmask |= 1u << it;
+        if (lane == 0) sm.cnt[it][warp] = __popc(b);
+      }
+    }
+    // P rows of inactive heads stay zero for the whole pass
+    for (int i = tid; i < 2 * kMtpHeads * kPhStride / 2; i += kThreads) reinterpret_cast<uint32_t*>(&sm.ph[0][0][0])[i] = 0u;
+    __syncthreads();
+    {
+      int base_all = 0;
+#pragma unroll
+      for (int it = 0; it < kCompactIters; ++it) {
+        if (it < iters) {
+          int base = base_all;
+          for (int w = 0; w < warp; ++w) base += sm.cnt[it][w];
+          if (vmask & (1u << it)) sm.sel[base + pre[it]] = rowid[it];
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) base_all += sm.cnt[it][w];
+        }
+      }
+      if (tid == 0) sm.total = base_all;
+    }
+    __syncthreads();
+    const int n = sm.total;
+    const int ntiles = (n + kTile - 1) / kTile;
+
+    // ---------------- CTA-wide gather ring: warp 0 issues, every warp consumes ----------------
+    auto issue_tile = [&](int k) {
+      const int st = (tiles_done + k) % kMtpStages;
+      const uint32_t bar = smem_u32(&sm.full_bar[st]);
+      const int j0 = k * kTile;
+      const int count = min(kTile, n - j0);
+      // the stage was last read by generic loads (ordered before the barrier that let us here)
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+      __syncwarp();
+      if (lane < kTile / 4) {
+        int32_t rows[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int t = group_token(lane, j);
+          rows[j] = t < count ? sm.sel[j0 + t] : p.total_rows;  // out of range: zero fill
+        }
+        gather4_g2s(smem_u32(&sm.rec[st][lane * 4 * kRecordBytes]), &p.rows_map, rows[0], rows[1], rows[2], rows[3],
+                    bar);
+      }
+    };
+    if (warp == 0 && !aborted) {
+      for (int k = 0; k < kMtpStages - 1 && k < ntiles; ++k) issue_tile(k);
+    }
+
+    float oacc[kMtpMTiles][8][4];
+#pragma unroll
+    for (int t = 0; t < kMtpMTiles; ++t)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oacc[t][j][0] = oacc[t][j][1] = oacc[t][j][2] = oacc[t][j][3] = 0.0f;
+    const bool srow = warp < act;  // this warp runs a row's scores and softmax
+    const float smul_r = (srow && r < G) ? sm.smul[warp * G + r] : 1.0f;
+    const float smul_r8 = (srow && r + 8 < G) ? sm.smul[warp * G + r + 8] : 1.0f;
+    float m_r = kMaskedScore, m_r8 = kMaskedScore;
+    float l_r = 0.0f, l_r8 = 0.0f;
+    // ldmatrix row addresses: K (tokens x dims) for B of S, P (heads x tokens) for A of P V
+    const uint32_t kh_lane = (uint32_t)(((((lane >> 4) << 3) + (lane & 7)) * kKhStride + ((lane >> 3) & 1) * 8) * 2);
+    const uint32_t ph_lane = (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kPhStride + (lane >> 4) * 8) * 2);
+    const int vtok[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+
+    int k = 0;
+    for (; k < ntiles && !aborted; ++k) {
+      const int st = (tiles_done + k) % kMtpStages;
+      const bool ok = mbar_wait(smem_u32(&sm.full_bar[st]), (uint32_t)(((tiles_done + k) / kMtpStages) & 1));
+      const uint8_t* stage = sm.rec[st];
+      const int buf = k & 1;
+      // ---- K: warp w dequantises dims [64w, 64w + 64); lane -> token lane/2, dims 64w + 32 (lane % 2) + [0, 32) ----
+      {
+        const int t = lane >> 1, h = lane & 1;
+        const uint8_t* rec = stage + slot_off(t);
+        const uint4 kb = *reinterpret_cast<const uint4*>(rec + 32 * warp + 16 * h);
+        const uint32_t sc = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 4 * warp + 2 * h));
+        const uint32_t s0 = dup_lo(sc), s1 = dup_hi(sc);
+        const uint32_t wd[4] = {kb.x, kb.y, kb.z, kb.w};
+        uint32_t o[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t sg = q < 2 ? s0 : s1;
+          o[4 * q + 0] = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(wd[q]), sg);
+          o[4 * q + 1] = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(wd[q]), sg);
+          o[4 * q + 2] = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(wd[q]), sg);
+          o[4 * q + 3] = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(wd[q]), sg);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(&sm.kh[buf][t][64 * warp + 32 * h]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      }
+      if (!__syncthreads_and(ok)) {  // (A) K tile complete; every warp is past the previous tile's P V
+        if (tid == 0) sm.abort = 1;
+        aborted = true;
+        break;
+      }
+      if (warp == 0 && k + kMtpStages - 1 < ntiles) issue_tile(k + kMtpStages - 1);  // into tile k-1's stage
+
+      // ---- S = Q K^T for row `warp`, online softmax, P into the packed tile ----
+      if (srow) {
+        float sacc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+        const uint32_t kaddr = smem_u32(&sm.kh[buf][0][0]) + kh_lane;
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kaddr + 32u * s, b0, b1, b2, b3);
+          const uint4 qa = sm.qf[warp][s][lane];
+          mma_f16(sacc[0], qa.x, qa.y, qa.z, qa.w, b0, b1);
+          mma_f16(sacc[1], qa.x, qa.y, qa.z, qa.w, b2, b3);
+        }
+        const int tok_base = k * kTile;
+        if (tok_base + kTile > n) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int t0 = tok_base + 8 * nt + 2 * c;
+            if (t0 >= n) { sacc[nt][0] = -1.0e30f; sacc[nt][2] = -1.0e30f; }
+            if (t0 + 1 >= n) { sacc[nt][1] = -1.0e30f; sacc[nt][3] = -1.0e30f; }
+          }
+        }
+        float mx_r = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
+        float mx_r8 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
+        mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 1));
+        mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 2));
+        mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 1));
+        mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 2));
+        mx_r *= smul_r;
+        mx_r8 *= smul_r8;
+        const bool up_r = mx_r > m_r + kRescaleThreshold;
+        const bool up_r8 = mx_r8 > m_r8 + kRescaleThreshold;
+        const bool up = __any_sync(0xffffffffu, up_r || up_r8);
+        if (up) {
+          const float mn_r = up_r ? mx_r : m_r, mn_r8 = up_r8 ? mx_r8 : m_r8;
+          const float a_r = ex2(m_r - mn_r), a_r8 = ex2(m_r8 - mn_r8);
+          m_r = mn_r;
+          m_r8 = mn_r8;
+          l_r *= a_r;
+          l_r8 *= a_r8;
+          if (c == 0) {
+            if (r < G) sm.alpha[buf][warp * G + r] = a_r;
+            if (r + 8 < G) sm.alpha[buf][warp * G + r + 8] = a_r8;
+          }
+        }
+        if (lane == 0) sm.resc[buf][warp] = up ? 1 : 0;
+        float pv[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          pv[nt][0] = ex2(fmaf(sacc[nt][0], smul_r, -m_r));
+          pv[nt][1] = ex2(fmaf(sacc[nt][1], smul_r, -m_r));
+          pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
+          pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
+        }
+        if (tok_base + kTile > n) {  // masked scores must not count even while the running max is still -1e20
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int t0 = tok_base + 8 * nt + 2 * c;
+            if (t0 >= n) { pv[nt][0] = 0.0f; pv[nt][2] = 0.0f; }
+            if (t0 + 1 >= n) { pv[nt][1] = 0.0f; pv[nt][3] = 0.0f; }
+          }
+        }
+        l_r += (pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1]);
+        l_r8 += (pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          if (r < G)
+            *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r][8 * nt + 2 * c]) = pack_half2(pv[nt][0], pv[nt][1]);
+          if (r + 8 < G)
+            *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r + 8][8 * nt + 2 * c]) =
+                pack_half2(pv[nt][2], pv[nt][3]);
+        }
+      } else if (lane == 0) {
+        sm.resc[buf][warp] = 0;
+      }
+      __syncthreads();  // (B) P and the rescale factors of every row are in place
+
+      // ---- O += P V over dims [64w, 64w + 64) of every packed head ----
+      {
+        const int any = sm.resc[buf][0] | sm.resc[buf][1] | sm.resc[buf][2] | sm.resc[buf][3];
+        if (any) {
+#pragma unroll
+          for (int t = 0; t < kMtpMTiles; ++t) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int head = 16 * t + r + 8 * hh;
+              const int hrow = head / G;
+              const float a = (head < act * G && sm.resc[buf][hrow]) ? sm.alpha[buf][head] : 1.0f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                oacc[t][j][2 * hh] *= a;
+                oacc[t][j][2 * hh + 1] *= a;
+              }
+            }
+          }
+        }
+        uint32_t pa[kMtpMTiles][4];
+        const uint32_t paddr = smem_u32(&sm.ph[buf][0][0]) + ph_lane;
+#pragma unroll
+        for (int t = 0; t < kMtpMTiles; ++t)
+          ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
+        // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9}, dims 64w + 8r + [0, 8)
+        uint32_t vw[4], vsb[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint8_t* rec = stage + slot_off(vtok[q]);
+          vw[q] = *reinterpret_cast<const uint32_t*>(rec + 144 + 32 * warp + 4 * r);
+          vsb[q] = rec[272 + 4 * warp + (r >> 1)];
+        }
+        const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
+        const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
+        // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
+        const uint32_t x01 = (vw[0] & 0x0f0f0f0fu) | ((vw[1] & 0x0f0f0f0fu) << 4);
+        const uint32_t y01 = ((vw[0] >> 4) & 0x0f0f0f0fu) | (vw[1] & 0xf0f0f0f0u);
+        const uint32_t x23 = (vw[2] & 0x0f0f0f0fu) | ((vw[3] & 0x0f0f0f0fu) << 4);
+        const uint32_t y23 = ((vw[2] >> 4) & 0x0f0f0f0fu) | (vw[3] & 0xf0f0f0f0u);
+        // n-tile 2B + x, column n <-> dim 64w + 8n + 2B + x
+#define NVQSA_MTP_PV_BYTE(B)                                                                     \
+  {                                                                                              \
+    const uint32_t bx0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x01), s01);                         \
+    const uint32_t bx1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x23), s23);                         \
+    const uint32_t by0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(y01), s01);                         \
+    const uint32_t by1 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(y23), s23);                         \
+    _Pragma("unroll") for (int t = 0; t < kMtpMTiles; ++t) {                                     \
+      mma_f16(oacc[t][2 * (B)], pa[t][0], pa[t][1], pa[t][2], pa[t][3], bx0, bx1);               \
+      mma_f16(oacc[t][2 * (B) + 1], pa[t][0], pa[t][1], pa[t][2], pa[t][3], by0, by1);           \
+    }                                                                                            \
+  }
+        NVQSA_MTP_PV_BYTE(0)
+        NVQSA_MTP_PV_BYTE(1)
+        NVQSA_MTP_PV_BYTE(2)
+        NVQSA_MTP_PV_BYTE(3)
+#undef NVQSA_MTP_PV_BYTE
+      }
+    }
+    if (aborted && warp == 0) {
+      // let copies still in flight land (bounded) before the ring is reused or released
+      for (int k2 = k + 1; k2 < ntiles && k2 < k + kMtpStages; ++k2)
+        mbar_wait(smem_u32(&sm.full_bar[(tiles_done + k2) % kMtpStages]),
+                  (uint32_t)(((tiles_done + k2) / kMtpStages) & 1), kDrainSpinLimit);
+    }
+    tiles_done += ntiles;
+
+    // ---------------- per-head (m, l) of the active rows ----------------
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
+    l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
+    l_r8 += __shfl_xor_sync(0xffffffffu, l_r8, 1);
+    l_r8 += __shfl_xor_sync(0xffffffffu, l_r8, 2);
+    if (srow && c == 0) {
+      if (r < G) { sm.m_s[warp * G + r] = m_r; sm.l_s[warp * G + r] = l_r; }
+      if (r + 8 < G) { sm.m_s[warp * G + r + 8] = m_r8; sm.l_s[warp * G + r + 8] = l_r8; }
+    }
+    __syncthreads();  // (m, l) visible; no copy in flight, the ring is free
+    aborted = sm.abort != 0;
+
+    // bf16 output of packed head `head` (< act * G), dims d0 and d1
+    auto out_ptr = [&](int head) {
+      const int hrow = head / G, j = head - hrow * G;
+      return p.out + (prow + hrow) * p.o_stride_row + (int64_t)(kvh * G + j) * p.o_stride_head;
+    };
+    if (p.cluster > 1) {
+      // Every rank publishes its (O, m, l); then every rank merges one slice of the O fragments of all ranks
+      // (fragment f = 8t + n-tile of each warp, slice [24 rank / cluster, 24 (rank + 1) / cluster)) over
+      // distributed shared memory and stores it, with per-head weights 2^(m_rank - M) / sum computed once.
+      float4* pub = reinterpret_cast<float4*>(&sm.rec[0][0]);  // [warp][24][32]
+      if (!aborted) {
+#pragma unroll
+        for (int t = 0; t < kMtpMTiles; ++t)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            pub[(warp * 24 + t * 8 + j) * 32 + lane] = make_float4(oacc[t][j][0], oacc[t][j][1], oacc[t][j][2], oacc[t][j][3]);
+      }
+      cluster_sync();
+      const int rank = split % p.cluster;
+      float* wts = reinterpret_cast<float*>(&sm.ph[0][0][0]);  // [cluster][48] merge weights (P space is free)
+      if (tid == 0) {
+        int bad = 0;
+        for (int rk = 0; rk < p.cluster; ++rk) bad |= cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk));
+        sm.total = bad;
+      }
+      if (tid < kMtpHeads && tid < act * G) {
+        float mr[16], M = kMaskedScore;
+        for (int rk = 0; rk < p.cluster; ++rk) {
+          mr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.m_s[tid]), (uint32_t)rk)));
+          M = fmaxf(M, mr[rk]);
+        }
+        float L = 0.0f;
+        for (int rk = 0; rk < p.cluster; ++rk) {
+          mr[rk] = ex2(mr[rk] - M);
+          L += mr[rk] * __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.l_s[tid]), (uint32_t)rk)));
+        }
+        // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
+        const float inv = L > 0.0f ? p.inv_value_scale / fmaxf(L, 1.0e-20f) : 0.0f;
+        for (int rk = 0; rk < p.cluster; ++rk) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
+      }
+      __syncthreads();
+      if (!sm.total) {
+        const int f_lo = rank * 24 / p.cluster, f_hi = (rank + 1) * 24 / p.cluster;
+        for (int f = f_lo; f < f_hi; ++f) {
+          const int t = f >> 3, jn = f & 7;
+          const int h0 = 16 * t + r, h1 = h0 + 8;
+          const bool l0 = h0 < act * G, l1 = h1 < act * G;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          const uint32_t off = (uint32_t)((warp * 24 + f) * 32 + lane) * 16u;
+          for (int rk = 0; rk < p.cluster; ++rk) {
+            const float4 v = cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off);
+            const float w0 = l0 ? wts[rk * kMtpHeads + h0] : 0.0f, w1 = l1 ? wts[rk * kMtpHeads + h1] : 0.0f;
+            acc.x += w0 * v.x; acc.y += w0 * v.y; acc.z += w1 * v.z; acc.w += w1 * v.w;
+          }
+          // n-tile jn, columns 2c and 2c+1: dims 64w + 16c + jn and 64w + 16c + 8 + jn
+          const int d = 64 * warp + 16 * c + jn;
+          if (l0) {
+            __nv_bfloat16* op = out_ptr(h0);
+            op[d] = __float2bfloat16_rn(acc.x);
+            op[d + 8] = __float2bfloat16_rn(acc.y);
+          }
+          if (l1) {
+            __nv_bfloat16* op = out_ptr(h1);
+            op[d] = __float2bfloat16_rn(acc.z);
+            op[d + 8] = __float2bfloat16_rn(acc.w);
+          }
+        }
+      }
+      cluster_sync();  // every rank keeps its shared memory until all have read it
+    } else if (!aborted) {
+      // one CTA per group: normalise and store every fragment from registers
+#pragma unroll
+      for (int t = 0; t < kMtpMTiles; ++t) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int head = 16 * t + r + 8 * hh;
+          if (head >= act * G) continue;
+          const float l = sm.l_s[head];
+          // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
+          const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
+          // dims 64w + 16c + i (n = 2c, n-tile i) and 64w + 16c + 8 + i (n = 2c + 1)
+          uint32_t wv[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 lo2 = __floats2bfloat162_rn(oacc[t][2 * i][2 * hh] * inv, oacc[t][2 * i + 1][2 * hh] * inv);
+            __nv_bfloat162 hi2 =
+                __floats2bfloat162_rn(oacc[t][2 * i][2 * hh + 1] * inv, oacc[t][2 * i + 1][2 * hh + 1] * inv);
+            wv[i] = *reinterpret_cast<uint32_t*>(&lo2);
+            wv[4 + i] = *reinterpret_cast<uint32_t*>(&hi2);
+          }
+          __nv_bfloat16* op = out_ptr(head) + 64 * warp + 16 * c;
+          if (p.vec_o) {
+            reinterpret_cast<uint4*>(op)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            reinterpret_cast<uint4*>(op)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+          } else {
+            unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              os[2 * i] = (unsigned short)(wv[i] & 0xffffu);
+              os[2 * i + 1] = (unsigned short)(wv[i] >> 16);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();  // the next pass rewrites shared memory
+  }
+}

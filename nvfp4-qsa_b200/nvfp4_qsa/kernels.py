@@ -183,6 +183,7 @@ def qsa_sparse_paged_attention_nvfp4(
     block_table,
     token_to_request,
     output,
+    rows_per_group=1,
 ):
     """Sparse paged GQA decode over an NVFP4 cache; writes ``output`` in place.
 
@@ -192,6 +193,12 @@ def qsa_sparse_paged_attention_nvfp4(
     page or physical block is out of range; rows without a valid selection
     become zeros.  Split-KV scratch comes from the caching allocator on the
     current stream.
+
+    ``rows_per_group`` (keyword, default 1: the reference behaviour) is a hint
+    for multi-token-prediction batches: consecutive rows in groups of this
+    size (2..4) that share their request and selections are served by one
+    gather per record (verified on the device; groups that do not share are
+    processed row by row, with the same result).
     """
     _check_read(query, key_data, key_scale, value_data, value_scale, logical_indices, block_table,
                 token_to_request)
@@ -209,7 +216,7 @@ def qsa_sparse_paged_attention_nvfp4(
     with _device_ctx(device):
         ws_bytes = _workspace_bytes(torch.cuda.current_device(), rows, query_heads, kv_heads, head_dim, topk)
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
-        status = lib.nvqsa_sparse_attention(
+        common = (
             query.data_ptr(), query.stride(0), query.stride(1),
             *_cache_args(key_data, key_scale, value_data, value_scale),
             float(key_global_scale), float(value_global_scale),
@@ -217,8 +224,12 @@ def qsa_sparse_paged_attention_nvfp4(
             block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
             token_to_request.data_ptr(),
             output.data_ptr(), output.stride(0), output.stride(1),
-            rows, query_heads, head_dim,
-            workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+            rows, query_heads, head_dim)
+        tail = (workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+        if rows_per_group == 1:
+            status = lib.nvqsa_sparse_attention(*common, *tail)
+        else:
+            status = lib.nvqsa_sparse_attention_grouped(*common, int(rows_per_group), *tail)
     _native.check(status, "qsa_sparse_paged_attention_nvfp4")
 
 
