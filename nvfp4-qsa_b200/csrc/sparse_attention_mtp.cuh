@@ -95,6 +95,39 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
     sm.abort = 0;
   }
 
+  // Selections of row `prow` for this CTA's chunks -> record rows (gather4), -1 when masked
+  // (kernels.py:236-257).  Pass 0 always follows the group's first row, shared or not, so its
+  // selections and block-table entries are loaded before the sharing check below.
+  const bool huge_page = p.page_size > 0x7fffffffLL;
+  int32_t rowid[kCompactIters];
+  auto load_selections = [&](int64_t prow) {
+    const int32_t req = __ldg(p.token_to_request + prow);
+    const int32_t* idx_row = p.indices + prow * p.topk;
+    int32_t iv[kCompactIters];
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      const int lc = it * kWarps + warp;
+      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
+      iv[it] = (lc < my_chunks && pos < p.topk) ? __ldg(idx_row + pos) : -1;
+    }
+    const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
+    const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
+#pragma unroll
+    for (int it = 0; it < kCompactIters; ++it) {
+      rowid[it] = -1;
+      const int32_t idx = iv[it];
+      if (req_ok && idx >= 0) {
+        const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
+        if ((int64_t)lpage < p.table_width) {
+          const int32_t phys = __ldg(bt_row + lpage);
+          const int32_t off = huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size);
+          if (phys >= 0 && (int64_t)phys < p.num_blocks) rowid[it] = (phys * p.kv_heads + kvh) * (int32_t)p.page_size + off;
+        }
+      }
+    }
+  };
+  load_selections(row_lo);
+
   // ---------------- do the group's rows share request and selections (this CTA's chunks)? ----------------
   bool same = true;
   {
@@ -120,13 +153,9 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
     // every rank of the cluster takes the same passes
     if (tid == 0) sm.shared_ok = same ? 1 : 0;
     cluster_sync();
-    if (tid == 0) {
-      int all = 1;
-      for (int rk = 0; rk < p.cluster; ++rk) all &= cluster_ld_s32(cluster_map(smem_u32(&sm.shared_ok), (uint32_t)rk));
-      sm.total = all;
-    }
+    const int mine = tid < p.cluster ? cluster_ld_s32(cluster_map(smem_u32(&sm.shared_ok), (uint32_t)tid)) : 1;
+    same = __syncthreads_and(mine) != 0;
     cluster_sync();  // no rank rewrites shared_ok before every rank has read it
-    same = sm.total != 0;
   }
   const int passes = same ? 1 : nrows;
   int tiles_done = 0;  // tiles consumed in earlier passes: ring stage and phase carry over
@@ -136,16 +165,8 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
     const int act = same ? nrows : 1;                    // active S warps (rows) of this pass
     bool aborted = sm.abort != 0;
 
-    // ---------------- prologue: selections, block table, Q of the active rows ----------------
-    const int32_t req = __ldg(p.token_to_request + prow);
-    const int32_t* idx_row = p.indices + prow * p.topk;
-    int32_t iv[kCompactIters];
-#pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
-      const int lc = it * kWarps + warp;
-      const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
-      iv[it] = (lc < my_chunks && pos < p.topk) ? __ldg(idx_row + pos) : -1;
-    }
+    // ---------------- prologue: selections (pass 0: loaded above), Q of the active rows ----------------
+    if (pass > 0) load_selections(prow);  // a group that does not share: row prow alone, on warp 0
     // warp w loads row w's heads: lane L holds dims [8L, 8L + 8) of each head
     uint32_t qw[16][4];
 #pragma unroll
@@ -164,24 +185,6 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
         }
       }
     }
-    const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
-    const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
-    const bool huge_page = p.page_size > 0x7fffffffLL;
-    int32_t rowid[kCompactIters];
-#pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
-      rowid[it] = -1;
-      const int32_t idx = iv[it];
-      if (req_ok && idx >= 0) {
-        const uint32_t lpage = huge_page ? 0u : (uint32_t)idx / (uint32_t)p.page_size;
-        if ((int64_t)lpage < p.table_width) {
-          const int32_t phys = __ldg(bt_row + lpage);
-          const int32_t off = huge_page ? idx : (int)((uint32_t)idx - lpage * (uint32_t)p.page_size);
-          if (phys >= 0 && (int64_t)phys < p.num_blocks) rowid[it] = (phys * p.kv_heads + kvh) * (int32_t)p.page_size + off;
-        }
-      }
-    }
-
     // Q: per-head power-of-two pre-scale (exact) into f16 A-fragments of the row's m16 tile (natural
     // dim order: k-step s covers dims [16s, 16s + 16)); heads >= G stay zero.
     if (warp < kMtpRows) {
@@ -495,28 +498,33 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
       cluster_sync();
       const int rank = split % p.cluster;
       float* wts = reinterpret_cast<float*>(&sm.ph[0][0][0]);  // [cluster][48] merge weights (P space is free)
-      if (tid == 0) {
-        int bad = 0;
-        for (int rk = 0; rk < p.cluster; ++rk) bad |= cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk));
-        sm.total = bad;
-      }
+      const int bad_rank = tid < p.cluster ? cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)tid)) : 0;
       if (tid < kMtpHeads && tid < act * G) {
-        float mr[16], M = kMaskedScore;
-        for (int rk = 0; rk < p.cluster; ++rk) {
-          mr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.m_s[tid]), (uint32_t)rk)));
-          M = fmaxf(M, mr[rk]);
+        float mr[kMtpMaxCluster], lr[kMtpMaxCluster], M = kMaskedScore;
+#pragma unroll
+        for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
+          mr[rk] = kMaskedScore;
+          lr[rk] = 0.0f;
+          if (rk < p.cluster) {
+            mr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.m_s[tid]), (uint32_t)rk)));
+            lr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.l_s[tid]), (uint32_t)rk)));
+          }
         }
+#pragma unroll
+        for (int rk = 0; rk < kMtpMaxCluster; ++rk) M = fmaxf(M, mr[rk]);
         float L = 0.0f;
-        for (int rk = 0; rk < p.cluster; ++rk) {
+#pragma unroll
+        for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
           mr[rk] = ex2(mr[rk] - M);
-          L += mr[rk] * __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.l_s[tid]), (uint32_t)rk)));
+          L += mr[rk] * lr[rk];
         }
         // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
         const float inv = L > 0.0f ? p.inv_value_scale / fmaxf(L, 1.0e-20f) : 0.0f;
-        for (int rk = 0; rk < p.cluster; ++rk) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
+#pragma unroll
+        for (int rk = 0; rk < kMtpMaxCluster; ++rk)
+          if (rk < p.cluster) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
       }
-      __syncthreads();
-      if (!sm.total) {
+      if (!__syncthreads_or(bad_rank)) {  // weights in place; no rank gave up
         const int f_lo = rank * 24 / p.cluster, f_hi = (rank + 1) * 24 / p.cluster;
         for (int f = f_lo; f < f_hi; ++f) {
           const int t = f >> 3, jn = f & 7;
@@ -524,10 +532,16 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
           const bool l0 = h0 < act * G, l1 = h1 < act * G;
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           const uint32_t off = (uint32_t)((warp * 24 + f) * 32 + lane) * 16u;
-          for (int rk = 0; rk < p.cluster; ++rk) {
-            const float4 v = cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off);
+          float4 v[kMtpMaxCluster];
+#pragma unroll
+          for (int rk = 0; rk < kMtpMaxCluster; ++rk)  // every rank's fragment in flight at once
+            v[rk] = rk < p.cluster ? cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
+            if (rk >= p.cluster) break;
             const float w0 = l0 ? wts[rk * kMtpHeads + h0] : 0.0f, w1 = l1 ? wts[rk * kMtpHeads + h1] : 0.0f;
-            acc.x += w0 * v.x; acc.y += w0 * v.y; acc.z += w1 * v.z; acc.w += w1 * v.w;
+            acc.x += w0 * v[rk].x; acc.y += w0 * v[rk].y; acc.z += w1 * v[rk].z; acc.w += w1 * v[rk].w;
           }
           // n-tile jn, columns 2c and 2c+1: dims 64w + 16c + jn and 64w + 16c + 8 + jn
           const int d = 64 * warp + 16 * c + jn;
