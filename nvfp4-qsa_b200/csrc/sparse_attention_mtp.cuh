@@ -29,20 +29,21 @@
 // one slice of the output fragments of all ranks over distributed shared
 // memory and stores it.
 
-constexpr int kMtpStages = 3;     // ring stages of 16 records
+constexpr int kMtpStages = 4;     // ring stages of 16 records (two tiles in use, two being filled)
+constexpr int kMtpStep = 2 * kTile;  // tokens per step: two tiles per pair of CTA barriers
 constexpr int kMtpHeads = 48;     // packed query heads of a group (rows x group size)
 constexpr int kMtpMTiles = 3;     // m16 tiles of packed heads
 constexpr int kKhStride = 264;    // halfs per token row of the dequantised K tile (256 + 8: ldmatrix conflict-free)
-constexpr int kPhStride = 24;     // halfs per head row of the P tile (16 + 8: ldmatrix conflict-free)
+constexpr int kPhStride = 40;     // halfs per head row of the P tile (32 + 8: ldmatrix conflict-free)
 constexpr int kMtpRows = 4;       // rows per group (one S warp each)
 constexpr int kMtpMaxCluster = 8;   // splits of a group: one portable cluster
 
 struct __align__(128) SmemMtp {
   // rec, kh and qf are contiguous: after the last tile they hold the cluster merge's published O.
   uint8_t rec[kMtpStages][kStageBytes];   // gather ring, CTA-wide
-  __half kh[2][kTile][kKhStride];         // dequantised K of a tile, double-buffered
+  __half kh[2][kMtpStep][kKhStride];      // dequantised K of a step, double-buffered
   uint4 qf[kMtpRows][16][33];             // Q A-fragments of each row: [row][k-step][lane] (+1: conflict-free stores)
-  __half ph[2][kMtpHeads][kPhStride];     // P of a tile (packed heads x tokens), double-buffered
+  __half ph[2][kMtpHeads][kPhStride];     // P of a step (packed heads x tokens), double-buffered
   int32_t sel[kMaxRange];                 // record rows (gather4) of the valid shared selections
   float alpha[2][kMtpHeads];              // rescale factor of each packed head (read only when its row rescaled)
   int resc[2][kMtpRows];                  // row rescaled its running max in this tile
@@ -65,7 +66,7 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d
                : "r"(addr));
 }
 
-__global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SmemMtp& sm = *reinterpret_cast<SmemMtp*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
 
@@ -270,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
       }
     };
     if (warp == 0 && !aborted) {
-      for (int k = 0; k < kMtpStages - 1 && k < ntiles; ++k) issue_tile(k);
+      for (int k = 0; k < 2 && k < ntiles; ++k) issue_tile(k);
     }
 
     float oacc[kMtpMTiles][8][4];
@@ -288,16 +289,25 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
     const uint32_t ph_lane = (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kPhStride + (lane >> 4) * 8) * 2);
     const int vtok[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 
-    int k = 0;
-    for (; k < ntiles && !aborted; ++k) {
-      const int st = (tiles_done + k) % kMtpStages;
-      const bool ok = mbar_wait(smem_u32(&sm.full_bar[st]), (uint32_t)(((tiles_done + k) / kMtpStages) & 1));
-      const uint8_t* stage = sm.rec[st];
-      const int buf = k & 1;
-      // ---- K: warp w dequantises dims [64w, 64w + 64); lane -> token lane/2, dims 64w + 32 (lane % 2) + [0, 32) ----
-      {
+    // Steps of two tiles (32 tokens): tile k sits in ring stage (tiles_done + k) % kMtpStages.  After the
+    // step's first barrier every warp is past the previous step's P V, so warp 0 refills those two stages
+    // with the next step's tiles.
+    const int nsteps = (ntiles + 1) / 2;
+    int i = 0;
+    for (; i < nsteps && !aborted; ++i) {
+      const int k0 = 2 * i;
+      const bool two = k0 + 1 < ntiles;
+      const int buf = i & 1;
+      bool ok = true;
+      // ---- K: warp w dequantises dims [64w, 64w + 64); lane -> token lane/2 of each tile, dims 64w + 32 (lane % 2) + [0, 32) ----
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (u == 1 && !two) break;
+        const int kk = k0 + u;
+        const int st = (tiles_done + kk) % kMtpStages;
+        ok &= mbar_wait(smem_u32(&sm.full_bar[st]), (uint32_t)(((tiles_done + kk) / kMtpStages) & 1));
         const int t = lane >> 1, h = lane & 1;
-        const uint8_t* rec = stage + slot_off(t);
+        const uint8_t* rec = sm.rec[st] + slot_off(t);
         const uint4 kb = *reinterpret_cast<const uint4*>(rec + 32 * warp + 16 * h);
         const uint32_t sc = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 4 * warp + 2 * h));
         const uint32_t s0 = dup_lo(sc), s1 = dup_hi(sc);
@@ -311,42 +321,52 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
           o[4 * q + 2] = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(wd[q]), sg);
           o[4 * q + 3] = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(wd[q]), sg);
         }
-        uint4* dst = reinterpret_cast<uint4*>(&sm.kh[buf][t][64 * warp + 32 * h]);
+        uint4* dst = reinterpret_cast<uint4*>(&sm.kh[buf][kTile * u + t][64 * warp + 32 * h]);
 #pragma unroll
         for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
       }
-      if (!__syncthreads_and(ok)) {  // (A) K tile complete; every warp is past the previous tile's P V
+      if (!__syncthreads_and(ok)) {  // (A) K of the step complete; every warp is past the previous step's P V
         if (tid == 0) sm.abort = 1;
         aborted = true;
         break;
       }
-      if (warp == 0 && k + kMtpStages - 1 < ntiles) issue_tile(k + kMtpStages - 1);  // into tile k-1's stage
+      if (warp == 0) {
+        if (k0 + 2 < ntiles) issue_tile(k0 + 2);  // into the stages of tiles k0 - 2 and k0 - 1
+        if (k0 + 3 < ntiles) issue_tile(k0 + 3);
+      }
 
-      // ---- S = Q K^T for row `warp`, online softmax, P into the packed tile ----
+      // ---- S = Q K^T for row `warp` over the step's 32 tokens, online softmax, P into the packed tile ----
+      // (a missing second tile leaves stale K rows: their scores are masked below)
       if (srow) {
-        float sacc[2][4];
+        float sacc[4][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+        for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
         const uint32_t kaddr = smem_u32(&sm.kh[buf][0][0]) + kh_lane;
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
-          uint32_t b0, b1, b2, b3;
+          uint32_t b0, b1, b2, b3, b4, b5, b6, b7;
           ldsm_x4(kaddr + 32u * s, b0, b1, b2, b3);
+          ldsm_x4(kaddr + (uint32_t)(kTile * kKhStride * 2) + 32u * s, b4, b5, b6, b7);
           const uint4 qa = sm.qf[warp][s][lane];
           mma_f16(sacc[0], qa.x, qa.y, qa.z, qa.w, b0, b1);
           mma_f16(sacc[1], qa.x, qa.y, qa.z, qa.w, b2, b3);
+          mma_f16(sacc[2], qa.x, qa.y, qa.z, qa.w, b4, b5);
+          mma_f16(sacc[3], qa.x, qa.y, qa.z, qa.w, b6, b7);
         }
-        const int tok_base = k * kTile;
-        if (tok_base + kTile > n) {
+        const int tok_base = i * kMtpStep;
+        const bool tail = tok_base + kMtpStep > n;
+        if (tail) {
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
+          for (int nt = 0; nt < 4; ++nt) {
             const int t0 = tok_base + 8 * nt + 2 * c;
             if (t0 >= n) { sacc[nt][0] = -1.0e30f; sacc[nt][2] = -1.0e30f; }
             if (t0 + 1 >= n) { sacc[nt][1] = -1.0e30f; sacc[nt][3] = -1.0e30f; }
           }
         }
-        float mx_r = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
-        float mx_r8 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
+        float mx_r = fmaxf(fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1])),
+                           fmaxf(fmaxf(sacc[2][0], sacc[2][1]), fmaxf(sacc[3][0], sacc[3][1])));
+        float mx_r8 = fmaxf(fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3])),
+                            fmaxf(fmaxf(sacc[2][2], sacc[2][3]), fmaxf(sacc[3][2], sacc[3][3])));
         mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 1));
         mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 2));
         mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 1));
@@ -369,26 +389,26 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
           }
         }
         if (lane == 0) sm.resc[buf][warp] = up ? 1 : 0;
-        float pv[2][4];
+        float pv[4][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+        for (int nt = 0; nt < 4; ++nt) {
           pv[nt][0] = ex2(fmaf(sacc[nt][0], smul_r, -m_r));
           pv[nt][1] = ex2(fmaf(sacc[nt][1], smul_r, -m_r));
           pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
           pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
         }
-        if (tok_base + kTile > n) {  // masked scores must not count even while the running max is still -1e20
+        if (tail) {  // masked scores must not count even while the running max is still -1e20
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
+          for (int nt = 0; nt < 4; ++nt) {
             const int t0 = tok_base + 8 * nt + 2 * c;
             if (t0 >= n) { pv[nt][0] = 0.0f; pv[nt][2] = 0.0f; }
             if (t0 + 1 >= n) { pv[nt][1] = 0.0f; pv[nt][3] = 0.0f; }
           }
         }
-        l_r += (pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1]);
-        l_r8 += (pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3]);
+        l_r += ((pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1])) + ((pv[2][0] + pv[2][1]) + (pv[3][0] + pv[3][1]));
+        l_r8 += ((pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3])) + ((pv[2][2] + pv[2][3]) + (pv[3][2] + pv[3][3]));
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
+        for (int nt = 0; nt < 4; ++nt) {
           if (r < G)
             *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r][8 * nt + 2 * c]) = pack_half2(pv[nt][0], pv[nt][1]);
           if (r + 8 < G)
@@ -400,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
       }
       __syncthreads();  // (B) P and the rescale factors of every row are in place
 
-      // ---- O += P V over dims [64w, 64w + 64) of every packed head ----
+      // ---- O += P V over dims [64w, 64w + 64) of every packed head, one k-step per tile ----
       {
         const int any = sm.resc[buf][0] | sm.resc[buf][1] | sm.resc[buf][2] | sm.resc[buf][3];
         if (any) {
@@ -419,27 +439,31 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
             }
           }
         }
-        uint32_t pa[kMtpMTiles][4];
-        const uint32_t paddr = smem_u32(&sm.ph[buf][0][0]) + ph_lane;
 #pragma unroll
-        for (int t = 0; t < kMtpMTiles; ++t)
-          ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
-        // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9}, dims 64w + 8r + [0, 8)
-        uint32_t vw[4], vsb[4];
+        for (int u = 0; u < 2; ++u) {
+          if (u == 1 && !two) break;  // no stale V enters O
+          const uint8_t* stage = sm.rec[(tiles_done + k0 + u) % kMtpStages];
+          uint32_t pa[kMtpMTiles][4];
+          const uint32_t paddr = smem_u32(&sm.ph[buf][0][0]) + ph_lane + (uint32_t)(kTile * 2 * u);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint8_t* rec = stage + slot_off(vtok[q]);
-          vw[q] = *reinterpret_cast<const uint32_t*>(rec + 144 + 32 * warp + 4 * r);
-          vsb[q] = rec[272 + 4 * warp + (r >> 1)];
-        }
-        const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
-        const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
-        // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
-        const uint32_t x01 = (vw[0] & 0x0f0f0f0fu) | ((vw[1] & 0x0f0f0f0fu) << 4);
-        const uint32_t y01 = ((vw[0] >> 4) & 0x0f0f0f0fu) | (vw[1] & 0xf0f0f0f0u);
-        const uint32_t x23 = (vw[2] & 0x0f0f0f0fu) | ((vw[3] & 0x0f0f0f0fu) << 4);
-        const uint32_t y23 = ((vw[2] >> 4) & 0x0f0f0f0fu) | (vw[3] & 0xf0f0f0f0u);
-        // n-tile 2B + x, column n <-> dim 64w + 8n + 2B + x
+          for (int t = 0; t < kMtpMTiles; ++t)
+            ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
+          // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9} of the tile, dims 64w + 8r + [0, 8)
+          uint32_t vw[4], vsb[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint8_t* rec = stage + slot_off(vtok[q]);
+            vw[q] = *reinterpret_cast<const uint32_t*>(rec + 144 + 32 * warp + 4 * r);
+            vsb[q] = rec[272 + 4 * warp + (r >> 1)];
+          }
+          const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
+          const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
+          // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
+          const uint32_t x01 = (vw[0] & 0x0f0f0f0fu) | ((vw[1] & 0x0f0f0f0fu) << 4);
+          const uint32_t y01 = ((vw[0] >> 4) & 0x0f0f0f0fu) | (vw[1] & 0xf0f0f0f0u);
+          const uint32_t x23 = (vw[2] & 0x0f0f0f0fu) | ((vw[3] & 0x0f0f0f0fu) << 4);
+          const uint32_t y23 = ((vw[2] >> 4) & 0x0f0f0f0fu) | (vw[3] & 0xf0f0f0f0u);
+          // n-tile 2B + x, column n <-> dim 64w + 8n + 2B + x
 #define NVQSA_MTP_PV_BYTE(B)                                                                     \
   {                                                                                              \
     const uint32_t bx0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x01), s01);                         \
@@ -451,16 +475,17 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_mtp_kernel(const
       mma_f16(oacc[t][2 * (B) + 1], pa[t][0], pa[t][1], pa[t][2], pa[t][3], by0, by1);           \
     }                                                                                            \
   }
-        NVQSA_MTP_PV_BYTE(0)
-        NVQSA_MTP_PV_BYTE(1)
-        NVQSA_MTP_PV_BYTE(2)
-        NVQSA_MTP_PV_BYTE(3)
+          NVQSA_MTP_PV_BYTE(0)
+          NVQSA_MTP_PV_BYTE(1)
+          NVQSA_MTP_PV_BYTE(2)
+          NVQSA_MTP_PV_BYTE(3)
 #undef NVQSA_MTP_PV_BYTE
+        }
       }
     }
     if (aborted && warp == 0) {
       // let copies still in flight land (bounded) before the ring is reused or released
-      for (int k2 = k + 1; k2 < ntiles && k2 < k + kMtpStages; ++k2)
+      for (int k2 = 2 * i; k2 < ntiles && k2 < 2 * i + 2; ++k2)
         mbar_wait(smem_u32(&sm.full_bar[(tiles_done + k2) % kMtpStages]),
                   (uint32_t)(((tiles_done + k2) / kMtpStages) & 1), kDrainSpinLimit);
     }
