@@ -342,7 +342,8 @@ def bench_mtp(args, device, steps):
         "roofline": {"bound": "hbm", "achieved": algo / g4 / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": algo / g4 / 1e9 / peak, "peak_kind": kind,
                      "kernel": "sparse_attention_mtp_kernel (one layer, splits merged in a cluster)",
-                     "algorithmic_bytes_per_launch": algo},
+                     "algorithmic_bytes_per_launch": algo,
+                     "traffic": profile_traffic("sparse_attention_mtp.md")},
         "gpu_launches": 2 * (max(20, steps) + 5) * layers,
     }
 
