@@ -23,7 +23,60 @@ import torch
 
 from . import kernels
 
-__all__ = ["split_nvfp4_kv_cache", "QSANVFP4AttentionHooks", "write_nvfp4_kv"]
+__all__ = ["split_nvfp4_kv_cache", "QSANVFP4AttentionHooks", "write_nvfp4_kv", "is_qsa_nvfp4_dtype",
+           "nvfp4_storage_dim", "nvfp4_kv_cache_spec_fields", "customize_nvfp4_spec", "nvfp4_page_bytes"]
+
+# ---------------------------------------------------------------------------
+# Cache planner accounting: the NVFP4 parts of the backend's spec methods
+# (integration/snapshot/qsa.py:66-68, :187-204 and :556-566), as plain host
+# arithmetic so that a serving stack sizes its pages for the 288-byte record.
+# ---------------------------------------------------------------------------
+
+
+def is_qsa_nvfp4_dtype(dtype) -> bool:
+    """True for the QSA-owned packed E2M1 + group-scale cache dtypes (snapshot/qsa.py:66-68)."""
+    return isinstance(dtype, str) and dtype in ("nvfp4", "nvfp4_4over6")
+
+
+def nvfp4_storage_dim(head_dim: int) -> int:
+    """Bytes of one packed K (or V) region per (token, kv head): head_dim/2 codes + head_dim/16 scales."""
+    if head_dim <= 0 or head_dim % 16:
+        raise ValueError(f"NVFP4 head_dim must be a positive multiple of 16, got {head_dim}")
+    return head_dim // 2 + head_dim // 16
+
+
+def nvfp4_kv_cache_spec_fields(block_size: int, num_kv_heads: int, head_dim: int) -> dict:
+    """Fields of the per-layer cache spec the backend reports for an NVFP4 cache (snapshot/qsa.py:556-566).
+
+    The physical width replaces the logical head size for both K and V and the
+    element type is uint8, so the planner allocates [blocks, kv_heads, block_size,
+    2 * storage_dim] bytes per layer (the layout ``split_nvfp4_kv_cache`` cuts).
+    The reference also passes vLLM's "auto" quant mode: QSA owns writer and reader.
+    """
+    storage_dim = nvfp4_storage_dim(head_dim)
+    return {"block_size": int(block_size), "num_kv_heads": int(num_kv_heads), "head_size": storage_dim,
+            "head_size_v": storage_dim, "dtype": torch.uint8}
+
+
+def customize_nvfp4_spec(spec, nvfp4_quant_mode):
+    """``customize_spec`` of the backend (snapshot/qsa.py:187-204) for any dataclass spec.
+
+    A spec whose ``kv_quant_mode`` is ``nvfp4_quant_mode`` still carries the
+    logical ``head_size``; the packed K + V bytes per head slot are advertised
+    through ``state_content_bytes`` (the spec multiplies by ``num_kv_heads``
+    itself).  Any other spec is returned unchanged, so applying it to the final
+    physical spec (quant mode "auto", 144-byte regions) is a no-op.
+    """
+    import dataclasses
+
+    if getattr(spec, "kv_quant_mode", None) != nvfp4_quant_mode:
+        return spec
+    return dataclasses.replace(spec, state_content_bytes=2 * nvfp4_storage_dim(spec.head_size))
+
+
+def nvfp4_page_bytes(block_size: int, num_kv_heads: int, head_dim: int) -> int:
+    """Bytes of one cache block of one layer: block_size x kv_heads records of 2 * storage_dim bytes."""
+    return int(block_size) * int(num_kv_heads) * 2 * nvfp4_storage_dim(head_dim)
 
 
 def split_nvfp4_kv_cache(kv_cache: torch.Tensor, head_size: int):

@@ -141,3 +141,47 @@ def test_write_hook_hands_the_writer_the_reference_arguments(recorded):
 def test_hooks_module_calls_through_kernels_namespace():
     # the hooks look the raw ops up on nvfp4_qsa.kernels at call time (monkeypatch-able, one code path)
     assert vllm_hooks.kernels is kernels
+
+
+# ---- cache planner accounting (snapshot/qsa.py:66-68, :187-204, :556-566) ----
+
+def test_nvfp4_dtype_names():
+    assert vllm_hooks.is_qsa_nvfp4_dtype("nvfp4") and vllm_hooks.is_qsa_nvfp4_dtype("nvfp4_4over6")
+    for other in ("fp8", "auto", "bfloat16", None, torch.uint8):
+        assert not vllm_hooks.is_qsa_nvfp4_dtype(other)
+
+
+def test_storage_dim_and_page_bytes_match_the_record():
+    assert vllm_hooks.nvfp4_storage_dim(256) == 144
+    assert vllm_hooks.nvfp4_storage_dim(128) == 72
+    with pytest.raises(ValueError):
+        vllm_hooks.nvfp4_storage_dim(100)
+    # one 3,136-token block of one layer, 2 kv heads: 3136 x 2 x 288 bytes
+    assert vllm_hooks.nvfp4_page_bytes(3136, 2, 256) == 3136 * 2 * 288
+    f = vllm_hooks.nvfp4_kv_cache_spec_fields(16, 2, 256)
+    assert f == {"block_size": 16, "num_kv_heads": 2, "head_size": 144, "head_size_v": 144, "dtype": torch.uint8}
+    # a cache allocated from those fields is what split_nvfp4_kv_cache cuts into the four regions
+    cache = torch.zeros(3, f["num_kv_heads"], f["block_size"], f["head_size"] + f["head_size_v"], dtype=f["dtype"])
+    kd, ks, vd, vs = split_nvfp4_kv_cache(cache, 256)
+    assert kd.shape[-1] == 128 and ks.shape[-1] == 16 and vd.shape[-1] == 128 and vs.shape[-1] == 16
+    assert cache.numel() == 3 * vllm_hooks.nvfp4_page_bytes(16, 2, 256)
+
+
+def test_customize_spec_advertises_packed_bytes_and_is_idempotent():
+    from dataclasses import dataclass
+
+    @dataclass(frozen=True)
+    class Spec:
+        block_size: int
+        num_kv_heads: int
+        head_size: int
+        kv_quant_mode: str
+        state_content_bytes: int = 0
+
+    logical = Spec(16, 2, 256, "nvfp4-mode")
+    out = vllm_hooks.customize_nvfp4_spec(logical, "nvfp4-mode")
+    assert out.state_content_bytes == 288 and out.head_size == 256 and logical.state_content_bytes == 0
+    physical = Spec(16, 2, 144, "auto")
+    assert vllm_hooks.customize_nvfp4_spec(physical, "nvfp4-mode") is physical
+    bf16 = Spec(16, 2, 256, "bf16-mode")
+    assert vllm_hooks.customize_nvfp4_spec(bf16, "nvfp4-mode") is bf16
