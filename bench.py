@@ -614,7 +614,8 @@ def main_ours(args):
 
     split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
-    mtp = bench_mtp(args, device, args.steps) if rank == 0 and not args.skip_mtp else None
+    # config 4 is a single-GPU side measurement: one GPU runs only
+    mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
     del graph
     result = None
     if rank == 0:
