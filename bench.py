@@ -55,6 +55,7 @@ def parse_args():
     ap.add_argument("--split-topk", type=int, default=8192, help="split-KV section: selected tokens per row")
     ap.add_argument("--skip-split", action="store_true", help="skip the split-KV section")
     ap.add_argument("--skip-mtp", action="store_true", help="skip the MTP (config 4) section")
+    ap.add_argument("--skip-fp8", action="store_true", help="skip the FP8 sibling-reader section")
     return ap.parse_args()
 
 
@@ -348,6 +349,73 @@ def bench_mtp(args, device, steps):
     }
 
 
+def bench_fp8(args, device, steps):
+    """FP8 sibling reader (src/qsa_fp8_harness.py:42-208) on the config-5a row shape.
+
+    96 rows x 2 KV heads x top-2,048 over float8_e4m3 K and V caches [blocks, page, 2, 256] (one per layer,
+    context 32,768 so that 12 layers fit beside the NVFP4 workload: 201 MB of selected rows per layer, more
+    than L2), 12 layers replayed from one CUDA graph per step.  Bytes: the selected K and V rows (512 B per
+    row and KV head), indices, q and out.
+    """
+    import torch
+    from nvfp4_qsa import kernels
+
+    seqs, ctx, page, layers, topk = args.seqs, 32768, args.page, args.layers, args.topk
+    width = (ctx + page - 1) // page
+    blocks = seqs * width
+    gen = torch.Generator(device=device).manual_seed(8)
+    L = []
+    for layer in range(layers):
+        kc = torch.empty(blocks, page, KV_HEADS, HEAD_DIM, dtype=torch.float8_e4m3fn, device=device)
+        vc = torch.empty_like(kc)
+        for b0 in range(0, blocks, 64):
+            b1 = min(blocks, b0 + 64)
+            kc[b0:b1] = torch.randn(b1 - b0, page, KV_HEADS, HEAD_DIM, device=device, generator=gen).to(kc.dtype)
+            vc[b0:b1] = torch.randn(b1 - b0, page, KV_HEADS, HEAD_DIM, device=device, generator=gen).to(vc.dtype)
+        table = torch.randperm(blocks, device=device, generator=gen).to(torch.int32).view(seqs, width).contiguous()
+        idx = torch.rand(seqs, ctx, device=device, generator=gen).topk(topk, dim=1).indices
+        idx = idx.sort(dim=1).values.to(torch.int32).contiguous()
+        q = torch.randn(seqs, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+        L.append(dict(kc=kc, vc=vc, table=table, idx=idx, q=q, out=torch.empty_like(q)))
+    t2r = torch.arange(seqs, device=device, dtype=torch.int32)
+    torch.cuda.synchronize(device)
+
+    def step():
+        for d in L:
+            kernels.qsa_sparse_paged_attention_fp8(d["q"], d["kc"], d["vc"], 1.0, 1.0, d["idx"], d["table"], t2r,
+                                                   d["out"])
+
+    step()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    reps = max(20, steps)
+    per_layer = timed(graph.replay, reps, device) / reps / layers
+    del graph
+    algo = seqs * KV_HEADS * topk * 2 * HEAD_DIM + seqs * topk * 4 + 2 * seqs * QUERY_HEADS * HEAD_DIM * 2
+    peak, kind = measured_peaks()
+    return {
+        "config": {"workload": f"FP8 sibling reader on the config-5a row shape: {seqs} rows x 2 KV heads x top-{topk} "
+                               f"of {ctx} tokens, float8_e4m3 K and V caches, page {page}, {layers} layers (one "
+                               "cache each) in one CUDA graph per step",
+                   "l2": f"inputs larger than L2: {seqs * KV_HEADS * topk * 512 / 1e6:.0f} MB of selected rows per layer"},
+        "us_per_layer": per_layer * 1e6,
+        "gb_per_s": algo / per_layer / 1e9,
+        "roofline": {"bound": "hbm", "achieved": algo / per_layer / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algo / per_layer / 1e9 / peak, "peak_kind": kind,
+                     "kernel": "sparse_attention_kernel<3> (one layer, FP8 rows)",
+                     "algorithmic_bytes_per_launch": algo},
+        "gpu_launches": (reps + 5) * layers,
+    }
+
+
 def bench_split_kv(args, device, world, rank, steps):
     """Config 5b: one 169,984-token sequence, 8,192 selected per row, 12 layers, split-KV over the ranks.
 
@@ -614,8 +682,9 @@ def main_ours(args):
 
     split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
-    # config 4 is a single-GPU side measurement: one GPU runs only
+    # config 4 and the FP8 sibling reader are single-GPU side measurements: one GPU runs only
     mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
+    fp8 = bench_fp8(args, device, args.steps) if world == 1 and not args.skip_fp8 else None
     del graph
     result = None
     if rank == 0:
@@ -652,6 +721,8 @@ def main_ours(args):
             result["split_kv"] = split
         if mtp is not None:
             result["mtp"] = mtp
+        if fp8 is not None:
+            result["fp8"] = fp8
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
         print(json.dumps(result), flush=True)

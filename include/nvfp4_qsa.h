@@ -174,6 +174,32 @@ int nvqsa_sparse_attention_grouped(
     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * FP8 sibling reader: the same sparse paged decode attention over float8_e4m3
+ * K and V caches (one byte per element) instead of NVFP4 records.  Replaces
+ * the reference's qsa_sparse_paged_attention_fp8 (src/qsa_fp8_harness.py:211-325,
+ * kernel :42-208; called from integration/snapshot/qsa.py:328-350).
+ *
+ * key_cache, value_cache : float8_e4m3fn [num_blocks, page_size, kv_heads,
+ *                          head_dim] with byte strides (block, token, head),
+ *                          innermost stride 1; 16-byte aligned rows and strides.
+ * k_scale multiplies the scores (with head_dim^-0.5), v_scale the normalised
+ * output, both per-tensor, finite and positive.  Masking, split-KV and the
+ * workspace as for nvqsa_sparse_attention (size from
+ * nvqsa_sparse_attention_workspace_size with the same rows, heads and topk).
+ */
+int nvqsa_sparse_attention_fp8(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_cache, int64_t kc_stride_block, int64_t kc_stride_token, int64_t kc_stride_head,
+    const void* value_cache, int64_t vc_stride_block, int64_t vc_stride_token, int64_t vc_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads, float k_scale, float v_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Partial (un-merged) variant for split-KV across devices: writes, for every
  * (row, query head), the softmax-normalized output of the selections this
  * device holds, already divided by value_global_scale, and its base-2

@@ -73,6 +73,11 @@ constexpr int kMaxChunks = kMaxRange / kChunk;   // chunks per CTA
 constexpr int kCompactIters = kMaxRange / kThreads;
 constexpr int kRecordBytes = 288;                // K data + K scales + V data + V scales
 constexpr int kStageBytes = kTile * kRecordBytes;
+// FP8 sibling reader (gather mode 3): float8_e4m3 K and V rows of 256 bytes from two caches, staged as
+// K | V | 16 bytes of skew per token (the skew keeps the per-lane K and V reads bank-conflict free).
+constexpr int kGatherFp8 = 3;
+constexpr int kFp8RecordBytes = 528;
+constexpr int kFp8Stages = 2;
 constexpr float kMaskedScore = -1.0e20f;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: P <= 2^8 between rescales
 constexpr uint32_t kSpinLimit = 1u << 22;        // bounded mbarrier waits
@@ -117,17 +122,20 @@ struct AttnParams {
   float* part_lse;               // [splits][rows][query_heads]
 };
 
-struct __align__(128) Smem {
-  uint8_t rec[kWarps][kWarpStages][kStageBytes];   // private gather ring of each warp
+template <int REC, int STAGES>
+struct __align__(128) SmemT {
+  uint8_t rec[kWarps][STAGES][kTile * REC];       // private gather ring of each warp
   uint4 qfrag[16][32];                             // Q A-fragments: [k-step][lane] -> {a0a1,a2a3,a4a5,a6a7}
   int2 sel[kMaxRange];                             // (physical block, token in page) of valid selections
-  unsigned long long full_bar[kWarps][kWarpStages];
+  unsigned long long full_bar[kWarps][STAGES];
   float smul[16];
   int cnt[kCompactIters][kWarps];
   int total;
   int abort;
   int last;
 };
+using Smem = SmemT<kRecordBytes, kWarpStages>;      // NVFP4 records
+using SmemFp8 = SmemT<kFp8RecordBytes, kFp8Stages>;  // FP8 K and V rows
 
 __device__ unsigned int g_error_flags;       // bit 0: an mbarrier wait ran out
 constexpr unsigned int kErrWaitTimeout = 1u;
@@ -509,9 +517,15 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
 // mode branches.
 template <int GMODE>
 __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __grid_constant__ AttnParams p) {
+  constexpr bool kFp8 = GMODE == kGatherFp8;
+  constexpr int kStages = kFp8 ? kFp8Stages : kWarpStages;
+  constexpr int kAh = kStages - 1;
+  using SM = SmemT<kFp8 ? kFp8RecordBytes : kRecordBytes, kStages>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   // Tensor copies need 128-byte aligned destinations: align the base explicitly.
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
+  SM& sm = *reinterpret_cast<SM*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
+  // Byte offset of token t inside a stage: the permuted NVFP4 rows, or plain FP8 slots.
+  auto soff = [](int t) { return kFp8 ? t * kFp8RecordBytes : slot_off(t); };
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -531,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
 
   if (lane == 0) {
 #pragma unroll
-    for (int b = 0; b < kWarpStages; ++b) mbar_init(smem_u32(&sm.full_bar[warp][b]), 1);
+    for (int b = 0; b < kStages; ++b) mbar_init(smem_u32(&sm.full_bar[warp][b]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (tid == 0) sm.abort = 0;
@@ -654,9 +668,9 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   // ---------------- per-warp gather pipeline: tiles warp, warp+4, ... ----------------
   const uint8_t* const reg0 = p.region[0];
   const int64_t sb0 = p.stride[0][0], st0 = p.stride[0][1], sh0 = p.stride[0][2];
-  auto issue_tile = [&](int k) {  // local tile k of this warp -> ring slot k % kWarpStages
+  auto issue_tile = [&](int k) {  // local tile k of this warp -> ring slot k % kStages
     const int tile = warp + kWarps * k;
-    const int slot = k % kWarpStages;
+    const int slot = k % kStages;
     const uint32_t bar = smem_u32(&sm.full_bar[warp][slot]);
     const int j0 = tile * kTile;
     const int count = min(kTile, n - j0);
@@ -681,13 +695,19 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       }
       return;
     }
-    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(count * kRecordBytes));
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(count * (kFp8 ? 2 * kHeadDim : kRecordBytes)));
     __syncwarp();
     if (lane < count) {
       const int2 e = sm.sel[j0 + lane];
-      const uint32_t dst = smem_u32(&sm.rec[warp][slot][slot_off(lane)]);
+      const uint32_t dst = smem_u32(&sm.rec[warp][slot][soff(lane)]);
       if constexpr (GMODE == 1) {
         bulk_g2s(dst, reg0 + (int64_t)e.x * sb0 + (int64_t)e.y * st0 + (int64_t)kvh * sh0, kRecordBytes, bar);
+      } else if constexpr (kFp8) {  // K row of cache region 0, V row of region 2
+        bulk_g2s(dst, reg0 + (int64_t)e.x * sb0 + (int64_t)e.y * st0 + (int64_t)kvh * sh0, kHeadDim, bar);
+        bulk_g2s(dst + kHeadDim,
+                 p.region[2] + (int64_t)e.x * p.stride[2][0] + (int64_t)e.y * p.stride[2][1] +
+                     (int64_t)kvh * p.stride[2][2],
+                 kHeadDim, bar);
       } else {
         const uint32_t dofs[4] = {0, 128, 144, 272};
         const uint32_t size[4] = {128, 16, 128, 16};
@@ -702,17 +722,17 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   };
   const int my_tiles = ntiles > warp ? (ntiles - warp + kWarps - 1) / kWarps : 0;
 #pragma unroll
-  for (int k = 0; k < kAhead; ++k)
+  for (int k = 0; k < kAh; ++k)
     if (k < my_tiles) issue_tile(k);
 
   // Per-lane constants: K bytes of token 8*nt + r (chunks c and 4+c), V tokens {2c, 2c+1, 2c+8, 2c+9}.
   int k_off[2], v_off[4];
 #pragma unroll
-  for (int nt = 0; nt < 2; ++nt) k_off[nt] = slot_off(8 * nt + r);
+  for (int nt = 0; nt < 2; ++nt) k_off[nt] = soff(8 * nt + r);
   {
     const int tt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) v_off[q] = slot_off(tt[q]);
+    for (int q = 0; q < 4; ++q) v_off[q] = soff(tt[q]);
   }
   const float smul_r = sm.smul[r];
   const float smul_r8 = sm.smul[r + 8];
@@ -729,6 +749,33 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
 
     // ---- S = Q K^T: 16 k-steps over all 256 dims, each on both n-tiles of 8 tokens ----
     float sacc[2][4];
+    if constexpr (kFp8) {
+      // FP8: one byte per dim; k-step s takes dims d..d+3 of the permuted order (d = 32c + 4s, +128 past
+      // s = 7), i.e. word s of the lane's 32 K bytes of its half, converted exactly to f16 pairs (the K
+      // scale is folded into the score scale).
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint4 kq[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint8_t* kr = stage + k_off[nt] + 128 * half + 32 * c;
+          kq[nt][0] = *reinterpret_cast<const uint4*>(kr);
+          kq[nt][1] = *reinterpret_cast<const uint4*>(kr + 16);
+        }
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          const uint4 qa = sm.qfrag[8 * half + s2][lane];
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const uint4 v = kq[nt][s2 >> 2];
+            const uint32_t word = (s2 & 3) == 0 ? v.x : (s2 & 3) == 1 ? v.y : (s2 & 3) == 2 ? v.z : v.w;
+            mma_f16(sacc[nt], qa.x, qa.y, qa.z, qa.w, cvt_e4m3x2_f16x2(word & 0xffffu), cvt_e4m3x2_f16x2(word >> 16));
+          }
+        }
+      }
+    } else {
     uint32_t sg[2][4];  // f16x2 group scales {lo, hi} x {chunk c, chunk 4+c}, duplicated per half
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -766,6 +813,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
         }
       }
     }
+    }  // NVFP4 S
 
     // ---- online softmax (base 2): p = 2^(s * smul - m) with one FFMA ----
     uint32_t pf[4];
@@ -828,6 +876,36 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     // ---- O += P V: 32 n-tiles of 8 dims; half h covers dims [128h, 128h+128) ----
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      if constexpr (kFp8) {
+        // FP8: lane (r, c) takes the 16 V bytes of dims 128h + 16r + [0, 16) of tokens {2c, 2c+1, 2c+8, 2c+9};
+        // n-tile 16h + 8kk + 2B + x, column r <-> dim 128h + 16r + 8kk + 2B + x as in the NVFP4 path, so the
+        // epilogue stores both alike.  A byte permute pairs the two tokens of each operand.
+        uint4 vq[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) vq[q] = *reinterpret_cast<const uint4*>(stage + v_off[q] + kHeadDim + 128 * h + 16 * r);
+        if constexpr (TAIL) {  // stale slots past the last valid token: zero V so that 0 * V stays 0
+          const int tt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (tok_base + tt[q] >= n) vq[q] = make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+          for (int B = 0; B < 4; ++B) {
+            const int wi = 2 * kk + (B >> 1), pb = 2 * (B & 1);
+            const uint32_t sel = (uint32_t)(pb | ((pb + 4) << 4) | ((pb + 1) << 8) | ((pb + 5) << 12));
+            auto word = [&](const uint4& v) { return wi == 0 ? v.x : wi == 1 ? v.y : wi == 2 ? v.z : v.w; };
+            const uint32_t u01 = __byte_perm(word(vq[0]), word(vq[1]), sel);
+            const uint32_t u23 = __byte_perm(word(vq[2]), word(vq[3]), sel);
+            const int nt = 16 * h + 8 * kk + 2 * B;
+            mma_f16(oacc[nt], pf[0], pf[1], pf[2], pf[3], cvt_e4m3x2_f16x2(u01 & 0xffffu),
+                    cvt_e4m3x2_f16x2(u23 & 0xffffu));
+            mma_f16(oacc[nt + 1], pf[0], pf[1], pf[2], pf[3], cvt_e4m3x2_f16x2(u01 >> 16), cvt_e4m3x2_f16x2(u23 >> 16));
+          }
+        }
+        continue;
+      }
       uint2 vw[4];
       uint32_t vsb[4];
 #pragma unroll
@@ -876,9 +954,9 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
 
   int k = 0;
   for (; k < my_tiles; ++k) {
-    if (k + kAhead < my_tiles) issue_tile(k + kAhead);  // into the slot tile k-1 used
-    const int slot = k % kWarpStages;
-    if (!mbar_wait(smem_u32(&sm.full_bar[warp][slot]), (uint32_t)((k / kWarpStages) & 1))) {
+    if (k + kAh < my_tiles) issue_tile(k + kAh);  // into the slot tile k-1 used
+    const int slot = k % kStages;
+    if (!mbar_wait(smem_u32(&sm.full_bar[warp][slot]), (uint32_t)((k / kStages) & 1))) {
       if (lane == 0) sm.abort = 1;
       break;
     }
@@ -900,8 +978,8 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   if (k < my_tiles) {
     // This warp gave up: let its copies still in flight land (bounded) before the
     // CTA's shared memory can be released.
-    for (int k2 = k + 1; k2 < my_tiles && k2 <= k + kAhead; ++k2)
-      mbar_wait(smem_u32(&sm.full_bar[warp][k2 % kWarpStages]), (uint32_t)((k2 / kWarpStages) & 1), kDrainSpinLimit);
+    for (int k2 = k + 1; k2 < my_tiles && k2 <= k + kAh; ++k2)
+      mbar_wait(smem_u32(&sm.full_bar[warp][k2 % kStages]), (uint32_t)((k2 / kStages) & 1), kDrainSpinLimit);
   }
   __syncthreads();  // every warp left its loop: no bulk copy is in flight, the rings are free
   const bool aborted = sm.abort != 0;
@@ -1215,6 +1293,8 @@ struct ReaderKernel {
   size_t smem;  // + slack for the 128-byte alignment of the base
 };
 ReaderKernel reader_kernel(int gather_mode, bool pair) {
+  if (gather_mode == kGatherFp8)
+    return {reinterpret_cast<const void*>(sparse_attention_kernel<kGatherFp8>), sizeof(SmemFp8) + 128};
   if (pair && !kTensorMemoryReader) {
     switch (gather_mode) {
       case 0: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<0>), sizeof(SmemPair<0>) + 128};
@@ -1241,8 +1321,8 @@ int configure_smem() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    for (int k = 0; k < 6; ++k) {
-      const ReaderKernel rk = reader_kernel(k % 3, k >= 3);
+    for (int k = 0; k < 7; ++k) {
+      const ReaderKernel rk = k == 6 ? reader_kernel(kGatherFp8, false) : reader_kernel(k % 3, k >= 3);
       if (cudaFuncSetAttribute(rk.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rk.smem) != cudaSuccess ||
           cudaFuncSetAttribute(rk.fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return NVQSA_ERR_CUDA;
@@ -1266,7 +1346,8 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
                   const int32_t* token_to_request, void* output, int64_t o_stride_row, int64_t o_stride_head,
                   float* partial_out, float* partial_lse, int64_t rows, int32_t query_heads, int32_t head_dim,
                   void* workspace, size_t workspace_bytes, void* stream, float* const* xpeers = nullptr,
-                  int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0, int32_t rows_per_group = 1) {
+                  int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0, int32_t rows_per_group = 1,
+                  bool fp8 = false) {
   if (rows < 0 || topk < 0 || kv_heads < 1 || query_heads < 1 || num_blocks < 0 || page_size < 1 ||
       num_requests < 0 || table_width < 0)
     return NVQSA_ERR_BAD_SHAPE;
@@ -1296,8 +1377,9 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   const int sms = device_sm_count();
   if (sms <= 0) return NVQSA_ERR_CUDA;
   if (rows_per_group < 1 || rows_per_group > kMtpRows) return NVQSA_ERR_BAD_SHAPE;
-  const MtpPlan mp = make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
-  const Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms);
+  const MtpPlan mp = fp8 ? MtpPlan{false, 1, 0} : make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
+  Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms);
+  if (fp8) pl.pair = false;  // the FP8 rows run on the full-width reader only
   const Workspace wl = mp.use ? Workspace{0, 0, 0} : workspace_layout(pl, rows, query_heads, kv_heads);
   const size_t need = wl.bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned_to(workspace, 16))) return NVQSA_ERR_WORKSPACE;
@@ -1339,6 +1421,14 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   p.query_heads = query_heads;
   p.score_scale = (float)(0.0625 * 1.4426950408889634) * (1.0f / key_global_scale);
   p.inv_value_scale = 1.0f / value_global_scale;
+  if (fp8) {
+    // FP8 sibling reader (src/qsa_fp8_harness.py:101-102, :175): the per-tensor k_scale multiplies the
+    // scores, v_scale the normalised output; regions 0 and 2 are the K and V caches.
+    p.gather_mode = kGatherFp8;
+    p.total_rows = 0;
+    p.score_scale = (float)(0.0625 * 1.4426950408889634) * key_global_scale;
+    p.inv_value_scale = value_global_scale;
+  }
   p.indices = logical_indices;
   p.topk = topk;
   p.block_table = block_table;
@@ -1524,6 +1614,28 @@ extern "C" int nvqsa_sparse_attention_grouped(
                        key_global_scale, value_global_scale, logical_indices, topk, block_table, num_requests,
                        table_width, token_to_request, output, o_stride_row, o_stride_head, nullptr, nullptr, rows,
                        query_heads, head_dim, workspace, workspace_bytes, stream, nullptr, 0, 0, 0, rows_per_group);
+}
+
+extern "C" int nvqsa_sparse_attention_fp8(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_cache, int64_t kc_stride_block, int64_t kc_stride_token, int64_t kc_stride_head,
+    const void* value_cache, int64_t vc_stride_block, int64_t vc_stride_token, int64_t vc_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads, float k_scale, float v_scale,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const void* region[4] = {key_cache, key_cache, value_cache, value_cache};
+  const int64_t strides[4][3] = {{kc_stride_block, kc_stride_token, kc_stride_head},
+                                 {kc_stride_block, kc_stride_token, kc_stride_head},
+                                 {vc_stride_block, vc_stride_token, vc_stride_head},
+                                 {vc_stride_block, vc_stride_token, vc_stride_head}};
+  return run_attention(query, q_stride_row, q_stride_head, region, strides, num_blocks, page_size, kv_heads, k_scale,
+                       v_scale, logical_indices, topk, block_table, num_requests, table_width, token_to_request,
+                       output, o_stride_row, o_stride_head, nullptr, nullptr, rows, query_heads, head_dim, workspace,
+                       workspace_bytes, stream, nullptr, 0, 0, 0, 1, true);
 }
 
 extern "C" int nvqsa_sparse_attention_partial(

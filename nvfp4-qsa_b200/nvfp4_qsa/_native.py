@@ -73,6 +73,17 @@ _SIGNATURES = {
         _P, _I64, _I64,
         _I64, _I32, _I32, _I32,
         _P, c_size_t, _P]),
+    "nvqsa_sparse_attention_fp8": (c_int, [
+        _P, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _I64, _I64, _I32, _F, _F,
+        _P, _I64,
+        _P, _I64, _I64,
+        _P,
+        _P, _I64, _I64,
+        _I64, _I32, _I32,
+        _P, c_size_t, _P]),
     "nvqsa_sparse_attention_partial": (c_int, [
         _P, _I64, _I64,
         _P, _I64, _I64, _I64,

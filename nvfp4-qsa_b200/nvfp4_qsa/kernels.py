@@ -26,6 +26,7 @@ __all__ = [
     "qsa_sparse_paged_attention_nvfp4",
     "qsa_write_cache_nvfp4",
     "qsa_sparse_paged_attention_nvfp4_partial",
+    "qsa_sparse_paged_attention_fp8",
     "qsa_merge_partials",
     "qsa_merge_partials_strided",
     "qsa_sparse_paged_attention_nvfp4_split_kv",
@@ -231,6 +232,65 @@ def qsa_sparse_paged_attention_nvfp4(
         else:
             status = lib.nvqsa_sparse_attention_grouped(*common, int(rows_per_group), *tail)
     _native.check(status, "qsa_sparse_paged_attention_nvfp4")
+
+
+def qsa_sparse_paged_attention_fp8(
+    q,
+    k_cache,
+    v_cache,
+    k_scale,
+    v_scale,
+    logical_indices,
+    block_table,
+    token_to_req,
+    out=None,
+):
+    """FP8 sibling of the NVFP4 reader (src/qsa_fp8_harness.py:211-325); returns ``out``.
+
+    ``k_cache`` / ``v_cache`` are float8_e4m3fn [blocks, page, kv_heads, head_dim]
+    (vLLM's view of the fp8 main cache, snapshot/qsa.py:328-350); the per-tensor
+    ``k_scale`` multiplies the scores and ``v_scale`` the output.  Masking and
+    output rules as ``qsa_sparse_paged_attention_nvfp4``; ``out`` defaults to a
+    new bf16 tensor shaped like ``q``.
+    """
+    if q.dim() != 3 or q.dtype != torch.bfloat16 or q.stride(-1) != 1:
+        raise ValueError("QSA FP8 query must be bf16 [rows, query_heads, head_dim] with contiguous last dim")
+    for t in (k_cache, v_cache):
+        if t.dtype != torch.float8_e4m3fn or t.dim() != 4 or t.stride(-1) != 1:
+            raise ValueError("QSA FP8 caches must be float8_e4m3fn [blocks, page, kv_heads, head_dim]")
+    if k_cache.shape != v_cache.shape or k_cache.shape[-1] != q.shape[2]:
+        raise ValueError("QSA FP8 K/V caches must match each other and the query head_dim")
+    for t in (logical_indices, block_table, token_to_req):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("QSA FP8 metadata must be contiguous int32")
+    if out is None:
+        out = torch.empty_like(q)
+    if out.shape != q.shape or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError("QSA FP8 output must be bf16 shaped like q with contiguous last dim")
+    device = q.device
+    _check_same_device((k_cache, v_cache, logical_indices, block_table, token_to_req, out), device)
+    rows, query_heads, head_dim = q.shape
+    if rows == 0:
+        return out
+    topk = logical_indices.shape[1]
+    kv_heads = k_cache.shape[2]
+    lib = _native.load()
+    with _device_ctx(device):
+        ws_bytes = _workspace_bytes(torch.cuda.current_device(), rows, query_heads, kv_heads, head_dim, topk)
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+        status = lib.nvqsa_sparse_attention_fp8(
+            q.data_ptr(), q.stride(0), q.stride(1),
+            k_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+            v_cache.data_ptr(), v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+            k_cache.shape[0], k_cache.shape[1], kv_heads, float(k_scale), float(v_scale),
+            logical_indices.data_ptr(), topk,
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            token_to_req.data_ptr(),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            rows, query_heads, head_dim,
+            workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+    _native.check(status, "qsa_sparse_paged_attention_fp8")
+    return out
 
 
 def qsa_sparse_paged_attention_nvfp4_partial(

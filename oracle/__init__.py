@@ -78,6 +78,10 @@ def _load():
                                              P, I64, I64, I64, P, I64, I64, I64,
                                              I64, I64, I32, F, F,
                                              P, I64, P, I64, I64, P, P, I64, I32, I32, P]
+        lib.orc_sparse_attention_fp8.restype = None
+        lib.orc_sparse_attention_fp8.argtypes = [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
+                                                 I64, I64, I32, F, F,
+                                                 P, I64, P, I64, I64, P, P, I64, I32, I32, P]
         lib.orc_set_threads.restype = None
         lib.orc_set_threads.argtypes = [c_int]
         lib.orc_get_threads.restype = c_int
@@ -195,6 +199,34 @@ def sparse_attention(q_bits: np.ndarray, storage: np.ndarray, indices: np.ndarra
                                  float(value_global_scale), _ptr(indices), topk, _ptr(block_table),
                                  block_table.shape[0], block_table.shape[1], _ptr(token_to_request), _ptr(out),
                                  rows, qh, hd, _ptr(lse) if return_lse else None)
+    return (out, lse) if return_lse else out
+
+
+def sparse_attention_fp8(q_bits: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, indices: np.ndarray,
+                         block_table: np.ndarray, token_to_request: np.ndarray, k_scale: float = 1.0,
+                         v_scale: float = 1.0, return_lse: bool = False):
+    """FP8 sibling reader (src/qsa_fp8_harness.py:42-208) in float64; returns fp32 [rows, qh, hd].
+
+    ``k_cache`` / ``v_cache``: uint8 views of float8_e4m3fn [blocks, page, kv_heads, head_dim], C-contiguous.
+    Scores are scaled by head_dim^-0.5 * k_scale and outputs multiplied by v_scale.
+    """
+    q_bits = np.ascontiguousarray(q_bits, dtype=np.uint16)
+    indices = np.ascontiguousarray(indices, dtype=np.int32)
+    block_table = np.ascontiguousarray(block_table, dtype=np.int32)
+    token_to_request = np.ascontiguousarray(token_to_request, dtype=np.int32)
+    for c in (k_cache, v_cache):
+        assert c.flags["C_CONTIGUOUS"] and c.dtype == np.uint8 and c.shape == k_cache.shape
+    rows, qh, hd = q_bits.shape
+    blocks, page, kvh, _ = k_cache.shape
+    sb, st, sh = page * kvh * hd, kvh * hd, hd
+    out = np.zeros((rows, qh, hd), np.float32)
+    lse = np.full((rows, qh), -np.inf, np.float32)
+    topk = indices.shape[1] if indices.ndim == 2 else 0
+    _load().orc_sparse_attention_fp8(_ptr(q_bits), qh * hd, hd, _ptr(k_cache), sb, st, sh, _ptr(v_cache), sb, st, sh,
+                                     blocks, page, kvh, float(k_scale), float(v_scale), _ptr(indices), topk,
+                                     _ptr(block_table), block_table.shape[0], block_table.shape[1],
+                                     _ptr(token_to_request), _ptr(out), rows, qh, hd,
+                                     _ptr(lse) if return_lse else None)
     return (out, lse) if return_lse else out
 
 

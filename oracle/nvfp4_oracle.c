@@ -200,16 +200,16 @@ void orc_write_cache(const uint16_t* key, int64_t key_st, int64_t key_sh, const 
  * contiguous; lse_out (optional, fp32 [rows, query_heads]) receives each
  * head's base-2 log-sum-exp, or -inf when no selection is valid.  K/V are dequantised exactly (e2m1 * e4m3); the score scale is
  * head_dim^-0.5 / gk and the output is divided by gv. */
-void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kd, int64_t kd_sb,
+static void attention_core(int fp8, const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kd, int64_t kd_sb,
                           int64_t kd_st, int64_t kd_sh, const uint8_t* ks, int64_t ks_sb, int64_t ks_st,
                           int64_t ks_sh, const uint8_t* vd, int64_t vd_sb, int64_t vd_st, int64_t vd_sh,
                           const uint8_t* vs, int64_t vs_sb, int64_t vs_st, int64_t vs_sh, int64_t num_blocks,
-                          int64_t page_size, int32_t kv_heads, float gk, float gv, const int32_t* indices,
+                          int64_t page_size, int32_t kv_heads, double score_mul, double out_mul, const int32_t* indices,
                           int64_t topk, const int32_t* block_table, int64_t num_requests, int64_t table_width,
                           const int32_t* token_to_request, float* out, int64_t rows, int32_t query_heads,
                           int32_t head_dim, float* lse_out) {
   const int G = query_heads / kv_heads;
-  const double scale = 1.0 / sqrt((double)head_dim) / (double)gk;
+  const double scale = score_mul / sqrt((double)head_dim);
 #pragma omp parallel for collapse(2) schedule(dynamic)
   for (int64_t r = 0; r < rows; ++r) {
     for (int h = 0; h < kv_heads; ++h) {
@@ -239,6 +239,11 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
         const uint8_t* vdr = vd + b * vd_sb + o * vd_st + h * vd_sh;
         const uint8_t* vsr = vs + b * vs_sb + o * vs_st + h * vs_sh;
         for (int d = 0; d < head_dim; ++d) {
+          if (fp8) { /* one float8_e4m3fn byte per element (qsa_fp8_harness.py:139-158) */
+            K[t * head_dim + d] = (double)orc_e4m3_to_f32(kdr[d]);
+            V[t * head_dim + d] = (double)orc_e4m3_to_f32(vdr[d]);
+            continue;
+          }
           const uint8_t kb = kdr[d >> 1], vb = vdr[d >> 1];
           const uint8_t kn = (d & 1) ? (kb >> 4) : (kb & 0xf);
           const uint8_t vn = (d & 1) ? (vb >> 4) : (vb & 0xf);
@@ -272,7 +277,7 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
         for (int d = 0; d < head_dim; ++d) {
           double acc = 0.0;
           for (int64_t t = 0; t < nv; ++t) acc += s[t] * V[t * head_dim + d];
-          orow[d] = (float)(acc / den / (double)gv);
+          orow[d] = (float)(acc / den * out_mul);
         }
         /* base-2 log-sum-exp of the scaled scores, the split-KV partial format of
          * src/qsa_fp8_harness.py:183-208 (lse = m + log2 l in log2 units) */
@@ -285,6 +290,37 @@ void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const u
       free(s);
     }
   }
+}
+
+void orc_sparse_attention(const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kd, int64_t kd_sb,
+                          int64_t kd_st, int64_t kd_sh, const uint8_t* ks, int64_t ks_sb, int64_t ks_st,
+                          int64_t ks_sh, const uint8_t* vd, int64_t vd_sb, int64_t vd_st, int64_t vd_sh,
+                          const uint8_t* vs, int64_t vs_sb, int64_t vs_st, int64_t vs_sh, int64_t num_blocks,
+                          int64_t page_size, int32_t kv_heads, float gk, float gv, const int32_t* indices,
+                          int64_t topk, const int32_t* block_table, int64_t num_requests, int64_t table_width,
+                          const int32_t* token_to_request, float* out, int64_t rows, int32_t query_heads,
+                          int32_t head_dim, float* lse_out) {
+  attention_core(0, q, q_sr, q_sh, kd, kd_sb, kd_st, kd_sh, ks, ks_sb, ks_st, ks_sh, vd, vd_sb, vd_st, vd_sh, vs,
+                 vs_sb, vs_st, vs_sh, num_blocks, page_size, kv_heads, 1.0 / (double)gk, 1.0 / (double)gv, indices,
+                 topk, block_table, num_requests, table_width, token_to_request, out, rows, query_heads, head_dim,
+                 lse_out);
+}
+
+/* The FP8 sibling reader (src/qsa_fp8_harness.py:42-208): K and V caches of
+ * float8_e4m3fn bytes [blocks, page, kv_heads, head_dim] with byte strides;
+ * the per-tensor k_scale multiplies the scores (folded into the softmax scale,
+ * :101-102), v_scale the normalised output (:175).  Same masking, softmax and
+ * partial format as the NVFP4 reader. */
+void orc_sparse_attention_fp8(const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kc, int64_t kc_sb,
+                              int64_t kc_st, int64_t kc_sh, const uint8_t* vc, int64_t vc_sb, int64_t vc_st,
+                              int64_t vc_sh, int64_t num_blocks, int64_t page_size, int32_t kv_heads, float k_scale,
+                              float v_scale, const int32_t* indices, int64_t topk, const int32_t* block_table,
+                              int64_t num_requests, int64_t table_width, const int32_t* token_to_request,
+                              float* out, int64_t rows, int32_t query_heads, int32_t head_dim, float* lse_out) {
+  attention_core(1, q, q_sr, q_sh, kc, kc_sb, kc_st, kc_sh, kc, kc_sb, kc_st, kc_sh, vc, vc_sb, vc_st, vc_sh, vc,
+                 vc_sb, vc_st, vc_sh, num_blocks, page_size, kv_heads, (double)k_scale, (double)v_scale, indices,
+                 topk, block_table, num_requests, table_width, token_to_request, out, rows, query_heads, head_dim,
+                 lse_out);
 }
 
 void orc_set_threads(int n) {
