@@ -411,7 +411,8 @@ def bench_fp8(args, device, steps):
         "roofline": {"bound": "hbm", "achieved": algo / per_layer / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": algo / per_layer / 1e9 / peak, "peak_kind": kind,
                      "kernel": "sparse_attention_kernel<3> (one layer, FP8 rows)",
-                     "algorithmic_bytes_per_launch": algo},
+                     "algorithmic_bytes_per_launch": algo,
+                     "traffic": profile_traffic("sparse_attention_fp8.md")},
         "gpu_launches": (reps + 5) * layers,
     }
 
