@@ -259,6 +259,83 @@ def bench_write(device, steps):
     }
 
 
+def bench_fused_write(device, steps):
+    """Fused k-norm -> RoPE -> NVFP4 writer on the prefill configuration (8,192 projection rows).
+
+    K and V as they leave the QKV projection (before GemmaRMSNorm and a 64-dim NeoX rotary of Qwen3-Next's
+    shape) are normed, rotated, quantised and scattered by nvqsa_norm_rope_write_cache into a 64 x 3,136 cache;
+    once without and once with the rotated bf16 K written back (key_out).  8 rotating input sets (> L2)
+    per CUDA-graph round, like the plain writer's section.
+    """
+    import torch
+    from nvfp4_qsa import kernels
+    from nvfp4_qsa import workloads as W
+
+    tokens, blocks, page, sets, rot, max_pos = 8192, 64, 3136, 8, 64, 262144
+    gen = torch.Generator(device=device).manual_seed(98)
+    cos_sin = torch.from_numpy(W.rope_cos_sin(max_pos, rot)).to(device=device, dtype=torch.bfloat16)
+    weight = (torch.randn(HEAD_DIM, device=device, generator=gen) * 0.1).to(torch.bfloat16).float()
+    bufs = []
+    for i in range(sets):
+        kv = torch.randn(2, tokens, KV_HEADS, HEAD_DIM, device=device, generator=gen)
+        kv[0] *= torch.exp2(torch.rand(tokens, KV_HEADS, 1, device=device, generator=gen) * 4 - 1)
+        kv = torch.where(torch.rand(kv.shape, device=device, generator=gen) < 0.02, kv * 32, kv).to(torch.bfloat16)
+        storage = torch.zeros(blocks, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        slots = torch.randperm(blocks * page, device=device, generator=gen)[:tokens].contiguous()
+        pos = torch.randint(0, max_pos, (tokens,), device=device, generator=gen)
+        bufs.append((kv[0], kv[1], kd, ks, vd, vs, slots, pos, torch.empty_like(kv[0])))
+
+    def measure(with_key_out):
+        def one_round():
+            for k, v, kd, ks, vd, vs, slots, pos, ko in bufs:
+                kernels.qsa_norm_rope_write_cache_nvfp4(k, v, kd, ks, vd, vs, slots, 1.0, 1.0, positions=pos,
+                                                        cos_sin_cache=cos_sin, k_norm_weight=weight, eps=1e-6,
+                                                        key_out=ko if with_key_out else None)
+
+        one_round()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            one_round()
+        torch.cuda.current_stream(device).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            one_round()
+        for _ in range(3):
+            graph.replay()
+        rounds = max(20, steps)
+        secs = timed(graph.replay, rounds, device)
+        del graph
+        return secs / (rounds * sets), rounds * sets
+
+    per_launch, launches = measure(False)
+    per_launch_ko, launches_ko = measure(True)
+    # per token: K and V bf16 in (2,048 B), slot + position (16 B), the position's cos/sin row (128 B),
+    # two 288-byte records out; key_out adds the rotated K (1,024 B)
+    algo = tokens * (KV_HEADS * HEAD_DIM * 2 * 2 + 16 + rot * 2 + KV_HEADS * RECORD)
+    algo_ko = algo + tokens * KV_HEADS * HEAD_DIM * 2
+    peak, kind = measured_peaks()
+    return {
+        "config": {"workload": "prefill projection rows: 8192 tokens bf16 K/V [8192,2,256] before k_norm and RoPE "
+                               "(GemmaRMSNorm, NeoX rotary 64 of 256, positions U[0, 262144)), into a 64 x 3136 "
+                               "NVFP4 cache at random free slots; 8 rotating buffer sets (inputs > L2)",
+                   "launches": launches + launches_ko},
+        "us_per_launch": per_launch * 1e6,
+        "gb_per_s": algo / per_launch / 1e9,
+        "us_per_launch_key_out": per_launch_ko * 1e6,
+        "gb_per_s_key_out": algo_ko / per_launch_ko / 1e9,
+        "roofline": {"bound": "hbm", "achieved": algo / per_launch / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algo / per_launch / 1e9 / peak, "peak_kind": kind,
+                     "kernel": "write_cache_kernel<256, true, true, true> (fused k-norm + RoPE, no key_out)",
+                     "algorithmic_bytes_per_launch": algo,
+                     "traffic": profile_traffic("write_cache_fused.md")},
+        "gpu_launches": launches + launches_ko,
+    }
+
+
 def bench_mtp(args, device, steps):
     """Config 4: MTP=3 decode batch, 12 sequences x 4 rows sharing each sequence's 2,048 selections.
 
@@ -683,6 +760,7 @@ def main_ours(args):
 
     split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
+    fused_write = bench_fused_write(device, args.steps) if rank == 0 else None
     # config 4 and the FP8 sibling reader are single-GPU side measurements: one GPU runs only
     mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
     fp8 = bench_fp8(args, device, args.steps) if world == 1 and not args.skip_fp8 else None
@@ -717,6 +795,7 @@ def main_ours(args):
                     "eager_ms_per_step": eager_secs / e2e_steps * 1e3},
             "gpu_launches": args.steps * args.layers * launches_per_layer,
             "write": write,
+            "fused_write": fused_write,
         }
         if split is not None:
             result["split_kv"] = split

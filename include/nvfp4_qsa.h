@@ -87,6 +87,55 @@ int nvqsa_write_cache(
     float key_global_scale, float value_global_scale, void* stream);
 
 /*
+ * nvqsa_write_cache with the K rows first passed through the caller's k-norm
+ * and rotary embedding, in the same launch: K is read once from the QKV
+ * projection output and never written back as bf16 unless key_out asks for it.
+ *
+ * Replaces, at the reference's call site (integration/snapshot/qsa.py:618-667:
+ * qkv_proj -> k_norm (vLLM GemmaRMSNorm) -> rotary_emb -> qsa_write_cache_nvfp4),
+ * the k_norm and rotary steps for K plus the writer.  Per (token t, kv head h):
+ *   norm (norm_weight != NULL):
+ *     ss = sum_d x[d]^2 in fp32, x[d] bf16: 32 partial sums, partial l over
+ *          d in [l*E, l*E+E) (E = head_dim/32) as (FMA-sum of the squares at
+ *          even d, in order) + (FMA-sum of those at odd d, in order); the 32
+ *          partials added pairwise at distances 16, 8, 4, 2, 1
+ *     r  = 1 / sqrt(ss / head_dim + eps)             (IEEE sqrt and divide)
+ *     y[d] = bf16_rn((x[d] * r) * (norm_weight[d] + norm_weight_offset))
+ *          (norm_weight_offset = 1 for GemmaRMSNorm, 0 for a plain RMSNorm
+ *          with fp32 weights); without a norm, y = x.
+ *   rotation (rotary_dim > 0): c, s = cos_sin_cache[positions[t]] halves
+ *     (bf16 [max_position, cos_sin_stride], cos in [0, rotary_dim/2), sin in
+ *     [rotary_dim/2, rotary_dim)); NeoX pairs (y[i], y[i + rotary_dim/2]),
+ *     GPT-J pairs (y[2i], y[2i+1]):
+ *       o1 = bf16(bf16(x1 c) - bf16(x2 s)), o2 = bf16(bf16(x2 c) + bf16(x1 s))
+ *     -- vLLM's native rotary embedding in bf16 arithmetic, bit for bit.
+ *     Elements at or past rotary_dim pass through.
+ *   then K (rotated) and V (unchanged) are encoded and scattered exactly as
+ *   nvqsa_write_cache does; key_out (optional, bf16 [num_tokens, kv_heads,
+ *   head_dim] with element strides) receives the rotated K of every token
+ *   whose position is valid, whatever its slot.
+ * A token whose position is outside [0, max_position) is skipped entirely
+ * (no cache bytes, no key_out row).  rotary_dim must be a multiple of
+ * head_dim/16 and at most head_dim (NVQSA_ERR_BAD_SHAPE); rotary_dim = 0 and
+ * norm_weight = NULL give the plain writer.  eps must be finite and >= 0.
+ * No counterpart entry in the reference (its writer takes K after the norm
+ * and rotation).
+ */
+int nvqsa_norm_rope_write_cache(
+    const void* key, int64_t key_stride_token, int64_t key_stride_head,
+    const void* value, int64_t value_stride_token, int64_t value_stride_head,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int64_t num_tokens, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size, float key_global_scale, float value_global_scale,
+    const float* norm_weight, float norm_weight_offset, float eps,
+    const int64_t* positions, const void* cos_sin_cache, int64_t cos_sin_stride, int64_t max_position,
+    int32_t rotary_dim, int32_t is_neox_style,
+    void* key_out, int64_t key_out_stride_token, int64_t key_out_stride_head, void* stream);
+
+/*
  * Bytes of workspace nvqsa_sparse_attention needs for this problem on the
  * current device (0 when the problem runs without a split-KV merge).
  */

@@ -60,6 +60,21 @@ struct WriteParams {
   // 1: both global scales in [2^-6, 2^28] (see the encoder's fast path)
   int32_t plain;
   int32_t lut_by_scaling;  // 1: scale table by power-of-two scaling of g / k (see build_out_scale_lut)
+  // K-norm and RoPE ahead of the encoder (nvqsa_norm_rope_write_cache only).
+  const int64_t* positions;      // [num_tokens]
+  const __nv_bfloat16* cos_sin;  // [max_position, >= rot_dim]: cos in [0, rot/2), sin in [rot/2, rot)
+  int64_t cos_sin_stride;        // elements
+  int64_t max_position;
+  const float* norm_weight;      // [head_dim] or null (no norm)
+  float norm_offset;             // added to every weight in fp32 (1 for GemmaRMSNorm)
+  float norm_eps;
+  float inv_head_dim;
+  int32_t rot_dim;               // 0: no rotation
+  int32_t neox;                  // 1: rotate halves (x[i], x[i + rot/2]); 0: GPT-J pairs (x[2i], x[2i+1])
+  int32_t vec_cs;                // 1: cos/sin runs of one lane are aligned for one vector load
+  __nv_bfloat16* key_out;        // optional normed, rotated bf16 K [num_tokens, kv_heads, head_dim]
+  int64_t key_out_stride_token, key_out_stride_head;
+  int32_t vec_ko;                // 1: key_out rows take one vector store per lane
 };
 
 template <int EPL>
@@ -304,6 +319,218 @@ __device__ __forceinline__ void write_item(const WriteParams& p, const float (*o
     encode_store(std::false_type{});
 }
 
+// ---------------------------------------------------------------------------
+// K-norm + RoPE ahead of the encoder (nvqsa_norm_rope_write_cache).
+//
+// The caller of the reference writer (integration/snapshot/qsa.py:618-667)
+// takes K from the QKV projection through vLLM's GemmaRMSNorm k_norm and its
+// rotary embedding, both in bf16, and hands the result to
+// qsa_write_cache_nvfp4.  Here the same two steps run on the rows already in
+// registers, so K makes one trip from HBM instead of three.
+//   norm : ss = sum x^2 (fp32; per lane, the squares of its even and of its
+//          odd elements are summed in element order by FMA and then added;
+//          the 32 lane sums are added pairwise at distances 16, 8, 4, 2, 1),
+//          r = 1 / sqrt(ss / head_dim + eps) (IEEE sqrt, IEEE divide),
+//          y = bf16_rn((x * r) * (w + offset))      vLLM ir rms_norm order
+//   rope : cos/sin rows of the bf16 cache at the token's position,
+//          o1 = bf16(bf16(x1 c) - bf16(x2 s)), o2 = bf16(bf16(x2 c) + bf16(x1 s))
+//          -- torch's bf16 elementwise arithmetic of vLLM's native rotary
+//          embedding: each product and sum rounds to bf16 (here on packed
+//          bf16x2 words, which round identically; see bf16x2_mul).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// N consecutive bf16 values (N even) from p into N/2 words; vector loads when aligned.
+template <int N>
+__device__ __forceinline__ void load_bf16_run(const __nv_bfloat16* p, bool vec, uint32_t (&w)[N / 2]) {
+  if (vec) {
+    if constexpr (N == 2) {
+      w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+    } else if constexpr (N == 4) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = v.x;
+      w[1] = v.y;
+    } else {
+#pragma unroll
+      for (int q = 0; q < N / 8; ++q) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + q);
+        w[4 * q] = v.x;
+        w[4 * q + 1] = v.y;
+        w[4 * q + 2] = v.z;
+        w[4 * q + 3] = v.w;
+      }
+    }
+  } else {
+    const unsigned short* s = reinterpret_cast<const unsigned short*>(p);
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) w[i] = (uint32_t)__ldg(s + 2 * i) | ((uint32_t)__ldg(s + 2 * i + 1) << 16);
+  }
+}
+
+// Lane roles in the rotation: a lane holds elements [lane*EPL, lane*EPL + EPL).
+// NeoX: a lane below rot/2 holds x1 (its partner lane + rot/(2 EPL) holds x2),
+// a lane in [rot/2, rot) holds x2; both read cos/sin at element index mod rot/2.
+// GPT-J: (x[2i], x[2i+1]) lie in one word, cos/sin index i.
+struct RopeLane {
+  bool active;  // lane holds rotated elements
+  bool first;   // NeoX: lane holds x1
+  int partner;  // NeoX: lane holding the other half
+  int cs0;      // first cos/sin index of the lane
+};
+
+template <int EPL>
+__device__ __forceinline__ RopeLane rope_lane(const WriteParams& p, int lane) {
+  RopeLane r;
+  const int e0 = lane * EPL, half = p.rot_dim >> 1;
+  r.active = e0 < p.rot_dim;
+  r.first = e0 < half;
+  const int shift = half / EPL;
+  r.partner = p.neox ? (r.first ? lane + shift : lane - shift) : lane;
+  if (!r.active) r.partner = lane;
+  r.cs0 = p.neox ? (r.first ? e0 : e0 - half) : (e0 >> 1);
+  return r;
+}
+
+// cos/sin values of one lane for the token at `pos` (EPL each for NeoX, EPL/2 for GPT-J).
+template <int EPL>
+__device__ __forceinline__ void load_cos_sin(const WriteParams& p, const RopeLane& rl, int64_t pos,
+                                             uint32_t (&cw)[EPL / 2], uint32_t (&sw)[EPL / 2]) {
+  const __nv_bfloat16* row = p.cos_sin + pos * p.cos_sin_stride + rl.cs0;
+  const int half = p.rot_dim >> 1;
+  const bool vec = p.vec_cs != 0;
+  if (p.neox) {
+    load_bf16_run<EPL>(row, vec, cw);
+    load_bf16_run<EPL>(row + half, vec, sw);
+  } else if constexpr (EPL >= 4) {
+    uint32_t c2[EPL / 4], s2[EPL / 4];
+    load_bf16_run<EPL / 2>(row, vec, c2);
+    load_bf16_run<EPL / 2>(row + half, vec, s2);
+#pragma unroll
+    for (int i = 0; i < EPL / 4; ++i) {
+      cw[i] = c2[i];
+      sw[i] = s2[i];
+    }
+  } else {  // EPL == 2: one GPT-J pair per lane
+    cw[0] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(row));
+    sw[0] = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(row + half));
+  }
+}
+
+// Packed bf16 arithmetic (sm_90+ PTX).  For bf16 operands these equal
+// torch's bf16 elementwise ops (fp32 result, then round to bf16): a product
+// of two bf16 values is exact in fp32 except below 2^-126, where the fp32
+// rounding can only land on the bf16 tie at 2^-134 from below, which both
+// routes round to zero; a sum of two bf16 values is exact in fp32 unless
+// their exponents differ by more than 16, and then the fp32 rounding cannot
+// create a bf16 tie.  NaN results are the canonical 0x7fff in both.
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// k-norm + rotation of the K rows of both heads of an item (k1 is a copy of
+// k0's head when the item has one head).  The two rows share one reduction:
+// lanes 0-15 finish head h0's sum and lanes 16-31 head h1's, then one square
+// root and divide serve both.  Per lane the squares of the even and of the odd
+// elements are summed separately in element order (one f32x2 FMA per word)
+// and then added; the 32 lane sums are added pairwise at distances 16, 8, 4,
+// 2, 1.
+template <int EPL>
+__device__ __forceinline__ void norm_rope_pair(const WriteParams& p, int lane, const RopeLane& rl,
+                                               const float2 (&wp)[EPL / 2], const uint32_t (&cw)[EPL / 2],
+                                               const uint32_t (&sw)[EPL / 2], uint32_t (&k0)[EPL / 2],
+                                               uint32_t (&k1)[EPL / 2]) {
+  constexpr int NW = EPL / 2;
+  if (p.norm_weight != nullptr) {
+    float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const float2 f0 = make_float2(bf_lo(k0[i]), bf_hi(k0[i]));
+      const float2 f1 = make_float2(bf_lo(k1[i]), bf_hi(k1[i]));
+      a0 = __ffma2_rn(f0, f0, a0);
+      a1 = __ffma2_rn(f1, f1, a1);
+    }
+    const float s0 = __fadd_rn(a0.x, a0.y), s1 = __fadd_rn(a1.x, a1.y);
+    const bool low = lane < 16;
+    float t = low ? s0 : s1;
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, low ? s1 : s0, 16));
+#pragma unroll
+    for (int m = 8; m >= 1; m >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, m));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(t, p.inv_head_dim), p.norm_eps)));
+    const float r0 = __shfl_sync(0xffffffffu, r, 0), r1 = __shfl_sync(0xffffffffu, r, 16);
+    const float2 r02 = make_float2(r0, r0), r12 = make_float2(r1, r1);
+#pragma unroll
+    for (int i = 0; i < NW; ++i) {
+      const float2 y0 = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(k0[i]), bf_hi(k0[i])), r02), wp[i]);
+      const float2 y1 = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(k1[i]), bf_hi(k1[i])), r12), wp[i]);
+      k0[i] = pack_bf16x2(y0.x, y0.y);
+      k1[i] = pack_bf16x2(y1.x, y1.y);
+    }
+  }
+  if (p.rot_dim > 0) {
+    if (p.neox) {
+      // first half: own = x1, partner = x2 -> x1 c - x2 s; second half: own = x2, partner = x1 -> x2 c + x1 s
+      uint32_t o0[NW], o1[NW];
+#pragma unroll
+      for (int i = 0; i < NW; ++i) {
+        o0[i] = __shfl_sync(0xffffffffu, k0[i], rl.partner);
+        o1[i] = __shfl_sync(0xffffffffu, k1[i], rl.partner);
+      }
+      if (rl.active) {
+        const uint32_t neg = rl.first ? 0x80008000u : 0u;
+#pragma unroll
+        for (int i = 0; i < NW; ++i) {
+          k0[i] = bf16x2_add(bf16x2_mul(k0[i], cw[i]), bf16x2_mul(o0[i], sw[i]) ^ neg);
+          k1[i] = bf16x2_add(bf16x2_mul(k1[i], cw[i]), bf16x2_mul(o1[i], sw[i]) ^ neg);
+        }
+      }
+    } else if (rl.active) {
+      // word i = (x1, x2) = elements (2k, 2k+1), k = cs0 + i: (x1 c - x2 s, x2 c + x1 s)
+#pragma unroll
+      for (int i = 0; i < NW; ++i) {
+        const uint32_t sel = (i & 1) ? 0x3232u : 0x1010u;
+        const uint32_t cc = __byte_perm(cw[i >> 1], 0u, sel), ss = __byte_perm(sw[i >> 1], 0u, sel);
+        k0[i] = bf16x2_add(bf16x2_mul(k0[i], cc), bf16x2_mul(__byte_perm(k0[i], 0u, 0x1032u), ss) ^ 0x00008000u);
+        k1[i] = bf16x2_add(bf16x2_mul(k1[i], cc), bf16x2_mul(__byte_perm(k1[i], 0u, 0x1032u), ss) ^ 0x00008000u);
+      }
+    }
+  }
+}
+
+template <int EPL>
+__device__ __forceinline__ void store_bf16_row(__nv_bfloat16* p, bool vec, const uint32_t (&w)[EPL / 2]) {
+  if (vec) {
+    if constexpr (EPL == 2) {
+      *reinterpret_cast<uint32_t*>(p) = w[0];
+    } else if constexpr (EPL == 4) {
+      *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < EPL / 8; ++q)
+        reinterpret_cast<uint4*>(p)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+  } else {
+    unsigned short* s = reinterpret_cast<unsigned short*>(p);
+#pragma unroll
+    for (int i = 0; i < EPL / 2; ++i) {
+      s[2 * i] = (unsigned short)(w[i] & 0xffffu);
+      s[2 * i + 1] = (unsigned short)(w[i] >> 16);
+    }
+  }
+}
+
 // Item w -> (token, first kv head of its pair).
 template <bool RECORD>
 __device__ __forceinline__ void item_token(int64_t w, int head_pairs, int64_t& token, int& h0) {
@@ -319,24 +546,48 @@ __device__ __forceinline__ void item_token(int64_t w, int head_pairs, int64_t& t
 // rows loaded into registers.  Any head_dim and layout.  A warp issues every
 // global load of its first item (the slot and the K and V rows of both heads)
 // before the CTA builds its scale table, so the table is built while the
-// loads are in flight.
-template <int HEAD_DIM, bool VEC, bool RECORD>
-__global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kernel(const WriteParams p) {
+// loads are in flight.  FUSE: the K rows pass through the k-norm and the
+// rotary embedding first (nvqsa_norm_rope_write_cache); an item whose position
+// is outside [0, max_position) is skipped entirely.
+template <int HEAD_DIM, bool VEC, bool RECORD, bool FUSE>
+__global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : (FUSE ? 3 : 4)) write_cache_kernel(const WriteParams p) {
   constexpr int EPL = HEAD_DIM / 32;
   constexpr int NW = EPL / 2;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int head_pairs = (p.kv_heads + 1) >> 1;
   const int64_t items = p.num_tokens * head_pairs;
+  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   __shared__ float out_scale_lut[2][256];
   __shared__ float quot[2][16];
 
   int64_t token = 0, slot = -1;
   int h0 = 0;
   uint32_t x[4][NW];  // K h0, V h0, K h1, V h1
+  // FUSE state: the lane's norm weights (+ offset), rotation role, the item's position and cos/sin
+  float2 wp[FUSE ? EPL / 2 : 1];
+  uint32_t cw[FUSE ? NW : 1], sw[FUSE ? NW : 1];
+  RopeLane rl{};
+  bool pos_ok = true;
+  if constexpr (FUSE) {
+    rl = rope_lane<EPL>(p, lane);
+#pragma unroll
+    for (int j = 0; j < EPL / 2; ++j) {
+      const bool nw = p.norm_weight != nullptr;
+      wp[j] = make_float2(nw ? __fadd_rn(__ldg(p.norm_weight + lane * EPL + 2 * j), p.norm_offset) : 0.0f,
+                          nw ? __fadd_rn(__ldg(p.norm_weight + lane * EPL + 2 * j + 1), p.norm_offset) : 0.0f);
+    }
+  }
   auto load_item = [&](int64_t w) {
     item_token<RECORD>(w, head_pairs, token, h0);
     slot = __ldg(p.slots + token);
+    if constexpr (FUSE) {
+      if (p.rot_dim > 0) {
+        const int64_t pos = __ldg(p.positions + token);
+        pos_ok = pos >= 0 && pos < p.max_position;
+        if (pos_ok && rl.active) load_cos_sin<EPL>(p, rl, pos, cw, sw);
+      }
+    }
     const bool two = h0 + 1 < p.kv_heads;
     if constexpr (RECORD) {
       // one source offset for K and V: token * stride + head * stride + lane * EPL
@@ -358,19 +609,28 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
     }
   };
 
-  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (w0 < items) load_item(w0);
   build_out_scale_lut(p, out_scale_lut, quot);
   __syncthreads();
   for (int64_t w = w0; w < items; w += warps) {
     if (w != w0) load_item(w);
+    if constexpr (FUSE) {
+      if (!pos_ok) continue;  // warp-uniform: one position per item
+      const bool two = h0 + 1 < p.kv_heads;
+      norm_rope_pair<EPL>(p, lane, rl, wp, cw, sw, x[0], x[2]);
+      if (p.key_out != nullptr) {
+        __nv_bfloat16* ko = p.key_out + token * p.key_out_stride_token + h0 * p.key_out_stride_head + lane * EPL;
+        store_bf16_row<EPL>(ko, p.vec_ko != 0, x[0]);
+        if (two) store_bf16_row<EPL>(ko + p.key_out_stride_head, p.vec_ko != 0, x[2]);
+      }
+    }
     int64_t block, offset;
     if (slot_position<RECORD>(p, slot, block, offset))
       write_item<EPL, RECORD>(p, out_scale_lut, lane, block, offset, h0, x);
   }
 }
 
-template <int HD, bool VEC, bool RECORD>
+template <int HD, bool VEC, bool RECORD, bool FUSE>
 cudaError_t launch_write_impl(const WriteParams& p, cudaStream_t stream) {
   const int64_t items = p.num_tokens * ((p.kv_heads + 1) / 2);
   const int threads = 256;
@@ -379,22 +639,34 @@ cudaError_t launch_write_impl(const WriteParams& p, cudaStream_t stream) {
   // One resident wave (occupancy of this instantiation on this device); grid-stride beyond.
   static int per_sm = 0;
   if (per_sm <= 0 &&
-      (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, write_cache_kernel<HD, VEC, RECORD>, threads, 0) !=
-           cudaSuccess ||
+      (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, write_cache_kernel<HD, VEC, RECORD, FUSE>, threads,
+                                                     0) != cudaSuccess ||
        per_sm <= 0))
     per_sm = 2;
   const int sms = device_sm_count();
   const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * per_sm;
   if (blocks > cap) blocks = cap;
-  write_cache_kernel<HD, VEC, RECORD><<<(unsigned)blocks, threads, 0, stream>>>(p);
+  write_cache_kernel<HD, VEC, RECORD, FUSE><<<(unsigned)blocks, threads, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
-template <int HD>
+template <int HD, bool FUSE>
 cudaError_t launch_write(const WriteParams& p, cudaStream_t stream) {
   if (p.record)
-    return p.vec_src ? launch_write_impl<HD, true, true>(p, stream) : launch_write_impl<HD, false, true>(p, stream);
-  return p.vec_src ? launch_write_impl<HD, true, false>(p, stream) : launch_write_impl<HD, false, false>(p, stream);
+    return p.vec_src ? launch_write_impl<HD, true, true, FUSE>(p, stream)
+                     : launch_write_impl<HD, false, true, FUSE>(p, stream);
+  return p.vec_src ? launch_write_impl<HD, true, false, FUSE>(p, stream)
+                   : launch_write_impl<HD, false, false, FUSE>(p, stream);
+}
+
+template <bool FUSE>
+cudaError_t launch_write_any(const WriteParams& p, int head_dim, cudaStream_t s) {
+  switch (head_dim) {
+    case 64: return launch_write<64, FUSE>(p, s);
+    case 128: return launch_write<128, FUSE>(p, s);
+    case 256: return launch_write<256, FUSE>(p, s);
+    default: return launch_write<512, FUSE>(p, s);
+  }
 }
 
 }  // namespace
@@ -402,7 +674,10 @@ cudaError_t launch_write(const WriteParams& p, cudaStream_t stream) {
 
 using namespace nvqsa;
 
-extern "C" int nvqsa_write_cache(
+// Shared host checks and parameter setup of both writer entries.  Returns
+// NVQSA_OK with `go` set when there is work to launch.
+static int prepare_write(
+    WriteParams& p, bool& go,
     const void* key, int64_t key_stride_token, int64_t key_stride_head,
     const void* value, int64_t value_stride_token, int64_t value_stride_head,
     void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
@@ -410,15 +685,15 @@ extern "C" int nvqsa_write_cache(
     void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
     void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
     const int64_t* slot_mapping, int64_t num_tokens, int32_t kv_heads, int32_t head_dim,
-    int64_t num_blocks, int64_t page_size,
-    float key_global_scale, float value_global_scale, void* stream) {
+    int64_t num_blocks, int64_t page_size, float key_global_scale, float value_global_scale) {
+  go = false;
   if (num_tokens < 0 || kv_heads < 0 || num_blocks < 0 || page_size < 1) return NVQSA_ERR_BAD_SHAPE;
   if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512) return NVQSA_ERR_HEAD_DIM;
   if (num_tokens == 0 || kv_heads == 0 || num_blocks == 0) return NVQSA_OK;
   if (!key || !value || !key_data || !key_scale || !value_data || !value_scale || !slot_mapping)
     return NVQSA_ERR_NULL_POINTER;
 
-  WriteParams p;
+  p = WriteParams{};
   p.src[0] = static_cast<const __nv_bfloat16*>(key);
   p.src[1] = static_cast<const __nv_bfloat16*>(value);
   p.src_stride_token[0] = key_stride_token;
@@ -509,14 +784,93 @@ extern "C" int nvqsa_write_cache(
       vec = false;
   }
   p.vec_src = vec ? 1 : 0;
+  go = true;
+  return NVQSA_OK;
+}
 
-  cudaError_t err;
-  cudaStream_t s = as_stream(stream);
-  switch (head_dim) {
-    case 64: err = launch_write<64>(p, s); break;
-    case 128: err = launch_write<128>(p, s); break;
-    case 256: err = launch_write<256>(p, s); break;
-    default: err = launch_write<512>(p, s); break;
+extern "C" int nvqsa_write_cache(
+    const void* key, int64_t key_stride_token, int64_t key_stride_head,
+    const void* value, int64_t value_stride_token, int64_t value_stride_head,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int64_t num_tokens, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size,
+    float key_global_scale, float value_global_scale, void* stream) {
+  WriteParams p;
+  bool go = false;
+  const int st = prepare_write(p, go, key, key_stride_token, key_stride_head, value, value_stride_token,
+                               value_stride_head, key_data, kd_stride_block, kd_stride_token, kd_stride_head,
+                               key_scale, ks_stride_block, ks_stride_token, ks_stride_head, value_data,
+                               vd_stride_block, vd_stride_token, vd_stride_head, value_scale, vs_stride_block,
+                               vs_stride_token, vs_stride_head, slot_mapping, num_tokens, kv_heads, head_dim,
+                               num_blocks, page_size, key_global_scale, value_global_scale);
+  if (st != NVQSA_OK || !go) return st;
+  const cudaError_t err = launch_write_any<false>(p, head_dim, as_stream(stream));
+  return err == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
+}
+
+extern "C" int nvqsa_norm_rope_write_cache(
+    const void* key, int64_t key_stride_token, int64_t key_stride_head,
+    const void* value, int64_t value_stride_token, int64_t value_stride_head,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int64_t num_tokens, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size, float key_global_scale, float value_global_scale,
+    const float* norm_weight, float norm_weight_offset, float eps,
+    const int64_t* positions, const void* cos_sin_cache, int64_t cos_sin_stride, int64_t max_position,
+    int32_t rotary_dim, int32_t is_neox_style,
+    void* key_out, int64_t key_out_stride_token, int64_t key_out_stride_head, void* stream) {
+  // Rotation and norm arguments first, so that bad ones are reported even for an empty batch.
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256 && head_dim != 512) return NVQSA_ERR_HEAD_DIM;
+  const int epl = head_dim / 32;
+  if (rotary_dim < 0 || rotary_dim > head_dim || rotary_dim % (2 * epl) != 0) return NVQSA_ERR_BAD_SHAPE;
+  if (rotary_dim > 0) {
+    if (!positions || !cos_sin_cache) return NVQSA_ERR_NULL_POINTER;
+    if (max_position < 1 || cos_sin_stride < rotary_dim) return NVQSA_ERR_BAD_SHAPE;
+    if (!aligned_to(cos_sin_cache, 2)) return NVQSA_ERR_MISALIGNED;
   }
+  if (!(eps >= 0.0f) || !std::isfinite(eps) || !std::isfinite(norm_weight_offset)) return NVQSA_ERR_BAD_SHAPE;
+  if (key_out && !aligned_to(key_out, 2)) return NVQSA_ERR_MISALIGNED;
+  if (norm_weight && !aligned_to(norm_weight, 4)) return NVQSA_ERR_MISALIGNED;
+
+  WriteParams p;
+  bool go = false;
+  const int st = prepare_write(p, go, key, key_stride_token, key_stride_head, value, value_stride_token,
+                               value_stride_head, key_data, kd_stride_block, kd_stride_token, kd_stride_head,
+                               key_scale, ks_stride_block, ks_stride_token, ks_stride_head, value_data,
+                               vd_stride_block, vd_stride_token, vd_stride_head, value_scale, vs_stride_block,
+                               vs_stride_token, vs_stride_head, slot_mapping, num_tokens, kv_heads, head_dim,
+                               num_blocks, page_size, key_global_scale, value_global_scale);
+  if (st != NVQSA_OK || !go) return st;
+  p.norm_weight = norm_weight;
+  p.norm_offset = norm_weight_offset;
+  p.norm_eps = eps;
+  p.inv_head_dim = 1.0f / (float)head_dim;  // a power of two: exact
+  p.rot_dim = rotary_dim;
+  p.neox = is_neox_style ? 1 : 0;
+  p.positions = positions;
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin_cache);
+  p.cos_sin_stride = cos_sin_stride;
+  p.max_position = max_position;
+  // A lane reads head_dim/32 (NeoX) or head_dim/64 (GPT-J) consecutive cos and sin values starting at a
+  // multiple of that count: one vector load each when the row base and stride keep that alignment.
+  const int run_bytes = 2 * (is_neox_style ? epl : (epl / 2 > 0 ? epl / 2 : 1));
+  p.vec_cs = (run_bytes >= 4 && aligned_to(cos_sin_cache, run_bytes) && (cos_sin_stride * 2) % run_bytes == 0 &&
+              (rotary_dim / 2 * 2) % run_bytes == 0)
+                 ? 1
+                 : 0;
+  p.key_out = static_cast<__nv_bfloat16*>(key_out);
+  p.key_out_stride_token = key_out_stride_token;
+  p.key_out_stride_head = key_out_stride_head;
+  const int ko_bytes = 2 * epl > 16 ? 16 : 2 * epl;
+  p.vec_ko = (key_out && aligned_to(key_out, ko_bytes) && (key_out_stride_token * 2) % ko_bytes == 0 &&
+              (key_out_stride_head * 2) % ko_bytes == 0)
+                 ? 1
+                 : 0;
+  const cudaError_t err = launch_write_any<true>(p, head_dim, as_stream(stream));
   return err == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }

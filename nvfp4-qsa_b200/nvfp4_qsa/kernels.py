@@ -25,6 +25,7 @@ from . import _native
 __all__ = [
     "qsa_sparse_paged_attention_nvfp4",
     "qsa_write_cache_nvfp4",
+    "qsa_norm_rope_write_cache_nvfp4",
     "qsa_sparse_paged_attention_nvfp4_partial",
     "qsa_sparse_paged_attention_fp8",
     "qsa_merge_partials",
@@ -119,6 +120,100 @@ def qsa_write_cache_nvfp4(
             key_data.shape[0], key_data.shape[1],
             float(key_global_scale), float(value_global_scale), _stream_ptr(device))
     _native.check(status, "qsa_write_cache_nvfp4")
+
+
+def qsa_norm_rope_write_cache_nvfp4(
+    key,
+    value,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    slot_mapping,
+    key_global_scale,
+    value_global_scale,
+    positions=None,
+    cos_sin_cache=None,
+    k_norm_weight=None,
+    eps=1e-6,
+    is_neox_style=True,
+    norm_weight_offset=1.0,
+    key_out=None,
+):
+    """k-norm -> RoPE -> NVFP4 quantize -> scatter in one launch, K read once.
+
+    The reference's caller (integration/snapshot/qsa.py:618-667) runs vLLM's
+    GemmaRMSNorm ``k_norm`` and rotary embedding on K and then
+    ``qsa_write_cache_nvfp4``; this takes K straight from the QKV projection.
+    ``k_norm_weight`` is the GemmaRMSNorm weight (``norm_weight_offset=1.0``
+    multiplies by ``1 + w`` in fp32; 0.0 by ``w``) or None for no norm;
+    ``cos_sin_cache`` is the rotary embedding's ``[max_position, rotary_dim]``
+    cos|sin table, cast to bf16 as vLLM's native path casts it to the query
+    dtype; ``positions`` is int64 ``[tokens]``.  The rotation is vLLM's bf16
+    arithmetic bit for bit; the norm is fp32 with a fixed summation order and
+    an IEEE square root and divide (``include/nvfp4_qsa.h``), so it can differ
+    from torch's reduction by one bf16 ulp on rare elements.  ``key_out``
+    (bf16 ``[tokens, kv_heads, head_dim]``) optionally receives the rotated K.
+    Tokens whose position is outside the table are skipped entirely.
+    """
+    _check_write_region(key, key_data, key_scale, slot_mapping)
+    _check_write_region(value, value_data, value_scale, slot_mapping)
+    if key.shape != value.shape:
+        raise ValueError("NVFP4 QSA K and V must have the same shape")
+    if key_data.shape[:3] != value_data.shape[:3]:
+        raise ValueError("NVFP4 QSA K and V caches must share [blocks, page, kv_heads]")
+    if key_data.shape[2] != key.shape[1]:
+        raise ValueError("NVFP4 QSA cache kv_heads does not match K/V")
+    num_tokens, kv_heads, head_dim = key.shape
+    device = key.device
+    rotary_dim, max_position, cs_ptr, cs_stride, pos_ptr = 0, 0, 0, 0, 0
+    if cos_sin_cache is not None:
+        if positions is None:
+            raise ValueError("a rotary embedding needs positions")
+        if cos_sin_cache.dim() != 2 or cos_sin_cache.shape[1] % 2:
+            raise ValueError("cos_sin_cache must be [max_position, rotary_dim]")
+        if positions.dtype != torch.int64 or positions.dim() != 1 or positions.shape[0] != num_tokens:
+            raise ValueError("positions must be an int64 [tokens] vector")
+        cos_sin_cache = cos_sin_cache.to(torch.bfloat16)
+        if cos_sin_cache.stride(-1) != 1:
+            cos_sin_cache = cos_sin_cache.contiguous()
+        positions = positions.contiguous()
+        rotary_dim, max_position = cos_sin_cache.shape[1], cos_sin_cache.shape[0]
+        cs_ptr, cs_stride, pos_ptr = cos_sin_cache.data_ptr(), cos_sin_cache.stride(0), positions.data_ptr()
+        if rotary_dim > head_dim or rotary_dim % (head_dim // 16):
+            raise ValueError(f"rotary_dim {rotary_dim} must be a multiple of head_dim/16 and at most head_dim")
+    w_ptr = 0
+    if k_norm_weight is not None:
+        if k_norm_weight.numel() != head_dim:
+            raise ValueError("k_norm_weight must have head_dim elements")
+        k_norm_weight = k_norm_weight.reshape(head_dim).to(torch.float32).contiguous()
+        w_ptr = k_norm_weight.data_ptr()
+    ko_ptr, ko_st, ko_sh = 0, 0, 0
+    if key_out is not None:
+        if key_out.shape != key.shape or key_out.dtype != torch.bfloat16 or key_out.stride(-1) != 1:
+            raise ValueError("key_out must be bf16 like key with a contiguous last dimension")
+        ko_ptr, ko_st, ko_sh = key_out.data_ptr(), key_out.stride(0), key_out.stride(1)
+    extra = [t for t in (positions, cos_sin_cache, k_norm_weight, key_out) if t is not None]
+    _check_same_device((value, key_data, key_scale, value_data, value_scale, slot_mapping, *extra), device)
+    if num_tokens == 0:
+        return key_out
+    lib = _native.load()
+    with _device_ctx(device):
+        status = lib.nvqsa_norm_rope_write_cache(
+            key.data_ptr(), key.stride(0), key.stride(1),
+            value.data_ptr(), value.stride(0), value.stride(1),
+            key_data.data_ptr(), key_data.stride(0), key_data.stride(1), key_data.stride(2),
+            key_scale.data_ptr(), key_scale.stride(0), key_scale.stride(1), key_scale.stride(2),
+            value_data.data_ptr(), value_data.stride(0), value_data.stride(1), value_data.stride(2),
+            value_scale.data_ptr(), value_scale.stride(0), value_scale.stride(1), value_scale.stride(2),
+            slot_mapping.data_ptr(), num_tokens, kv_heads, head_dim,
+            key_data.shape[0], key_data.shape[1],
+            float(key_global_scale), float(value_global_scale),
+            w_ptr, float(norm_weight_offset), float(eps),
+            pos_ptr, cs_ptr, cs_stride, max_position, rotary_dim, 1 if is_neox_style else 0,
+            ko_ptr, ko_st, ko_sh, _stream_ptr(device))
+    _native.check(status, "qsa_norm_rope_write_cache_nvfp4")
+    return key_out
 
 
 @lru_cache(maxsize=256)

@@ -79,6 +79,39 @@ def prefill_config(seed: int = 3, tokens: int = 8192, blocks: int = 64, page: in
     return kv[0], kv[1], slots
 
 
+def rope_cos_sin(max_position: int, rotary_dim: int, base: float = 1.0e7) -> np.ndarray:
+    """float32 [max_position, rotary_dim] cos | sin table built like vLLM's RotaryEmbedding cache.
+
+    inv_freq = base^(-2i / rotary_dim), angle = position * inv_freq; the writer
+    and vLLM's native path use it cast to bf16.  base 1e7 is Qwen3-Next's rope_theta.
+    """
+    inv = 1.0 / (base ** (np.arange(0, rotary_dim, 2, dtype=np.float64) / rotary_dim))
+    ang = np.outer(np.arange(max_position, dtype=np.float64), inv).astype(np.float32)
+    return np.concatenate([np.cos(ang), np.sin(ang)], axis=1).astype(np.float32)
+
+
+def projection_config(seed: int = 5, tokens: int = 8192, blocks: int = 64, page: int = 3136,
+                      max_position: int = 262144, rotary_dim: int = 64):
+    """K/V as they leave the QKV projection, before k_norm and RoPE (config 3's shape).
+
+    Returns (K bits, V bits, slots int64, positions int64, cos_sin float32
+    [max_position, rotary_dim], k_norm weight float32 [256]).  K rows carry a
+    per-head magnitude spread like un-normalised projections (RMS 0.5 to 8),
+    2 % outliers x32; the GemmaRMSNorm weight is small around 0 (scale 1 + w).
+    """
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((tokens, KV_HEADS, HEAD_DIM), dtype=np.float32)
+    k *= np.exp2(rng.uniform(-1, 3, (tokens, KV_HEADS, 1))).astype(np.float32)
+    k = np.where(rng.random(k.shape) < 0.02, k * 32.0, k).astype(np.float32)
+    v = rng.standard_normal((tokens, KV_HEADS, HEAD_DIM), dtype=np.float32)
+    v = np.where(rng.random(v.shape) < 0.02, v * 32.0, v).astype(np.float32)
+    slots = rng.permutation(blocks * page)[:tokens].astype(np.int64)
+    positions = rng.integers(0, max_position, tokens).astype(np.int64)
+    weight = bf16_bits_to_f32(f32_to_bf16_bits((rng.standard_normal(HEAD_DIM) * 0.1).astype(np.float32)))
+    return (f32_to_bf16_bits(k), f32_to_bf16_bits(v), slots, positions, rope_cos_sin(max_position, rotary_dim),
+            weight)
+
+
 @dataclass
 class DecodeCase:
     """A paged sparse-decode problem (CPU arrays; K/V as bf16 bits)."""

@@ -82,6 +82,8 @@ def _load():
         lib.orc_sparse_attention_fp8.argtypes = [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
                                                  I64, I64, I32, F, F,
                                                  P, I64, P, I64, I64, P, P, I64, I32, I32, P]
+        lib.orc_norm_rope.restype = None
+        lib.orc_norm_rope.argtypes = [P, I64, I64, I64, I32, I32, P, F, F, P, P, I64, I64, I32, I32, P, P]
         lib.orc_set_threads.restype = None
         lib.orc_set_threads.argtypes = [c_int]
         lib.orc_get_threads.restype = c_int
@@ -169,6 +171,32 @@ def write_cache(key_bits: np.ndarray, value_bits: np.ndarray, storage: np.ndarra
         args += [base + off, sb, st, sh]
     _load().orc_write_cache(_ptr(key_bits), kvh * hd, hd, _ptr(value_bits), kvh * hd, hd, *args, _ptr(slots),
                             tokens, kvh, hd, blocks, page, float(key_global_scale), float(value_global_scale))
+
+
+def norm_rope(key_bits: np.ndarray, positions=None, cos_sin_bits=None, weight=None, offset: float = 1.0,
+              eps: float = 1e-6, neox: bool = True):
+    """K-norm + rotary embedding of bf16 K bits [tokens, kv_heads, head_dim] (the writer's fused prologue).
+
+    Returns (bf16 bits [tokens, kv_heads, head_dim], valid [tokens] bool); rows of
+    tokens whose position is outside the table are returned unchanged and not valid.
+    """
+    key_bits = np.ascontiguousarray(key_bits, dtype=np.uint16)
+    tokens, kvh, hd = key_bits.shape
+    out = key_bits.copy()
+    valid = np.ones(tokens, np.uint8)
+    rot, max_pos, cs_ptr, cs_stride, pos_ptr = 0, 0, None, 0, None
+    if cos_sin_bits is not None:
+        cos_sin_bits = np.ascontiguousarray(cos_sin_bits, dtype=np.uint16)
+        positions = np.ascontiguousarray(positions, dtype=np.int64)
+        max_pos, rot = cos_sin_bits.shape
+        cs_ptr, cs_stride, pos_ptr = _ptr(cos_sin_bits), rot, _ptr(positions)
+    w_ptr = None
+    if weight is not None:
+        weight = np.ascontiguousarray(weight, dtype=np.float32)
+        w_ptr = _ptr(weight)
+    _load().orc_norm_rope(_ptr(key_bits), kvh * hd, hd, tokens, kvh, hd, w_ptr, float(offset), float(eps),
+                          pos_ptr, cs_ptr, cs_stride, max_pos, rot, 1 if neox else 0, _ptr(out), _ptr(valid))
+    return out, valid.astype(bool)
 
 
 def sparse_attention(q_bits: np.ndarray, storage: np.ndarray, indices: np.ndarray, block_table: np.ndarray,

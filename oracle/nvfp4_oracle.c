@@ -195,6 +195,81 @@ void orc_write_cache(const uint16_t* key, int64_t key_st, int64_t key_sh, const 
   }
 }
 
+/* bf16 round-to-nearest-even of an fp32 value (NaN -> 0x7fff, the sm_100a
+ * conversion's canonical NaN). */
+static inline uint16_t bf16_rn_bits(float f) {
+  const uint32_t u = bits_from_f32(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fff;
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+static inline float bf16_round(float f) { return bf16_to_f32(bf16_rn_bits(f)); }
+
+/* K-norm + rotary embedding ahead of the writer: the K path of the
+ * reference's caller (integration/snapshot/qsa.py:618-667), vLLM's
+ * GemmaRMSNorm (ir rms_norm: fp32, x * rsqrt(mean(x^2) + eps) * (w + 1), to
+ * bf16) and native rotary embedding (bf16 tensor arithmetic: every product
+ * and sum rounded to bf16), with the summation order and the square root /
+ * divide that nvqsa_norm_rope_write_cache specifies: 32 partial sums, partial
+ * l over elements [l*E, l*E+E) (E = head_dim/32) as (fmaf-sum of the squares
+ * of its even elements, in order) + (the same over its odd elements), then
+ * added pairwise at distances 16, 8, 4, 2, 1; r = 1 / sqrtf(ss / head_dim + eps).
+ * key: bf16 bits with element strides; out: bf16 bits [tokens, kv_heads,
+ * head_dim] contiguous; valid[t] = 0 for a position outside [0, max_pos)
+ * (the token is skipped: its out rows are left as they are). */
+void orc_norm_rope(const uint16_t* key, int64_t st, int64_t sh, int64_t tokens, int32_t kv_heads, int32_t head_dim,
+                   const float* weight, float offset, float eps, const int64_t* positions, const uint16_t* cos_sin,
+                   int64_t cs_stride, int64_t max_pos, int32_t rot, int32_t neox, uint16_t* out, uint8_t* valid) {
+  const int E = head_dim / 32;
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < tokens; ++t) {
+    int64_t pos = 0;
+    if (rot > 0) {
+      pos = positions[t];
+      if (pos < 0 || pos >= max_pos) {
+        valid[t] = 0;
+        continue;
+      }
+    }
+    valid[t] = 1;
+    for (int h = 0; h < kv_heads; ++h) {
+      const uint16_t* src = key + t * st + h * sh;
+      float y[4096];
+      for (int d = 0; d < head_dim; ++d) y[d] = bf16_to_f32(src[d]);
+      if (weight) {
+        float part[32];
+        for (int l = 0; l < 32; ++l) {
+          float even = 0.0f, odd = 0.0f;
+          for (int j = 0; j < E; j += 2) {
+            even = fmaf(y[l * E + j], y[l * E + j], even);
+            odd = fmaf(y[l * E + j + 1], y[l * E + j + 1], odd);
+          }
+          part[l] = even + odd;
+        }
+        for (int m = 16; m >= 1; m >>= 1)
+          for (int l = 0; l < m; ++l) part[l] = part[l] + part[l + m];
+        const float r = 1.0f / sqrtf(part[0] * (1.0f / (float)head_dim) + eps);
+        for (int d = 0; d < head_dim; ++d) y[d] = bf16_round((y[d] * r) * (weight[d] + offset));
+      }
+      if (rot > 0) {
+        const uint16_t* cs = cos_sin + pos * cs_stride;
+        const int half = rot / 2;
+        float o[4096];
+        memcpy(o, y, sizeof(float) * (size_t)head_dim);
+        for (int i = 0; i < half; ++i) {
+          const int i1 = neox ? i : 2 * i, i2 = neox ? i + half : 2 * i + 1;
+          const float c = bf16_to_f32(cs[i]), s = bf16_to_f32(cs[half + i]);
+          const float x1 = y[i1], x2 = y[i2];
+          o[i1] = bf16_round(bf16_round(x1 * c) - bf16_round(x2 * s));
+          o[i2] = bf16_round(bf16_round(x2 * c) + bf16_round(x1 * s));
+        }
+        memcpy(y, o, sizeof(float) * (size_t)head_dim);
+      }
+      uint16_t* dst = out + (t * kv_heads + h) * head_dim;
+      for (int d = 0; d < head_dim; ++d) dst[d] = bf16_rn_bits(y[d]);
+    }
+  }
+}
+
 /* Sparse paged GQA decode attention (kernels.py:168-345 masking; math in
  * float64 as src/qsa_ref.py:12-52).  out: fp32 [rows, query_heads, head_dim]
  * contiguous; lse_out (optional, fp32 [rows, query_heads]) receives each
