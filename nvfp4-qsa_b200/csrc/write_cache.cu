@@ -565,18 +565,14 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : (FUSE ? 3 : 4)) wri
   int h0 = 0;
   uint32_t x[4][NW];  // K h0, V h0, K h1, V h1
   // FUSE state: the lane's norm weights (+ offset), rotation role, the item's position and cos/sin
-  float2 wp[FUSE ? EPL / 2 : 1];
+  __shared__ __align__(16) float wsm[FUSE ? HEAD_DIM : 1];
   uint32_t cw[FUSE ? NW : 1], sw[FUSE ? NW : 1];
   RopeLane rl{};
   bool pos_ok = true;
   if constexpr (FUSE) {
     rl = rope_lane<EPL>(p, lane);
-#pragma unroll
-    for (int j = 0; j < EPL / 2; ++j) {
-      const bool nw = p.norm_weight != nullptr;
-      wp[j] = make_float2(nw ? __fadd_rn(__ldg(p.norm_weight + lane * EPL + 2 * j), p.norm_offset) : 0.0f,
-                          nw ? __fadd_rn(__ldg(p.norm_weight + lane * EPL + 2 * j + 1), p.norm_offset) : 0.0f);
-    }
+    if (p.norm_weight != nullptr)
+      for (int j = threadIdx.x; j < HEAD_DIM; j += blockDim.x) wsm[j] = __fadd_rn(__ldg(p.norm_weight + j), p.norm_offset);
   }
   auto load_item = [&](int64_t w) {
     item_token<RECORD>(w, head_pairs, token, h0);
@@ -617,6 +613,9 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : (FUSE ? 3 : 4)) wri
     if constexpr (FUSE) {
       if (!pos_ok) continue;  // warp-uniform: one position per item
       const bool two = h0 + 1 < p.kv_heads;
+      float2 wp[EPL / 2];
+#pragma unroll
+      for (int j = 0; j < EPL / 2; ++j) wp[j] = reinterpret_cast<const float2*>(wsm + lane * EPL)[j];
       norm_rope_pair<EPL>(p, lane, rl, wp, cw, sw, x[0], x[2]);
       if (p.key_out != nullptr) {
         __nv_bfloat16* ko = p.key_out + token * p.key_out_stride_token + h0 * p.key_out_stride_head + lane * EPL;
