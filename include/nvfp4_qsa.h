@@ -112,11 +112,14 @@ int nvqsa_write_cache(
  *     Elements at or past rotary_dim pass through.
  *   then K (rotated) and V (unchanged) are encoded and scattered exactly as
  *   nvqsa_write_cache does; key_out (optional, bf16 [num_tokens, kv_heads,
- *   head_dim] with element strides) receives the rotated K of every token
- *   whose position is valid, whatever its slot.
+ *   head_dim] with element strides, base and strides aligned to
+ *   min(head_dim/16, 16) bytes, else NVQSA_ERR_MISALIGNED) receives the
+ *   rotated K of every token whose position is valid, whatever its slot.
  * A token whose position is outside [0, max_position) is skipped entirely
  * (no cache bytes, no key_out row).  rotary_dim must be a multiple of
- * head_dim/16 and at most head_dim (NVQSA_ERR_BAD_SHAPE); rotary_dim = 0 and
+ * head_dim/16 and at most head_dim (NVQSA_ERR_BAD_SHAPE); the table's base
+ * and row stride must be aligned to head_dim/16 bytes for NeoX, head_dim/32
+ * for GPT-J (NVQSA_ERR_MISALIGNED; a contiguous table is); rotary_dim = 0 and
  * norm_weight = NULL give the plain writer.  eps must be finite and >= 0.
  * No counterpart entry in the reference (its writer takes K after the norm
  * and rotation).

@@ -71,10 +71,8 @@ struct WriteParams {
   float inv_head_dim;
   int32_t rot_dim;               // 0: no rotation
   int32_t neox;                  // 1: rotate halves (x[i], x[i + rot/2]); 0: GPT-J pairs (x[2i], x[2i+1])
-  int32_t vec_cs;                // 1: cos/sin runs of one lane are aligned for one vector load
   __nv_bfloat16* key_out;        // optional normed, rotated bf16 K [num_tokens, kv_heads, head_dim]
   int64_t key_out_stride_token, key_out_stride_head;
-  int32_t vec_ko;                // 1: key_out rows take one vector store per lane
 };
 
 template <int EPL>
@@ -346,30 +344,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// N consecutive bf16 values (N even) from p into N/2 words; vector loads when aligned.
+// N consecutive bf16 values (N even) from p into N/2 words with vector loads (p aligned to 2N bytes).
 template <int N>
-__device__ __forceinline__ void load_bf16_run(const __nv_bfloat16* p, bool vec, uint32_t (&w)[N / 2]) {
-  if (vec) {
-    if constexpr (N == 2) {
-      w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
-    } else if constexpr (N == 4) {
-      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-      w[0] = v.x;
-      w[1] = v.y;
-    } else {
-#pragma unroll
-      for (int q = 0; q < N / 8; ++q) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + q);
-        w[4 * q] = v.x;
-        w[4 * q + 1] = v.y;
-        w[4 * q + 2] = v.z;
-        w[4 * q + 3] = v.w;
-      }
-    }
+__device__ __forceinline__ void load_bf16_run(const __nv_bfloat16* p, uint32_t (&w)[N / 2]) {
+  if constexpr (N == 2) {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  } else if constexpr (N == 4) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+    w[0] = v.x;
+    w[1] = v.y;
   } else {
-    const unsigned short* s = reinterpret_cast<const unsigned short*>(p);
 #pragma unroll
-    for (int i = 0; i < N / 2; ++i) w[i] = (uint32_t)__ldg(s + 2 * i) | ((uint32_t)__ldg(s + 2 * i + 1) << 16);
+    for (int q = 0; q < N / 8; ++q) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + q);
+      w[4 * q] = v.x;
+      w[4 * q + 1] = v.y;
+      w[4 * q + 2] = v.z;
+      w[4 * q + 3] = v.w;
+    }
   }
 }
 
@@ -403,14 +395,13 @@ __device__ __forceinline__ void load_cos_sin(const WriteParams& p, const RopeLan
                                              uint32_t (&cw)[EPL / 2], uint32_t (&sw)[EPL / 2]) {
   const __nv_bfloat16* row = p.cos_sin + pos * p.cos_sin_stride + rl.cs0;
   const int half = p.rot_dim >> 1;
-  const bool vec = p.vec_cs != 0;
   if (p.neox) {
-    load_bf16_run<EPL>(row, vec, cw);
-    load_bf16_run<EPL>(row + half, vec, sw);
+    load_bf16_run<EPL>(row, cw);
+    load_bf16_run<EPL>(row + half, sw);
   } else if constexpr (EPL >= 4) {
     uint32_t c2[EPL / 4], s2[EPL / 4];
-    load_bf16_run<EPL / 2>(row, vec, c2);
-    load_bf16_run<EPL / 2>(row + half, vec, s2);
+    load_bf16_run<EPL / 2>(row, c2);
+    load_bf16_run<EPL / 2>(row + half, s2);
 #pragma unroll
     for (int i = 0; i < EPL / 4; ++i) {
       cw[i] = c2[i];
@@ -509,25 +500,17 @@ __device__ __forceinline__ void norm_rope_pair(const WriteParams& p, int lane, c
   }
 }
 
+// The EPL bf16 values of one lane with vector stores (p aligned to min(2 EPL, 16) bytes).
 template <int EPL>
-__device__ __forceinline__ void store_bf16_row(__nv_bfloat16* p, bool vec, const uint32_t (&w)[EPL / 2]) {
-  if (vec) {
-    if constexpr (EPL == 2) {
-      *reinterpret_cast<uint32_t*>(p) = w[0];
-    } else if constexpr (EPL == 4) {
-      *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < EPL / 8; ++q)
-        reinterpret_cast<uint4*>(p)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-    }
+__device__ __forceinline__ void store_bf16_row(__nv_bfloat16* p, const uint32_t (&w)[EPL / 2]) {
+  if constexpr (EPL == 2) {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  } else if constexpr (EPL == 4) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
   } else {
-    unsigned short* s = reinterpret_cast<unsigned short*>(p);
 #pragma unroll
-    for (int i = 0; i < EPL / 2; ++i) {
-      s[2 * i] = (unsigned short)(w[i] & 0xffffu);
-      s[2 * i + 1] = (unsigned short)(w[i] >> 16);
-    }
+    for (int q = 0; q < EPL / 8; ++q)
+      reinterpret_cast<uint4*>(p)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
   }
 }
 
@@ -550,7 +533,7 @@ __device__ __forceinline__ void item_token(int64_t w, int head_pairs, int64_t& t
 // rotary embedding first (nvqsa_norm_rope_write_cache); an item whose position
 // is outside [0, max_position) is skipped entirely.
 template <int HEAD_DIM, bool VEC, bool RECORD, bool FUSE>
-__global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : (FUSE ? 3 : 4)) write_cache_kernel(const WriteParams p) {
+__global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kernel(const WriteParams p) {
   constexpr int EPL = HEAD_DIM / 32;
   constexpr int NW = EPL / 2;
   const int lane = threadIdx.x & 31;
@@ -619,8 +602,8 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : (FUSE ? 3 : 4)) wri
       norm_rope_pair<EPL>(p, lane, rl, wp, cw, sw, x[0], x[2]);
       if (p.key_out != nullptr) {
         __nv_bfloat16* ko = p.key_out + token * p.key_out_stride_token + h0 * p.key_out_stride_head + lane * EPL;
-        store_bf16_row<EPL>(ko, p.vec_ko != 0, x[0]);
-        if (two) store_bf16_row<EPL>(ko + p.key_out_stride_head, p.vec_ko != 0, x[2]);
+        store_bf16_row<EPL>(ko, x[0]);
+        if (two) store_bf16_row<EPL>(ko + p.key_out_stride_head, x[2]);
       }
     }
     int64_t block, offset;
@@ -833,7 +816,6 @@ extern "C" int nvqsa_norm_rope_write_cache(
     if (!aligned_to(cos_sin_cache, 2)) return NVQSA_ERR_MISALIGNED;
   }
   if (!(eps >= 0.0f) || !std::isfinite(eps) || !std::isfinite(norm_weight_offset)) return NVQSA_ERR_BAD_SHAPE;
-  if (key_out && !aligned_to(key_out, 2)) return NVQSA_ERR_MISALIGNED;
   if (norm_weight && !aligned_to(norm_weight, 4)) return NVQSA_ERR_MISALIGNED;
 
   WriteParams p;
@@ -856,20 +838,20 @@ extern "C" int nvqsa_norm_rope_write_cache(
   p.cos_sin_stride = cos_sin_stride;
   p.max_position = max_position;
   // A lane reads head_dim/32 (NeoX) or head_dim/64 (GPT-J) consecutive cos and sin values starting at a
-  // multiple of that count: one vector load each when the row base and stride keep that alignment.
-  const int run_bytes = 2 * (is_neox_style ? epl : (epl / 2 > 0 ? epl / 2 : 1));
-  p.vec_cs = (run_bytes >= 4 && aligned_to(cos_sin_cache, run_bytes) && (cos_sin_stride * 2) % run_bytes == 0 &&
-              (rotary_dim / 2 * 2) % run_bytes == 0)
-                 ? 1
-                 : 0;
+  // multiple of that count, with one vector load each: the table base and row stride must keep that
+  // alignment (a contiguous table always does, since rotary_dim is a multiple of head_dim/16).
+  if (rotary_dim > 0) {
+    const int run_bytes = 2 * (is_neox_style ? epl : (epl / 2 > 0 ? epl / 2 : 1));
+    if (!aligned_to(cos_sin_cache, run_bytes) || (cos_sin_stride * 2) % run_bytes != 0) return NVQSA_ERR_MISALIGNED;
+  }
   p.key_out = static_cast<__nv_bfloat16*>(key_out);
   p.key_out_stride_token = key_out_stride_token;
   p.key_out_stride_head = key_out_stride_head;
+  // key_out rows take one vector store per lane: base and strides aligned to min(head_dim/16, 16) bytes
   const int ko_bytes = 2 * epl > 16 ? 16 : 2 * epl;
-  p.vec_ko = (key_out && aligned_to(key_out, ko_bytes) && (key_out_stride_token * 2) % ko_bytes == 0 &&
-              (key_out_stride_head * 2) % ko_bytes == 0)
-                 ? 1
-                 : 0;
+  if (key_out && (!aligned_to(key_out, ko_bytes) || (key_out_stride_token * 2) % ko_bytes != 0 ||
+                  (key_out_stride_head * 2) % ko_bytes != 0))
+    return NVQSA_ERR_MISALIGNED;
   const cudaError_t err = launch_write_any<true>(p, head_dim, as_stream(stream));
   return err == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }

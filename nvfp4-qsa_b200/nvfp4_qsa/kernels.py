@@ -175,7 +175,11 @@ def qsa_norm_rope_write_cache_nvfp4(
         if positions.dtype != torch.int64 or positions.dim() != 1 or positions.shape[0] != num_tokens:
             raise ValueError("positions must be an int64 [tokens] vector")
         cos_sin_cache = cos_sin_cache.to(torch.bfloat16)
-        if cos_sin_cache.stride(-1) != 1:
+        # the kernel reads each lane's cos/sin run with one vector load: a table whose rows are not
+        # aligned to head_dim/16 bytes is made contiguous first
+        run_bytes = head_dim // 16 if is_neox_style else max(head_dim // 32, 2)
+        if (cos_sin_cache.stride(-1) != 1 or (cos_sin_cache.stride(0) * 2) % run_bytes
+                or cos_sin_cache.data_ptr() % run_bytes):
             cos_sin_cache = cos_sin_cache.contiguous()
         positions = positions.contiguous()
         rotary_dim, max_position = cos_sin_cache.shape[1], cos_sin_cache.shape[0]
@@ -189,9 +193,13 @@ def qsa_norm_rope_write_cache_nvfp4(
         k_norm_weight = k_norm_weight.reshape(head_dim).to(torch.float32).contiguous()
         w_ptr = k_norm_weight.data_ptr()
     ko_ptr, ko_st, ko_sh = 0, 0, 0
+    ko_dst = None  # an unaligned key_out view is written through an aligned temporary
     if key_out is not None:
         if key_out.shape != key.shape or key_out.dtype != torch.bfloat16 or key_out.stride(-1) != 1:
             raise ValueError("key_out must be bf16 like key with a contiguous last dimension")
+        ko_bytes = min(head_dim // 16, 16)
+        if key_out.data_ptr() % ko_bytes or (key_out.stride(0) * 2) % ko_bytes or (key_out.stride(1) * 2) % ko_bytes:
+            ko_dst, key_out = key_out, torch.empty(key.shape, dtype=torch.bfloat16, device=key_out.device)
         ko_ptr, ko_st, ko_sh = key_out.data_ptr(), key_out.stride(0), key_out.stride(1)
     extra = [t for t in (positions, cos_sin_cache, k_norm_weight, key_out) if t is not None]
     _check_same_device((value, key_data, key_scale, value_data, value_scale, slot_mapping, *extra), device)
@@ -213,6 +221,14 @@ def qsa_norm_rope_write_cache_nvfp4(
             pos_ptr, cs_ptr, cs_stride, max_position, rotary_dim, 1 if is_neox_style else 0,
             ko_ptr, ko_st, ko_sh, _stream_ptr(device))
     _native.check(status, "qsa_norm_rope_write_cache_nvfp4")
+    if ko_dst is not None:
+        # rows of skipped tokens stay as they were in the caller's tensor
+        if positions is not None and rotary_dim > 0:
+            valid = ((positions >= 0) & (positions < max_position)).view(-1, 1, 1)
+            ko_dst.copy_(torch.where(valid, key_out, ko_dst))  # no host sync
+        else:
+            ko_dst.copy_(key_out)
+        return ko_dst
     return key_out
 
 

@@ -159,7 +159,8 @@ def test_invalid_positions_and_slots_are_skipped():
 
 
 def test_strided_sources_unaligned_tables_and_separate_regions():
-    """K/V as column slices of one qkv tensor, a cos/sin table with an odd row stride (scalar loads),
+    """K/V as column slices of one qkv tensor, a cos/sin table with an odd row stride (the wrapper
+    makes it contiguous),
     key_out a strided view, and separate region tensors (the general-stride path)."""
     hd, kvh, tokens, rot = 256, 2, 150, 64
     kb, vb, slots, pos, cs, w, blocks, page = _inputs(31, tokens, kvh, hd, rot, max_pos=3000)
@@ -248,5 +249,11 @@ def test_fused_writer_rejects_bad_arguments():
                                            0, 0, 0, 0) == 2
     assert lib.nvqsa_norm_rope_write_cache(*args, ps.data_ptr(), csd.data_ptr(), 64, 5000, 24, 1, 0, 0, 0, 0) == 2
     assert lib.nvqsa_norm_rope_write_cache(*args, ps.data_ptr(), 0, 64, 5000, 64, 1, 0, 0, 0, 0) == 1
+    # a table row stride that breaks the vector loads (65 elements): misaligned
+    assert lib.nvqsa_norm_rope_write_cache(*args, ps.data_ptr(), csd.data_ptr(), 65, 4000, 64, 1, 0, 0, 0, 0) == 4
+    # a key_out row start off the 16-byte grid: misaligned (the Python wrapper goes through a temporary)
+    ko = torch.empty(16, 2, 264, dtype=torch.bfloat16, device="cuda")
+    assert lib.nvqsa_norm_rope_write_cache(*args, ps.data_ptr(), csd.data_ptr(), 64, 5000, 64, 1,
+                                           ko.data_ptr() + 8, 528, 264, 0) == 4
     assert lib.nvqsa_norm_rope_write_cache(*args, ps.data_ptr(), csd.data_ptr(), 64, 5000, 64, 1, 0, 0, 0, 0) == 0
     torch.cuda.synchronize()
