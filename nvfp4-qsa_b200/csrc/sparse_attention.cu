@@ -137,7 +137,15 @@ struct __align__(128) SmemT {
 using Smem = SmemT<kRecordBytes, kWarpStages>;      // NVFP4 records
 using SmemFp8 = SmemT<kFp8RecordBytes, kFp8Stages>;  // FP8 K and V rows
 
-__device__ unsigned int g_error_flags;       // bit 0: an mbarrier wait ran out
+__device__ unsigned int g_error_flags;
+
+// Programmatic dependent launch: let the stream's next reader launch as soon as every CTA of this grid has
+// started, and wait (hardware wait, no spin) for the previous grid's completion and memory before touching
+// global memory.  Both are no-ops for a launch without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}       // bit 0: an mbarrier wait ran out
 constexpr unsigned int kErrWaitTimeout = 1u;
 constexpr unsigned int kErrPeerTimeout = 2u;            // bit 1: another GPU's split-KV slot never arrived
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // 2 s
@@ -517,6 +525,7 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
 // mode branches.
 template <int GMODE>
 __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __grid_constant__ AttnParams p) {
+  pdl_enter();
   constexpr bool kFp8 = GMODE == kGatherFp8;
   constexpr int kStages = kFp8 ? kFp8Stages : kWarpStages;
   constexpr int kAh = kStages - 1;
@@ -1492,13 +1501,17 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = sizeof(SmemMtp) + 128;
     cfg.stream = as_stream(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)mp.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2], cluster_attr;
+    cluster_attr.id = cudaLaunchAttributeClusterDimension;
+    cluster_attr.val.clusterDim.x = (unsigned)mp.splits;
+    cluster_attr.val.clusterDim.y = 1;
+    cluster_attr.val.clusterDim.z = 1;
+    int nattr = 0;
+    if (mp.splits > 1) attr[nattr++] = cluster_attr;
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr++].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = mp.splits > 1 ? 1 : 0;
+    cfg.numAttrs = (unsigned)nattr;
     void* args[1] = {&p};
     if (cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(sparse_attention_mtp_kernel), args) != cudaSuccess)
       return NVQSA_ERR_LAUNCH;
@@ -1523,13 +1536,19 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = rk.smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)pl.cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2], cluster_attr;
+  cluster_attr.id = cudaLaunchAttributeClusterDimension;
+  cluster_attr.val.clusterDim.x = (unsigned)pl.cluster;
+  cluster_attr.val.clusterDim.y = 1;
+  cluster_attr.val.clusterDim.z = 1;
+  int nattr = 0;
+  if (pl.cluster > 1) attr[nattr++] = cluster_attr;
+  if (xworld == 0) {  // the cross-GPU exchange keeps plain stream order
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr++].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pl.cluster > 1 ? 1 : 0;
+  cfg.numAttrs = (unsigned)nattr;
   void* args[1] = {&p};
   if (cudaLaunchKernelExC(&cfg, rk.fn, args) != cudaSuccess) return NVQSA_ERR_LAUNCH;
   if (cudaGetLastError() != cudaSuccess) return NVQSA_ERR_LAUNCH;

@@ -67,6 +67,7 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d
 }
 
 __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SmemMtp& sm = *reinterpret_cast<SmemMtp*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
 

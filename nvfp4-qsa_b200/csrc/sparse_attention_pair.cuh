@@ -52,6 +52,7 @@ __device__ __forceinline__ void pair_sync(int pair) {
 
 template <int GMODE>
 __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(const __grid_constant__ AttnParams p) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SmemPair<GMODE>& sm =
       *reinterpret_cast<SmemPair<GMODE>*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));

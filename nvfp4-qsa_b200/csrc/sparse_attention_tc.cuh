@@ -95,6 +95,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 
 template <int GMODE>
 __global__ void __launch_bounds__(kThreads, 3) sparse_attention_tc_kernel(const __grid_constant__ AttnParams p) {
+  pdl_enter();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SmemTc<GMODE>& sm = *reinterpret_cast<SmemTc<GMODE>*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
 
