@@ -635,6 +635,32 @@ def cpu_baseline_read(args, budget_s):
                       f"selected of {ctx} tokens, page {page}) in {secs:.1f} s on {threads} OpenMP threads"}
 
 
+def cpu_baseline_write(fused, budget_s):
+    """C oracle restatement of the writer (fused: k-norm + rotation first) on prefill batches; rank 0 only."""
+    import numpy as np
+    import oracle
+    from nvfp4_qsa import workloads as W
+
+    tokens, blocks, page, rot = 8192, 64, 3136, 64
+    kb, vb, slots, pos, cs, w = W.projection_config(seed=21, tokens=tokens, blocks=blocks, page=page,
+                                                    max_position=65536, rotary_dim=rot)
+    csb = W.f32_to_bf16_bits(cs)
+    storage = np.zeros((blocks, KV_HEADS, page, RECORD), np.uint8)
+    threads = oracle.get_threads()
+    done, secs = 0, 0.0
+    while secs < budget_s or done == 0:
+        t0 = time.perf_counter()
+        k = oracle.norm_rope(kb, pos, csb, w)[0] if fused else kb
+        oracle.write_cache(k, vb, storage, slots)
+        secs += time.perf_counter() - t0
+        done += tokens
+    per_token = KV_HEADS * HEAD_DIM * 2 * 2 + 8 + KV_HEADS * RECORD + ((8 + rot * 2) if fused else 0)
+    what = "k-norm + rotation + writer" if fused else "writer"
+    return {"value": done * per_token / secs / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle/nvfp4_oracle.c {what} over {done} tokens (8,192-token prefill batches into a "
+                      f"64 x 3,136 cache) in {secs:.1f} s on {threads} OpenMP threads"}
+
+
 def main_ours(args):
     import torch
     import torch.distributed as dist
@@ -805,6 +831,8 @@ def main_ours(args):
             result["fp8"] = fp8
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
+            write["cpu_baseline"] = cpu_baseline_write(False, 3.0)
+            fused_write["cpu_baseline"] = cpu_baseline_write(True, 3.0)
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier()
