@@ -73,6 +73,7 @@ struct WriteParams {
   int32_t neox;                  // 1: rotate halves (x[i], x[i + rot/2]); 0: GPT-J pairs (x[2i], x[2i+1])
   __nv_bfloat16* key_out;        // optional normed, rotated bf16 K [num_tokens, kv_heads, head_dim]
   int64_t key_out_stride_token, key_out_stride_head;
+  int32_t group_path;  // head_dim 256, record layout, vector rows, 8-byte aligned records: write_cache_group_kernel
 };
 
 template <int EPL>
@@ -612,6 +613,88 @@ __global__ void __launch_bounds__(256, HEAD_DIM >= 512 ? 2 : 4) write_cache_kern
   }
 }
 
+// head_dim 256, record layout, 16-byte aligned source rows, no norm or rotation: a lane owns one whole
+// 16-element group of one head (lanes 0-15 head h0, lanes 16-31 head h0 + 1) of the K and the V row, so
+// the group amax needs no shuffle, each group's scale is computed once, and a lane stores 8 data bytes
+// and its scale byte per row.  Same arithmetic and bytes as write_cache_kernel.
+__global__ void __launch_bounds__(256, 4) write_cache_group_kernel(const WriteParams p) {
+  const int lane = threadIdx.x & 31;
+  const int hh = lane >> 4, g = lane & 15;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int head_pairs = (p.kv_heads + 1) >> 1;
+  const int64_t items = p.num_tokens * head_pairs;
+  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  __shared__ float out_scale_lut[2][256];
+  __shared__ float quot[2][16];
+
+  int64_t token = 0, slot = -1;
+  int h0 = 0;
+  uint32_t x[2][8];  // K, V: the lane's 16 bf16 values of its head
+  auto load_item = [&](int64_t w) {
+    item_token<true>(w, head_pairs, token, h0);
+    slot = __ldg(p.slots + token);
+    const int h = (h0 + 1 < p.kv_heads) ? h0 + hh : h0;
+    const int64_t off = (int64_t)(int32_t)token * p.src_token32 + (h * p.src_head32 + 16 * g);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(p.src[r] + off));
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(p.src[r] + off) + 1);
+      x[r][0] = a.x; x[r][1] = a.y; x[r][2] = a.z; x[r][3] = a.w;
+      x[r][4] = b.x; x[r][5] = b.y; x[r][6] = b.z; x[r][7] = b.w;
+    }
+  };
+
+  if (w0 < items) load_item(w0);
+  build_out_scale_lut(p, out_scale_lut, quot);
+  __syncthreads();
+  for (int64_t w = w0; w < items; w += warps) {
+    if (w != w0) load_item(w);
+    int64_t block, offset;
+    if (!slot_position<true>(p, slot, block, offset)) continue;
+    const bool mine = hh == 0 || h0 + 1 < p.kv_heads;
+    uint32_t amax_bits[2], sb[2];
+    float os[2];
+    bool rare = !p.plain;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      bool exact;
+      amax_bits[r] = group_amax_bits<16>(x[r]);
+      const float bs = div6_fast(__fmul_rn(p.global_scale[r], __uint_as_float(amax_bits[r])), exact);
+      sb[r] = cvt_e4m3(bs);
+      os[r] = out_scale_lut[r][sb[r]];
+      rare |= !exact;
+    }
+    const bool slow = __any_sync(0xffffffffu, rare);
+    if (slow) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        sb[r] = cvt_e4m3(__fdiv_rn(__fmul_rn(p.global_scale[r], __uint_as_float(amax_bits[r])), 6.0f));
+        os[r] = out_scale_lut[r][sb[r]];
+      }
+    }
+    uint8_t* rec = p.data[0] + ((int64_t)(int32_t)block * p.rec_block32 +
+                                (int32_t)((int32_t)offset * p.rec_token32 + (h0 + hh) * p.rec_head32));
+    uint8_t* drow[2] = {rec, rec + p.off_vd};
+    uint8_t* srow[2] = {rec + p.off_ks, rec + p.off_vs};
+    auto encode_store = [&](auto slow_tag) {
+      constexpr bool SLOW = decltype(slow_tag)::value;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        uint32_t packed[2];
+        encode_row<16, SLOW>(x[r], os[r], p.zero, packed);
+        if (mine) {
+          *reinterpret_cast<uint2*>(drow[r] + 8 * g) = make_uint2(packed[0], packed[1]);
+          srow[r][g] = (uint8_t)sb[r];
+        }
+      }
+    };
+    if (slow)
+      encode_store(std::true_type{});
+    else
+      encode_store(std::false_type{});
+  }
+}
+
 template <int HD, bool VEC, bool RECORD, bool FUSE>
 cudaError_t launch_write_impl(const WriteParams& p, cudaStream_t stream) {
   const int64_t items = p.num_tokens * ((p.kv_heads + 1) / 2);
@@ -634,6 +717,22 @@ cudaError_t launch_write_impl(const WriteParams& p, cudaStream_t stream) {
 
 template <int HD, bool FUSE>
 cudaError_t launch_write(const WriteParams& p, cudaStream_t stream) {
+  if constexpr (HD == 256 && !FUSE) {
+    if (p.group_path) {
+      const int64_t items = p.num_tokens * ((p.kv_heads + 1) / 2);
+      int64_t blocks = (items + 7) / 8;
+      static int per_sm = 0;
+      if (per_sm <= 0 &&
+          (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, write_cache_group_kernel, 256, 0) != cudaSuccess ||
+           per_sm <= 0))
+        per_sm = 2;
+      const int sms = device_sm_count();
+      const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * per_sm;
+      if (blocks > cap) blocks = cap;
+      write_cache_group_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p);
+      return cudaGetLastError();
+    }
+  }
   if (p.record)
     return p.vec_src ? launch_write_impl<HD, true, true, FUSE>(p, stream)
                      : launch_write_impl<HD, false, true, FUSE>(p, stream);
@@ -766,6 +865,10 @@ static int prepare_write(
       vec = false;
   }
   p.vec_src = vec ? 1 : 0;
+  p.group_path = (head_dim == 256 && record && vec && aligned_to(p.data[0], 8) && p.off_ks % 8 == 0 &&
+                  p.off_vd % 8 == 0 && p.rec_block32 % 8 == 0 && p.rec_token32 % 8 == 0 && p.rec_head32 % 8 == 0)
+                     ? 1
+                     : 0;
   go = true;
   return NVQSA_OK;
 }
