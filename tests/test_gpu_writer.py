@@ -315,3 +315,18 @@ def test_negative_products_that_underflow_to_zero_get_code_zero():
         if g == 2.0 ** -20:  # x0 -> +6 (code 7), x1, x2 underflow to -0 -> code 0, x3 rounds to -2^-149 -> 0x8
             assert exp[0, 0, 0, 0] == 0x07 and exp[0, 0, 0, 1] == 0x80 and exp[0, 0, 0, 2] == 0x00
         np.testing.assert_array_equal(st.cpu().numpy(), exp, err_msg=f"g={g}")
+
+
+@pytest.mark.parametrize("kv_heads", [1, 3, 4])
+def test_record_layout_with_other_head_counts(kv_heads):
+    # one head (the upper half-warp idle), an odd count (the last pair has one head) and two pairs per token
+    rng = np.random.default_rng(100 + kv_heads)
+    tokens, blocks, page = 300, 24, 16
+    key = W.f32_to_bf16_bits(rng.standard_normal((tokens, kv_heads, 256), dtype=np.float32) * 3)
+    value = W.f32_to_bf16_bits(rng.standard_normal((tokens, kv_heads, 256), dtype=np.float32))
+    slots = rng.permutation(blocks * page)[:tokens].astype(np.int64)
+    slots[::37] = -1
+    cache = PackedCache(blocks, page_size=page, kv_heads=kv_heads)
+    cache.write(bits_to_cuda(key), bits_to_cuda(value), torch.from_numpy(slots).cuda())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(cache.storage.cpu().numpy(), oracle_storage(key, value, slots, blocks, page))
