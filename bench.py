@@ -72,18 +72,16 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(name):
-    """dram read+write bytes per launch recorded from an ncu capture in profiles/<name>."""
-    p = ROOT / "profiles" / name
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each timed kernel, from one ncu
+# capture of that kernel on its bench workload shape; the command of each capture is given in the ncu
+# summary of that kernel.  Reported as roofline.traffic beside the algorithmic bytes.
+NCU_TRAFFIC = {
+    "read": 157334784,         # sparse_attention_kernel<0>, 96 rows x 2 KV heads x top-2048 (one layer)
+    "mtp": 19768576,           # sparse_attention_mtp_kernel, config 4 (12 x 4 rows, top-2048)
+    "fp8": 210388736,          # sparse_attention_kernel<3>, 96 rows x top-2048, FP8 K/V
+    "write": 16863744,         # write_cache_group_kernel, 8,192 tokens into 64 x 3,136
+    "fused_write": 18579712,   # write_cache_kernel<256,...,FUSE>, 8,192 tokens
+}
 
 
 # ---------------------------------------------------------------------------
@@ -254,7 +252,7 @@ def bench_write(device, steps):
         "roofline": {"bound": "hbm", "achieved": algo / per_launch / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": algo / per_launch / 1e9 / peak, "peak_kind": kind,
                      "algorithmic_bytes_per_launch": algo,
-                     "traffic": profile_traffic("write_cache_prefill.md")},
+                     "traffic": NCU_TRAFFIC["write"]},
         "gpu_launches": launches,
     }
 
@@ -331,7 +329,7 @@ def bench_fused_write(device, steps):
                      "frac": algo / per_launch / 1e9 / peak, "peak_kind": kind,
                      "kernel": "write_cache_kernel<256, true, true, true> (fused k-norm + RoPE, no key_out)",
                      "algorithmic_bytes_per_launch": algo,
-                     "traffic": profile_traffic("write_cache_fused.md")},
+                     "traffic": NCU_TRAFFIC["fused_write"]},
         "gpu_launches": launches + launches_ko,
     }
 
@@ -421,7 +419,7 @@ def bench_mtp(args, device, steps):
                      "frac": algo / g4 / 1e9 / peak, "peak_kind": kind,
                      "kernel": "sparse_attention_mtp_kernel (one layer, splits merged in a cluster)",
                      "algorithmic_bytes_per_launch": algo,
-                     "traffic": profile_traffic("sparse_attention_mtp.md")},
+                     "traffic": NCU_TRAFFIC["mtp"]},
         "gpu_launches": 2 * (max(20, steps) + 5) * layers,
     }
 
@@ -489,7 +487,7 @@ def bench_fp8(args, device, steps):
                      "frac": algo / per_layer / 1e9 / peak, "peak_kind": kind,
                      "kernel": "sparse_attention_kernel<3> (one layer, FP8 rows)",
                      "algorithmic_bytes_per_launch": algo,
-                     "traffic": profile_traffic("sparse_attention_fp8.md")},
+                     "traffic": NCU_TRAFFIC["fp8"]},
         "gpu_launches": (reps + 5) * layers,
     }
 
@@ -497,9 +495,14 @@ def bench_fp8(args, device, steps):
 def bench_split_kv(args, device, world, rank, steps):
     """Config 5b: one 169,984-token sequence, 8,192 selected per row, 12 layers, split-KV over the ranks.
 
-    Rank r holds only its contiguous share of the sequence's pages (nvfp4_qsa.distributed.SplitKV); per layer
-    every rank computes its partial, the ranks all_gather the packed partials over NCCL, and each merges them.
-    At N=1 the same step is the plain single-GPU reader.  Timed eagerly with CUDA events, max over ranks.
+    Every rank draws the same bf16 K/V and selections per layer (shared seeds) and writes only its contiguous
+    share of the sequence's pages (nvfp4_qsa.distributed.SplitKV).  Per layer, one reader launch computes the
+    rank's partial, pushes it into every rank's exchange buffer over NVLink and merges (``attend_fused``); the
+    NCCL variant (``attend``: partial kernel, all_gather of the packed partials, merge kernel) is timed beside
+    it.  At N=1 the step is the plain single-GPU reader.  Both the fused step and the N=1 reader are timed the
+    same two ways at every N: eager launches, and the 12 layers replayed from one CUDA graph.  Device time with
+    CUDA events, max over ranks.  Correctness: every rank's merged outputs of the last timed step are compared
+    with the single-GPU reader over the whole sequence (max-abs and mean-abs over all layers and ranks).
     """
     import torch
     import torch.distributed as dist
@@ -509,29 +512,40 @@ def bench_split_kv(args, device, world, rank, steps):
     ctx, topk, page, layers = args.split_context, args.split_topk, args.page, args.layers
     pages = (ctx + page - 1) // page
     sk = D.SplitKV(pages, page, world, rank)
-    gen = torch.Generator(device=device).manual_seed(4242 + rank)
-    shared = torch.Generator(device=device).manual_seed(777)  # indices and queries identical on every rank
+    shared = torch.Generator(device=device).manual_seed(777)  # K/V, indices and queries identical on every rank
     L = []
     positions = torch.arange(ctx, device=device)
     slots = sk.slot_mapping(positions) if world > 1 else positions
-    for layer in range(layers):
-        nblk = sk.local_blocks if world > 1 else pages
-        storage = torch.zeros(max(nblk, 1), KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+    t2r = torch.zeros(1, device=device, dtype=torch.int32)
+    full_table = torch.arange(pages, device=device, dtype=torch.int32).view(1, -1)
+
+    def regions_of(storage):
         parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
         kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
         vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
-        kv = torch.randn(2, ctx, KV_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
-        kernels.qsa_write_cache_nvfp4(kv[0], kv[1], kd, ks, vd, vs, slots, 1.0, 1.0)
-        del kv
+        return kd, ks, vd, vs
+
+    for layer in range(layers):
+        kv = torch.randn(2, ctx, KV_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=shared)
         idx = torch.rand(1, ctx, device=device, generator=shared).topk(topk, dim=1).indices
         idx = idx.sort(dim=1).values.to(torch.int32).contiguous()
         q = torch.randn(1, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=shared)
-        table = sk.block_table(device) if world > 1 else torch.arange(pages, device=device,
-                                                                      dtype=torch.int32).view(1, -1)
-        L.append(dict(regions=(kd, ks, vd, vs), idx=idx, q=q, table=table, out=torch.empty_like(q),
+        # the single-GPU answer over the whole sequence, for the correctness check
+        whole = torch.zeros(pages, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        kernels.qsa_write_cache_nvfp4(kv[0], kv[1], *regions_of(whole), positions, 1.0, 1.0)
+        ref = torch.empty_like(q)
+        kernels.qsa_sparse_paged_attention_nvfp4(q, *regions_of(whole), 1.0, 1.0, idx, full_table, t2r, ref)
+        del whole
+        nblk = sk.local_blocks if world > 1 else pages
+        storage = torch.zeros(max(nblk, 1), KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        regs = regions_of(storage)
+        kernels.qsa_write_cache_nvfp4(kv[0], kv[1], *regs, slots, 1.0, 1.0)
+        del kv
+        table = sk.block_table(device) if world > 1 else full_table
+        L.append(dict(regions=regs, idx=idx, q=q, table=table, out=torch.empty_like(q), ref=ref,
                       buf=sk.partial_buffer(1, QUERY_HEADS, HEAD_DIM, device)))
-    t2r = torch.zeros(1, device=device, dtype=torch.int32)
     exchange = D.PeerExchange(1, QUERY_HEADS, KV_HEADS) if world > 1 else None
+    assert exchange is None or layers % 2 == 0  # a graph replays the exchange parities of an even layer count
 
     def step():  # fused: the exchange over NVLink peer memory inside the reader kernel
         for d in L:
@@ -547,53 +561,75 @@ def bench_split_kv(args, device, world, rank, steps):
             sk.attend(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], block_table=d["table"],
                       buffer=d["buf"])
 
+    def check():
+        err = torch.zeros(2, device=device, dtype=torch.float64)
+        for d in L:
+            diff = (d["out"].float() - d["ref"].float()).abs()
+            err[0] = torch.maximum(err[0], diff.max().double())
+            err[1] += diff.mean().double() / len(L)
+        if world > 1:
+            dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        return {"max_abs": float(err[0].item()), "mean_abs": float(err[1].item()), "vs": "single-GPU reader"}
+
+    def sync_all():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    n = max(10, steps // 4)
     for _ in range(3):
         step()
-    torch.cuda.synchronize(device)
-    graph = None
-    if world == 1:  # one GPU: replay the 12 layers from a CUDA graph; N > 1 stays eager (NCCL outside graphs)
-        s = torch.cuda.Stream(device)
-        s.wait_stream(torch.cuda.current_stream(device))
-        with torch.cuda.stream(s):
-            step()
-        torch.cuda.current_stream(device).wait_stream(s)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    n = max(10, steps // 4)
-    secs = timed(graph.replay if graph is not None else step, n, device)
+    sync_all()
+    eager_secs = max_over_ranks(timed(step, n, device))
+    sync_all()
+    # the same step captured once and replayed (no NCCL call inside: only the fused reader launches)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream(device).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    sync_all()
+    secs = max_over_ranks(timed(graph.replay, n, device))
+    sync_all()
     del graph
-    nccl_secs = None
+    fused_check = check()
+    nccl_secs, nccl_check = None, None
     if world > 1:
         for _ in range(3):
             step_nccl()
-        torch.cuda.synchronize(device)
-        dist.barrier()
-        nccl_secs = timed(step_nccl, n, device)
-        t = torch.tensor([secs, nccl_secs], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        secs, nccl_secs = float(t[0].item()), float(t[1].item())
-        torch.cuda.synchronize(device)
-        dist.barrier()
+        sync_all()
+        nccl_secs = max_over_ranks(timed(step_nccl, n, device))
+        sync_all()
+        nccl_check = check()
         exchange.close()
     per_layer_bytes = KV_HEADS * topk * RECORD + topk * 4 + 2 * QUERY_HEADS * HEAD_DIM * 2
     return {
         "config": {"workload": f"split-KV decode (config 5b): one sequence of {ctx} tokens, {topk} selected per row, "
                                f"{layers} layers, page {page}, pages split contiguously over {world} GPU(s); "
                                "per layer one reader launch whose last CTA per (row, kv head) pushes its partial "
-                               "into every rank's exchange buffer over NVLink and merges (eager launches); "
-                               "one GPU: the plain reader, 12 layers replayed from a CUDA graph",
+                               "into every rank's exchange buffer over NVLink and merges; one GPU: the plain "
+                               "reader. Timed as a CUDA graph of the 12 layers and as eager launches.",
                    "scaling": "strong"},
         "ms_per_step": secs / n * 1e3,
         "us_per_layer": secs / n / layers * 1e6,
+        "us_per_layer_eager": eager_secs / n / layers * 1e6,
         "gb_per_s": per_layer_bytes * layers * n / secs / 1e9,
         "exchange_bytes_per_rank_per_layer": L[0]["buf"].numel() * 4 if world > 1 else 0,
         "nccl_us_per_layer": nccl_secs / n / layers * 1e6 if nccl_secs is not None else None,
+        "check": fused_check,
+        "nccl_check": nccl_check,
     }
 
 
@@ -777,10 +813,40 @@ def main_ours(args):
         dist.barrier()
     e2e_secs = timed(e2e_graph.replay, e2e_steps, device)
     del e2e_graph
+
+    # Copy-only leg: the same per-layer host<->device copies on the same streams, without the reader: the
+    # ceiling the host copy path alone puts on e2e at this N (all ranks copy at once through host memory).
+    def copy_graph_body():
+        comp = torch.cuda.current_stream(device)
+        copy_in.wait_stream(comp)
+        copy_out.wait_stream(comp)
+        for i, d in enumerate(L):
+            with torch.cuda.stream(copy_in):
+                qd[i].copy_(qh[i], non_blocking=True)
+                idd[i].copy_(ih[i], non_blocking=True)
+            with torch.cuda.stream(copy_out):
+                oh[i].copy_(d["out"], non_blocking=True)
+        comp.wait_stream(copy_in)
+        comp.wait_stream(copy_out)
+
+    copy_graph = torch.cuda.CUDAGraph()
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        copy_graph_body()
+    torch.cuda.current_stream(device).wait_stream(side)
+    with torch.cuda.graph(copy_graph):
+        copy_graph_body()
+    for _ in range(3):
+        copy_graph.replay()
+    torch.cuda.synchronize(device)
     if world > 1:
-        t = torch.tensor([e2e_secs, eager_secs], device=device, dtype=torch.float64)
+        dist.barrier()
+    copy_secs = timed(copy_graph.replay, e2e_steps, device)
+    del copy_graph
+    if world > 1:
+        t = torch.tensor([e2e_secs, eager_secs, copy_secs], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_secs, eager_secs = float(t[0].item()), float(t[1].item())
+        e2e_secs, eager_secs, copy_secs = float(t[0].item()), float(t[1].item()), float(t[2].item())
     e2e_value = world * step_bytes * e2e_steps / e2e_secs / 1e9
     e2e_eager_value = world * step_bytes * e2e_steps / eager_secs / 1e9
 
@@ -811,14 +877,21 @@ def main_ours(args):
                          "peak_kind": kind, "kernel": "sparse_attention_kernel (one layer, split-KV merge fused)",
                          "algorithmic_bytes_per_launch": step_bytes / args.layers,
                          "us_per_launch": per_layer * 1e6,
-                         "traffic": profile_traffic("sparse_attention_decode.md")},
+                         "traffic": NCU_TRAFFIC["read"]},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": qh.numel() * 2 + ih.numel() * 4,
                     "d2h_bytes_per_step": oh.numel() * 2, "ms_per_step": e2e_secs / e2e_steps * 1e3,
                     "api": "nvfp4_qsa.kernels.qsa_sparse_paged_attention_nvfp4 x12 with per-layer pinned copies in "
                            "and out on two copy streams overlapping the other layers' compute, captured from "
                            "those public calls into one CUDA graph replayed per step",
                     "eager_value": e2e_eager_value,
-                    "eager_ms_per_step": eager_secs / e2e_steps * 1e3},
+                    "eager_ms_per_step": eager_secs / e2e_steps * 1e3,
+                    "copy_only": {
+                        "ms_per_step": copy_secs / e2e_steps * 1e3,
+                        "h2d_gb_per_s_per_gpu": (qh.numel() * 2 + ih.numel() * 4) * e2e_steps / copy_secs / 1e9,
+                        "d2h_gb_per_s_per_gpu": oh.numel() * 2 * e2e_steps / copy_secs / 1e9,
+                        "value_ceiling": world * step_bytes * e2e_steps / copy_secs / 1e9,
+                        "what": "the same pinned copies on the same streams without the reader, graph-replayed, "
+                                "max over ranks: the e2e ceiling of the host copy path at this N"}},
             "gpu_launches": args.steps * args.layers * launches_per_layer,
             "write": write,
             "fused_write": fused_write,
@@ -863,17 +936,30 @@ def main_reference(args):
         oracle.write_cache(kv[0].view(np.uint16), kv[1].view(np.uint16), storage,
                            np.arange(s0, s0 + n, dtype=np.int64))
     table = rng.permutation(blocks).astype(np.int32).reshape(nseq, width)
+    # All of the host's cores, whatever OMP_NUM_THREADS the launcher set (torch.distributed.run sets 1).
+    oracle.set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count())
     threads = oracle.get_threads()
-    rows = max(threads, 8)  # one step = a bounded sample of the workload's rows (one layer)
-    q = torch.randn(rows, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
-    idx = np.stack([np.sort(rng.choice(ctx, topk, replace=False)) for _ in range(rows)]).astype(np.int32)
-    t2r = (np.arange(rows) % nseq).astype(np.int32)
-    steps, warmup = min(args.steps, 20), min(args.warmup, 3)
+
+    def sample(rows):
+        q = torch.randn(rows, QUERY_HEADS, HEAD_DIM, generator=gen).to(torch.bfloat16).view(torch.int16).numpy()
+        idx = np.stack([np.sort(rng.choice(ctx, topk, replace=False)) for _ in range(rows)]).astype(np.int32)
+        return q.view(np.uint16), idx, (np.arange(rows) % nseq).astype(np.int32)
+
+    # One step = a bounded sample of the workload's rows (one layer), sized from a calibration call so that
+    # the --warmup W + --steps K steps together take about two minutes of CPU time.
+    cq, cidx, ct2r = sample(threads)
+    t0 = time.perf_counter()
+    oracle.sparse_attention(cq, storage, cidx, table, ct2r)
+    per_row = (time.perf_counter() - t0) / threads
+    budget = min(10.0, 120.0 / max(1, args.steps + args.warmup))
+    rows = max(1, min(4 * threads, int(budget / per_row)))
+    q, idx, t2r = sample(rows)
+    steps, warmup = args.steps, args.warmup
     for _ in range(warmup):
-        oracle.sparse_attention(q.view(np.uint16), storage, idx, table, t2r)
+        oracle.sparse_attention(q, storage, idx, table, t2r)
     t0 = time.perf_counter()
     for _ in range(steps):
-        oracle.sparse_attention(q.view(np.uint16), storage, idx, table, t2r)
+        oracle.sparse_attention(q, storage, idx, table, t2r)
     secs = time.perf_counter() - t0
     value = rows * steps * read_bytes(1, topk, 1) / secs / 1e9
     sample = (f"oracle/nvfp4_oracle.c float64 reader: {rows} decode rows of one layer per step (2 KV heads x {topk} "

@@ -400,7 +400,10 @@ int nvqsa_decode_rows(
  * the need; about splits * rows * query_heads * 1 KiB) are rejected with
  * NVQSA_ERR_SCRATCH_LIMIT before anything is launched.
  * The first call on each device looks up the buffer's device address; make
- * that first call outside any stream capture.  All calls on a device share
+ * that first call outside any stream capture.  The looked-up address is kept
+ * for the process: after a cudaDeviceReset of that device it is stale, so
+ * do not call this entry point on a device that was reset.  All calls on a
+ * device share
  * the one buffer, so calls that may overlap on the GPU (different streams
  * without ordering between them) race and must be serialised by the caller.
  * Nothing in the buffer needs to start at zero: each call zeroes its

@@ -6,6 +6,7 @@
 // reference codec (python/nvfp4_qsa/oracle.py:47-69) bit for bit.
 #pragma once
 
+#include <atomic>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -125,7 +126,10 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 // within one ulp of x/6, the remainder r = x - 6q is exact under FMA, and
 // q + r * RN(1/6) rounds to the correctly rounded quotient (P. Markstein,
 // "Computation of elementary functions on the IBM RISC System/6000
-// processor", IBM J. Res. Dev. 34(1), 1990).  Zeros keep their sign.
+// processor", IBM J. Res. Dev. 34(1), 1990; the same one-FMA correction of a
+// product with a rounded constant is analysed by N. Brisebarre and J.-M.
+// Muller, "Correctly rounded multiplication by arbitrary precision
+// constants", IEEE Trans. Computers 57(2), 2008).  Zeros keep their sign.
 // div6_fast returns that quotient and clears `exact` for NaN, infinities and
 // |x| outside [2^-100, 2^127), which take the IEEE division (div6_rn does it
 // per value; the writer does it once per warp when any lane needs it).
@@ -160,5 +164,23 @@ inline int device_sm_count() {
 }
 
 inline bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Resident blocks per SM of one kernel instantiation, looked up once per device (devices of different kinds
+// in one process keep their own figure).  Atomic entries: concurrent first calls store the same value.
+struct OccupancyCache {
+  static constexpr int kDevices = 64;
+  std::atomic<int> per_sm[kDevices] = {};
+  template <typename Kernel>
+  int get(Kernel kernel, int threads) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevices) return 2;
+    int v = per_sm[dev].load(std::memory_order_relaxed);
+    if (v <= 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, threads, 0) != cudaSuccess || v <= 0) v = 2;
+      per_sm[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+  }
+};
 
 }  // namespace nvqsa

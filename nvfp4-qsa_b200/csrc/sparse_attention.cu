@@ -53,6 +53,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <type_traits>
 
@@ -1818,18 +1819,20 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NVQSA_NOALLOC_S
 namespace {
 // Device address of g_noalloc_scratch, looked up once per device.  In host
 // code the symbol names a host-side stand-in, never the device memory, so only
-// this address may be handed to a kernel.
-void* g_noalloc_scratch_ptr[nvqsa::kMaxDevices] = {};
+// this address may be handed to a kernel.  Atomic entries: host threads that
+// make their first call at the same time all store the same address.  A
+// cudaDeviceReset of the device invalidates the cached address.
+std::atomic<void*> g_noalloc_scratch_ptr[nvqsa::kMaxDevices] = {};
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= nvqsa::kMaxDevices) return NVQSA_ERR_CUDA;
-  if (!g_noalloc_scratch_ptr[dev]) {
-    void* ptr = nullptr;
+  void* ptr = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
+  if (!ptr) {
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return NVQSA_ERR_CUDA;
-    g_noalloc_scratch_ptr[dev] = ptr;
+    g_noalloc_scratch_ptr[dev].store(ptr, std::memory_order_relaxed);
   }
-  *out = g_noalloc_scratch_ptr[dev];
+  *out = ptr;
   return NVQSA_OK;
 }
 }  // namespace

@@ -702,12 +702,8 @@ cudaError_t launch_write_impl(const WriteParams& p, cudaStream_t stream) {
   const int warps_per_block = threads / 32;
   int64_t blocks = (items + warps_per_block - 1) / warps_per_block;
   // One resident wave (occupancy of this instantiation on this device); grid-stride beyond.
-  static int per_sm = 0;
-  if (per_sm <= 0 &&
-      (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, write_cache_kernel<HD, VEC, RECORD, FUSE>, threads,
-                                                     0) != cudaSuccess ||
-       per_sm <= 0))
-    per_sm = 2;
+  static OccupancyCache occ;
+  const int per_sm = occ.get(write_cache_kernel<HD, VEC, RECORD, FUSE>, threads);
   const int sms = device_sm_count();
   const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * per_sm;
   if (blocks > cap) blocks = cap;
@@ -721,11 +717,8 @@ cudaError_t launch_write(const WriteParams& p, cudaStream_t stream) {
     if (p.group_path) {
       const int64_t items = p.num_tokens * ((p.kv_heads + 1) / 2);
       int64_t blocks = (items + 7) / 8;
-      static int per_sm = 0;
-      if (per_sm <= 0 &&
-          (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, write_cache_group_kernel, 256, 0) != cudaSuccess ||
-           per_sm <= 0))
-        per_sm = 2;
+      static OccupancyCache occ;
+      const int per_sm = occ.get(write_cache_group_kernel, 256);
       const int sms = device_sm_count();
       const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * per_sm;
       if (blocks > cap) blocks = cap;

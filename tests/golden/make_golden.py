@@ -1,8 +1,9 @@
 #!/usr/bin/env python3
 """Generate the golden vectors in tests/golden/ from the REFERENCE implementation.
 
-Runs where the reference checkout is available (default /root/reference, or
---reference PATH / $NVQSA_REFERENCE).  It imports the reference's own CPU code:
+Runs where a checkout of the reference is available, named by --reference PATH
+or $NVQSA_REFERENCE (one of the two is required).  It imports the reference's
+own CPU code:
   src/nvfp4_oracle.py  encode / decode / global_scale_for / _round_e2m1_magnitude
   src/qsa_ref.py       qsa_reference (float64 sparse paged GQA)
 and records their outputs on seeded inputs (numpy PCG64, see
@@ -248,8 +249,11 @@ def make_decode_config(ref: Ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("NVQSA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("NVQSA_REFERENCE"),
+                    help="checkout of badbat4560/nvfp4-qsa (default: $NVQSA_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference PATH or NVQSA_REFERENCE")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = Ref(Path(args.reference))
     manifest = {"generator": "tests/golden/make_golden.py", "reference_files": [

@@ -48,20 +48,34 @@ def gpu_attend(storage, query, indices, block_table, t2r, gk=1.0, gv=1.0):
     return out
 
 
-def assert_attention_close(out: torch.Tensor, expected: np.ndarray, what=""):
-    """North-star tolerance on the error beyond the bf16 output's own rounding.
+# Outputs up to this magnitude are "O(1)": the raw absolute gate applies.  Below 8 a bf16 output's own
+# rounding is at most 2^-7 (half an ulp of [4, 8)), inside the 2e-2 gate.
+RAW_GATE_MAX_OUTPUT = 4.0
 
-    The output is bf16 (as in the reference kernel), whose rounding alone is up
-    to 2^-8 |x|: 0.06 for outputs near 30 in the outlier distributions.  That
-    share is discounted before the max-abs 2e-2 / mean-abs 2e-3 gates apply.
+
+def assert_attention_close(out: torch.Tensor, expected: np.ndarray, what=""):
+    """North-star tolerance against the float64 oracle over the same dequantized K/V.
+
+    Raw gate (every case whose outputs are O(1), max |expected| <= 4):
+    max |got - expected| <= 2e-2 and mean |got - expected| <= 2e-3, no discount.
+
+    Outlier gate (only the outlier and heavy-tail distributions, whose outputs
+    reach ~30): a bf16 output near 30 rounds by up to 0.06 on its own, so an
+    absolute 2e-2 cannot hold for any bf16 kernel there.  The same two bounds
+    then apply to the error relative to max(1, |expected|) per element.
+    Returns (max_abs, mean_abs) of the raw differences.
     """
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all(), f"{what}: non-finite output"
     diff = np.abs(got - expected)
-    excess = np.maximum(diff - np.abs(expected) * 2.0 ** -8, 0.0)
-    assert excess.max() <= TOL_MAX_ABS, f"{what}: max_abs {diff.max():.3e} (beyond bf16 rounding {excess.max():.3e})"
-    assert excess.mean() <= TOL_MEAN_ABS, f"{what}: mean_abs {diff.mean():.3e} (beyond bf16 {excess.mean():.3e})"
-    return float(diff.max()), float(diff.mean())
+    if np.abs(expected).max(initial=0.0) <= RAW_GATE_MAX_OUTPUT:
+        assert diff.max(initial=0.0) <= TOL_MAX_ABS, f"{what}: max_abs {diff.max():.3e} (raw gate)"
+        assert diff.mean() <= TOL_MEAN_ABS, f"{what}: mean_abs {diff.mean():.3e} (raw gate)"
+    else:
+        rel = diff / np.maximum(1.0, np.abs(expected))
+        assert rel.max() <= TOL_MAX_ABS, f"{what}: max_rel {rel.max():.3e} (outlier gate; max_abs {diff.max():.3e})"
+        assert rel.mean() <= TOL_MEAN_ABS, f"{what}: mean_rel {rel.mean():.3e} (outlier gate)"
+    return float(diff.max(initial=0.0)), float(diff.mean())
 
 
 def build_case_on_gpu(case: W.DecodeCase, device="cuda"):

@@ -69,6 +69,26 @@ def test_noalloc_matches_regular_entry_point_on_two_calls():
         assert diff <= TOL_MAX_ABS, diff
 
 
+def test_noalloc_back_to_back_on_one_stream():
+    # The serving pattern: two calls with different inputs and outputs queued on one stream with no host
+    # synchronisation between them.  The second call's counter reset and reader launch are stream-ordered
+    # after the first call's kernel, which uses the same static buffer.
+    lib = _native.load()
+    cases = [_storage_case(seed) for seed in (34, 35)]
+    outs = [torch.full_like(c[2], float("nan")) for c in cases]
+    torch.cuda.synchronize()
+    for (case, regions, q, idx, bt, t2r), got in zip(cases, outs):
+        status = _noalloc_call(lib, q, regions, idx, bt, t2r, got)
+        assert status == 0, _native.status_text(status)
+    torch.cuda.synchronize()
+    for (case, regions, q, idx, bt, t2r), got in zip(cases, outs):
+        expected = torch.empty_like(q)
+        kernels.qsa_sparse_paged_attention_nvfp4(q, *regions, 1.0, 1.0, idx, bt, t2r, expected)
+        torch.cuda.synchronize()
+        assert torch.isfinite(got.float()).all()
+        assert (got.float() - expected.float()).abs().max().item() <= TOL_MAX_ABS
+
+
 def test_noalloc_rejects_problems_beyond_its_buffer():
     lib = _native.load()
     case, regions, q, idx, bt, t2r = _storage_case(33)
