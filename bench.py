@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--skip-split", action="store_true", help="skip the split-KV section")
     ap.add_argument("--skip-mtp", action="store_true", help="skip the MTP (config 4) section")
     ap.add_argument("--skip-fp8", action="store_true", help="skip the FP8 sibling-reader section")
+    ap.add_argument("--skip-bf16", action="store_true", help="skip the BF16 sibling-reader section")
     return ap.parse_args()
 
 
@@ -492,6 +493,71 @@ def bench_fp8(args, device, steps):
     }
 
 
+def bench_bf16(args, device, steps):
+    """BF16 sibling reader (integration/snapshot/qsa.py:352-366) on the config-5a row shape.
+
+    96 rows x 2 KV heads x top-2,048 over bf16 caches laid out as vLLM allocates them, [blocks, 2, page, 512]
+    split into K and V views (context 16,384 per layer so that 12 layers fit beside the NVFP4 workload:
+    403 MB of selected rows per layer, more than L2), 12 layers replayed from one CUDA graph per step.  Bytes:
+    the selected K and V rows (1,024 B per row and KV head), indices, q and out.
+    """
+    import torch
+    from nvfp4_qsa import kernels
+
+    seqs, ctx, page, layers, topk = args.seqs, 16384, args.page, args.layers, args.topk
+    width = (ctx + page - 1) // page
+    blocks = seqs * width
+    gen = torch.Generator(device=device).manual_seed(9)
+    L = []
+    for layer in range(layers):
+        storage = torch.randn(blocks, KV_HEADS, page, 2 * HEAD_DIM, device=device, dtype=torch.bfloat16,
+                              generator=gen)
+        cache = storage.transpose(1, 2)
+        table = torch.randperm(blocks, device=device, generator=gen).to(torch.int32).view(seqs, width).contiguous()
+        idx = torch.rand(seqs, ctx, device=device, generator=gen).topk(topk, dim=1).indices
+        idx = idx.sort(dim=1).values.to(torch.int32).contiguous()
+        q = torch.randn(seqs, QUERY_HEADS, HEAD_DIM, device=device, dtype=torch.bfloat16, generator=gen)
+        L.append(dict(storage=storage, kc=cache[..., :HEAD_DIM], vc=cache[..., HEAD_DIM:], table=table, idx=idx,
+                      q=q, out=torch.empty_like(q)))
+    t2r = torch.arange(seqs, device=device, dtype=torch.int32)
+    torch.cuda.synchronize(device)
+
+    def step():
+        for d in L:
+            kernels.qsa_sparse_paged_attention(d["q"], d["kc"], d["vc"], d["idx"], d["table"], t2r, d["out"])
+
+    step()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    reps = max(20, steps)
+    per_layer = timed(graph.replay, reps, device) / reps / layers
+    del graph
+    algo = seqs * KV_HEADS * topk * 4 * HEAD_DIM + seqs * topk * 4 + 2 * seqs * QUERY_HEADS * HEAD_DIM * 2
+    peak, kind = measured_peaks()
+    return {
+        "config": {"workload": f"BF16 sibling reader on the config-5a row shape: {seqs} rows x 2 KV heads x "
+                               f"top-{topk} of {ctx} tokens, bf16 caches [blocks, 2, page, 512] (K and V views), "
+                               f"page {page}, {layers} layers (one cache each) in one CUDA graph per step",
+                   "l2": f"inputs larger than L2: {seqs * KV_HEADS * topk * 1024 / 1e6:.0f} MB of selected rows per layer"},
+        "us_per_layer": per_layer * 1e6,
+        "gb_per_s": algo / per_layer / 1e9,
+        "roofline": {"bound": "hbm", "achieved": algo / per_layer / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": algo / per_layer / 1e9 / peak, "peak_kind": kind,
+                     "kernel": "sparse_attention_bf16_kernel (one layer)",
+                     "algorithmic_bytes_per_launch": algo,
+                     "traffic": NCU_TRAFFIC.get("bf16")},
+        "gpu_launches": (reps + 5) * layers,
+    }
+
+
 def bench_split_kv(args, device, world, rank, steps):
     """Config 5b: one 169,984-token sequence, 8,192 selected per row, 12 layers, split-KV over the ranks.
 
@@ -856,6 +922,7 @@ def main_ours(args):
     # config 4 and the FP8 sibling reader are single-GPU side measurements: one GPU runs only
     mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
     fp8 = bench_fp8(args, device, args.steps) if world == 1 and not args.skip_fp8 else None
+    bf16 = bench_bf16(args, device, args.steps) if world == 1 and not args.skip_bf16 else None
     del graph
     result = None
     if rank == 0:
@@ -902,6 +969,8 @@ def main_ours(args):
             result["mtp"] = mtp
         if fp8 is not None:
             result["fp8"] = fp8
+        if bf16 is not None:
+            result["bf16"] = bf16
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
             write["cpu_baseline"] = cpu_baseline_write(False, 3.0)

@@ -252,6 +252,38 @@ int nvqsa_sparse_attention_fp8(
     void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * BF16 sibling reader: the same sparse paged decode attention over the bf16
+ * main cache (no quantisation).  Replaces vLLM's qsa_sparse_paged_attention
+ * that the reference calls in the third branch of forward_qsa
+ * (integration/snapshot/qsa.py:352-366); its arithmetic is the FP8 harness
+ * kernel's without the dequantisation (src/qsa_fp8_harness.py:42-208, scale
+ * head_dim^-0.5, P cast to bf16 before P V).
+ *
+ * key_cache, value_cache : bf16 [num_blocks, page_size, kv_heads, head_dim]
+ *                          with BYTE strides (block, token, head), innermost
+ *                          stride 1 element; 16-byte aligned rows and strides
+ *                          (vLLM's views of a [blocks, kv_heads, page, 2*256]
+ *                          bf16 cache qualify).
+ * Masking, output and split-KV rules as nvqsa_sparse_attention; the workspace
+ * size comes from nvqsa_sparse_attention_bf16_workspace_size.
+ */
+int nvqsa_sparse_attention_bf16(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_cache, int64_t kc_stride_block, int64_t kc_stride_token, int64_t kc_stride_head,
+    const void* value_cache, int64_t vc_stride_block, int64_t vc_stride_token, int64_t vc_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes nvqsa_sparse_attention_bf16 needs for this shape on the current device. */
+int nvqsa_sparse_attention_bf16_workspace_size(int64_t rows, int32_t query_heads, int32_t kv_heads, int32_t head_dim,
+                                               int64_t topk, size_t* workspace_bytes);
+
+/*
  * Partial (un-merged) variant for split-KV across devices: writes, for every
  * (row, query head), the softmax-normalized output of the selections this
  * device holds, already divided by value_global_scale, and its base-2

@@ -77,6 +77,7 @@ constexpr int kStageBytes = kTile * kRecordBytes;
 // FP8 sibling reader (gather mode 3): float8_e4m3 K and V rows of 256 bytes from two caches, staged as
 // K | V | 16 bytes of skew per token (the skew keeps the per-lane K and V reads bank-conflict free).
 constexpr int kGatherFp8 = 3;
+constexpr int kGatherBf16 = 4;   // BF16 sibling reader: bf16 K and V rows of 512 bytes (sparse_attention_bf16_kernel)
 constexpr int kFp8RecordBytes = 528;
 constexpr int kFp8Stages = 2;
 constexpr float kMaskedScore = -1.0e20f;
@@ -1144,7 +1145,7 @@ __global__ void __launch_bounds__(256) merge_kernel(MergeArgs a, int64_t rows, i
   merge_item(a, row, (int)(w - row * query_heads), w, lane);
 }
 
-#include "sparse_attention_tc.cuh"
+#include "sparse_attention_bf16.cuh"
 #include "sparse_attention_pair.cuh"
 #include "sparse_attention_mtp.cuh"
 
@@ -1202,10 +1203,8 @@ bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
   return true;
 }
 
-// The reader kernel of a launch: P.V on tcgen05 (sparse_attention_tc_kernel) or on
-// mma.sync (sparse_attention_kernel), per gather mode, with its shared-memory size.
-constexpr bool kTensorMemoryReader = false;
 constexpr int kReaderCtasPerSm = 3;  // resident CTAs per SM of the full-width reader (registers and shared memory)
+constexpr int kBf16CtasPerSm = 2;    // resident CTAs per SM of the BF16 sibling reader (shared memory)
 
 struct Plan {
   int splits;
@@ -1219,7 +1218,7 @@ constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
 // batch with at least one (row, kv head) unit per SM keeps the fewest splits
 // the 1024-selection CTA limit allows; batches with fewer units than SMs are
 // split until every SM has a CTA, down to one 32-position chunk per CTA.
-Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
+Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms, int ctas_per_sm = kReaderCtasPerSm) {
   Plan pl;
   const int64_t units = rows * kv_heads;
   const int64_t chunks = topk > 0 ? (topk + kChunk - 1) / kChunk : 1;
@@ -1232,7 +1231,7 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms) {
     // Up to as many splits as keep every SM's resident CTAs busy in one wave, rounded down to a power of two:
     // clusters of 3 do not pack onto the GPCs (measured on B200 at 148 units: 3 splits in clusters of 3
     // 71.5 us, 2 splits 46.3 us per 2,048-selection layer).
-    int64_t fill = (kReaderCtasPerSm * sm_count) / units;
+    int64_t fill = (ctas_per_sm * sm_count) / units;
     while (fill & (fill - 1)) fill &= fill - 1;
     if (fill > splits) splits = fill;
   }
@@ -1298,25 +1297,21 @@ size_t workspace_for(const Plan& pl, int64_t rows, int query_heads, int kv_heads
 constexpr int kMaxDevices = 64;
 bool smem_configured[kMaxDevices] = {};
 
+// The reader kernel of a launch (full-width, warp-pair, FP8 or BF16 sibling) with its shared-memory size.
 struct ReaderKernel {
   const void* fn;
   size_t smem;  // + slack for the 128-byte alignment of the base
 };
 ReaderKernel reader_kernel(int gather_mode, bool pair) {
+  if (gather_mode == kGatherBf16)
+    return {reinterpret_cast<const void*>(sparse_attention_bf16_kernel), sizeof(SmemBf) + 128};
   if (gather_mode == kGatherFp8)
     return {reinterpret_cast<const void*>(sparse_attention_kernel<kGatherFp8>), sizeof(SmemFp8) + 128};
-  if (pair && !kTensorMemoryReader) {
+  if (pair) {
     switch (gather_mode) {
       case 0: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<0>), sizeof(SmemPair<0>) + 128};
       case 1: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<1>), sizeof(SmemPair<1>) + 128};
       default: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<2>), sizeof(SmemPair<2>) + 128};
-    }
-  }
-  if (kTensorMemoryReader) {
-    switch (gather_mode) {
-      case 0: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<0>), sizeof(SmemTc<0>) + 128};
-      case 1: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<1>), sizeof(SmemTc<1>) + 128};
-      default: return {reinterpret_cast<const void*>(sparse_attention_tc_kernel<2>), sizeof(SmemTc<2>) + 128};
     }
   }
   switch (gather_mode) {
@@ -1331,8 +1326,10 @@ int configure_smem() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    for (int k = 0; k < 7; ++k) {
-      const ReaderKernel rk = k == 6 ? reader_kernel(kGatherFp8, false) : reader_kernel(k % 3, k >= 3);
+    for (int k = 0; k < 8; ++k) {
+      const ReaderKernel rk = k == 7   ? reader_kernel(kGatherBf16, false)
+                              : k == 6 ? reader_kernel(kGatherFp8, false)
+                                       : reader_kernel(k % 3, k >= 3);
       if (cudaFuncSetAttribute(rk.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rk.smem) != cudaSuccess ||
           cudaFuncSetAttribute(rk.fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
         return NVQSA_ERR_CUDA;
@@ -1357,7 +1354,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
                   float* partial_out, float* partial_lse, int64_t rows, int32_t query_heads, int32_t head_dim,
                   void* workspace, size_t workspace_bytes, void* stream, float* const* xpeers = nullptr,
                   int32_t xworld = 0, int32_t xrank = 0, int32_t xparity = 0, int32_t rows_per_group = 1,
-                  bool fp8 = false) {
+                  bool fp8 = false, bool bf16 = false) {
   if (rows < 0 || topk < 0 || kv_heads < 1 || query_heads < 1 || num_blocks < 0 || page_size < 1 ||
       num_requests < 0 || table_width < 0)
     return NVQSA_ERR_BAD_SHAPE;
@@ -1387,9 +1384,10 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   const int sms = device_sm_count();
   if (sms <= 0) return NVQSA_ERR_CUDA;
   if (rows_per_group < 1 || rows_per_group > kMtpRows) return NVQSA_ERR_BAD_SHAPE;
-  const MtpPlan mp = fp8 ? MtpPlan{false, 1, 0} : make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
-  Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms);
-  if (fp8) pl.pair = false;  // the FP8 rows run on the full-width reader only
+  const bool sibling = fp8 || bf16;
+  const MtpPlan mp = sibling ? MtpPlan{false, 1, 0} : make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
+  Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms, bf16 ? kBf16CtasPerSm : kReaderCtasPerSm);
+  if (sibling) pl.pair = false;  // the FP8 and BF16 rows run on their full-width readers only
   const Workspace wl = mp.use ? Workspace{0, 0, 0} : workspace_layout(pl, rows, query_heads, kv_heads);
   const size_t need = wl.bytes;
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned_to(workspace, 16))) return NVQSA_ERR_WORKSPACE;
@@ -1438,6 +1436,14 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     p.total_rows = 0;
     p.score_scale = (float)(0.0625 * 1.4426950408889634) * key_global_scale;
     p.inv_value_scale = value_global_scale;
+  }
+  if (bf16) {
+    // BF16 sibling reader (integration/snapshot/qsa.py:352-366): plain bf16 K and V, scale head_dim^-0.5;
+    // regions 0 and 2 are the K and V caches.
+    p.gather_mode = kGatherBf16;
+    p.total_rows = 0;
+    p.score_scale = (float)(0.0625 * 1.4426950408889634);
+    p.inv_value_scale = 1.0f;
   }
   p.indices = logical_indices;
   p.topk = topk;
@@ -1656,6 +1662,43 @@ extern "C" int nvqsa_sparse_attention_fp8(
                        v_scale, logical_indices, topk, block_table, num_requests, table_width, token_to_request,
                        output, o_stride_row, o_stride_head, nullptr, nullptr, rows, query_heads, head_dim, workspace,
                        workspace_bytes, stream, nullptr, 0, 0, 0, 1, true);
+}
+
+extern "C" int nvqsa_sparse_attention_bf16(
+    const void* query, int64_t q_stride_row, int64_t q_stride_head,
+    const void* key_cache, int64_t kc_stride_block, int64_t kc_stride_token, int64_t kc_stride_head,
+    const void* value_cache, int64_t vc_stride_block, int64_t vc_stride_token, int64_t vc_stride_head,
+    int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+    const int32_t* logical_indices, int64_t topk,
+    const int32_t* block_table, int64_t num_requests, int64_t table_width,
+    const int32_t* token_to_request,
+    void* output, int64_t o_stride_row, int64_t o_stride_head,
+    int64_t rows, int32_t query_heads, int32_t head_dim,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  const void* region[4] = {key_cache, key_cache, value_cache, value_cache};
+  const int64_t strides[4][3] = {{kc_stride_block, kc_stride_token, kc_stride_head},
+                                 {kc_stride_block, kc_stride_token, kc_stride_head},
+                                 {vc_stride_block, vc_stride_token, vc_stride_head},
+                                 {vc_stride_block, vc_stride_token, vc_stride_head}};
+  return run_attention(query, q_stride_row, q_stride_head, region, strides, num_blocks, page_size, kv_heads, 1.0f,
+                       1.0f, logical_indices, topk, block_table, num_requests, table_width, token_to_request, output,
+                       o_stride_row, o_stride_head, nullptr, nullptr, rows, query_heads, head_dim, workspace,
+                       workspace_bytes, stream, nullptr, 0, 0, 0, 1, false, true);
+}
+
+extern "C" int nvqsa_sparse_attention_bf16_workspace_size(int64_t rows, int32_t query_heads, int32_t kv_heads,
+                                                         int32_t head_dim, int64_t topk, size_t* workspace_bytes) {
+  if (!workspace_bytes) return NVQSA_ERR_NULL_POINTER;
+  *workspace_bytes = 0;
+  if (rows < 0 || topk < 0 || kv_heads < 1 || query_heads < 1 || query_heads % kv_heads) return NVQSA_ERR_BAD_SHAPE;
+  if (head_dim != kHeadDim) return NVQSA_ERR_HEAD_DIM;
+  if (rows == 0) return NVQSA_OK;
+  const int sms = device_sm_count();
+  if (sms <= 0) return NVQSA_ERR_CUDA;
+  Plan pl = make_plan(rows, kv_heads, topk, sms, kBf16CtasPerSm);
+  pl.pair = false;
+  *workspace_bytes = workspace_for(pl, rows, query_heads, kv_heads);
+  return NVQSA_OK;
 }
 
 extern "C" int nvqsa_sparse_attention_partial(

@@ -98,6 +98,18 @@ _SIGNATURES = {
         _P, _I64, _I64,
         _I64, _I32, _I32,
         _P, c_size_t, _P]),
+    "nvqsa_sparse_attention_bf16": (c_int, [
+        _P, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _I64, _I64, _I32,
+        _P, _I64,
+        _P, _I64, _I64,
+        _P,
+        _P, _I64, _I64,
+        _I64, _I32, _I32,
+        _P, c_size_t, _P]),
+    "nvqsa_sparse_attention_bf16_workspace_size": (c_int, [_I64, _I32, _I32, _I32, _I64, POINTER(c_size_t)]),
     "nvqsa_sparse_attention_partial": (c_int, [
         _P, _I64, _I64,
         _P, _I64, _I64, _I64,

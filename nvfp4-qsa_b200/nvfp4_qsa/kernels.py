@@ -28,6 +28,7 @@ __all__ = [
     "qsa_norm_rope_write_cache_nvfp4",
     "qsa_sparse_paged_attention_nvfp4_partial",
     "qsa_sparse_paged_attention_fp8",
+    "qsa_sparse_paged_attention",
     "qsa_merge_partials",
     "qsa_merge_partials_strided",
     "qsa_sparse_paged_attention_nvfp4_split_kv",
@@ -402,6 +403,70 @@ def qsa_sparse_paged_attention_fp8(
             workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
     _native.check(status, "qsa_sparse_paged_attention_fp8")
     return out
+
+
+def qsa_sparse_paged_attention(
+    query,
+    key_cache,
+    value_cache,
+    logical_indices,
+    block_table,
+    token_to_req,
+    output=None,
+):
+    """BF16 sibling reader: QSA sparse paged decode over the bf16 main cache; returns ``output``.
+
+    Replaces vLLM's ``qsa_sparse_paged_attention`` that the reference calls in the BF16 branch of
+    ``forward_qsa`` (integration/snapshot/qsa.py:352-366).  ``key_cache`` / ``value_cache`` are bf16
+    [blocks, page, kv_heads, head_dim] views (last dim contiguous; vLLM's split of a
+    [blocks, kv_heads, page, 2 * head_dim] cache), scale head_dim^-0.5.  Masking and output rules as
+    ``qsa_sparse_paged_attention_nvfp4``; ``output`` defaults to a new bf16 tensor shaped like ``query``.
+    """
+    if query.dim() != 3 or query.dtype != torch.bfloat16 or query.stride(-1) != 1:
+        raise NotImplementedError("QSA requires a BF16 query [rows, query_heads, head_dim] with contiguous last dim")
+    for t in (key_cache, value_cache):
+        if t.dtype != torch.bfloat16:
+            raise NotImplementedError("QSA requires BF16 Q/K/V")
+        if t.dim() != 4 or t.stride(-1) != 1:
+            raise ValueError("QSA BF16 caches must be [blocks, page, kv_heads, head_dim] with contiguous last dim")
+    if key_cache.shape != value_cache.shape or key_cache.shape[-1] != query.shape[2]:
+        raise ValueError("QSA BF16 K/V caches must match each other and the query head_dim")
+    for t in (logical_indices, block_table, token_to_req):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("QSA metadata must be contiguous int32")
+    if output is None:
+        output = torch.empty_like(query)
+    if output.shape != query.shape or output.dtype != torch.bfloat16 or output.stride(-1) != 1:
+        raise ValueError("QSA output must be bf16 shaped like query with contiguous last dim")
+    device = query.device
+    _check_same_device((key_cache, value_cache, logical_indices, block_table, token_to_req, output), device)
+    rows, query_heads, head_dim = query.shape
+    if rows == 0:
+        return output
+    topk = logical_indices.shape[1]
+    kv_heads = key_cache.shape[2]
+    lib = _native.load()
+    el = key_cache.element_size()
+    with _device_ctx(device):
+        size = ctypes.c_size_t()
+        _native.check(lib.nvqsa_sparse_attention_bf16_workspace_size(rows, query_heads, kv_heads, head_dim, topk,
+                                                                     ctypes.byref(size)), "workspace size")
+        ws_bytes = size.value
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+        status = lib.nvqsa_sparse_attention_bf16(
+            query.data_ptr(), query.stride(0), query.stride(1),
+            key_cache.data_ptr(), key_cache.stride(0) * el, key_cache.stride(1) * el, key_cache.stride(2) * el,
+            value_cache.data_ptr(), value_cache.stride(0) * el, value_cache.stride(1) * el,
+            value_cache.stride(2) * el,
+            key_cache.shape[0], key_cache.shape[1], kv_heads,
+            logical_indices.data_ptr(), topk,
+            block_table.data_ptr(), block_table.shape[0], block_table.shape[1],
+            token_to_req.data_ptr(),
+            output.data_ptr(), output.stride(0), output.stride(1),
+            rows, query_heads, head_dim,
+            workspace.data_ptr() if workspace is not None else None, ws_bytes, _stream_ptr(device))
+    _native.check(status, "qsa_sparse_paged_attention")
+    return output
 
 
 def qsa_sparse_paged_attention_nvfp4_partial(

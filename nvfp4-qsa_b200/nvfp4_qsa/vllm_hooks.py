@@ -96,13 +96,32 @@ def split_nvfp4_kv_cache(kv_cache: torch.Tensor, head_size: int):
     return key_data, key_scale, value_data, value_scale
 
 
+def canonicalize_singleton_dim_strides(t: torch.Tensor) -> torch.Tensor:
+    """The same view with every size-1 dim given the stride it would have in a dense layout.
+
+    A size-1 dim is never stepped over, so its stride carries no information, but the readers check every
+    stride for 16-byte alignment; vLLM applies the same normalisation before its QSA kernels
+    (snapshot/qsa.py:323-325).
+    """
+    strides = list(t.stride())
+    inner = 1
+    for i in range(t.dim() - 1, -1, -1):
+        if t.shape[i] == 1:
+            strides[i] = inner
+        inner = strides[i] * t.shape[i]
+    return t.as_strided(t.shape, strides)
+
+
 class QSANVFP4AttentionHooks:
-    """Mixin for a vLLM attention impl whose main KV cache is NVFP4.
+    """Mixin for a vLLM attention impl of the QSA backend (snapshot/qsa.py:263-366).
 
     Expects the impl attributes vLLM sets: ``head_size``, ``alibi_slopes``,
     ``sinks`` and ``sliding_window``; the layer carries ``topk_indices_buffer``
-    (int32 [max_tokens, topk], filled by the QSA indexer) and the fixed global
-    scales ``_qsa_nvfp4_k_global`` / ``_qsa_nvfp4_v_global`` (1.0 when absent).
+    (int32 [max_tokens, topk], filled by the QSA indexer).  The main cache is
+    NVFP4 unless the impl sets ``_qsa_kv_nvfp4 = False`` (fixed global scales
+    ``_qsa_nvfp4_k_global`` / ``_qsa_nvfp4_v_global``, 1.0 when absent); then
+    a uint8 cache with ``_qsa_kv_fp8`` goes to the FP8 sibling reader (layer
+    ``_k_scale_float`` / ``_v_scale_float``) and a bf16 cache to the BF16 one.
     """
 
     def forward_qsa(
@@ -136,15 +155,48 @@ class QSANVFP4AttentionHooks:
             raise RuntimeError("QSA owner did not provide its top-k buffer")
         logical_indices = topk_buffer[:num_tokens]
         token_to_req = token_to_req[:num_tokens]
-        key_data, key_scale, value_data, value_scale = split_nvfp4_kv_cache(kv_cache, self.head_size)
-        kernels.qsa_sparse_paged_attention_nvfp4(
+        if getattr(self, "_qsa_kv_nvfp4", True):
+            key_data, key_scale, value_data, value_scale = split_nvfp4_kv_cache(kv_cache, self.head_size)
+            kernels.qsa_sparse_paged_attention_nvfp4(
+                query[:num_tokens],
+                key_data,
+                key_scale,
+                value_data,
+                value_scale,
+                float(getattr(layer, "_qsa_nvfp4_k_global", 1.0)),
+                float(getattr(layer, "_qsa_nvfp4_v_global", 1.0)),
+                logical_indices,
+                attn_metadata.block_table,
+                token_to_req,
+                output[:num_tokens],
+            )
+            return output
+
+        # The BF16 and FP8 main caches (snapshot/qsa.py:323-366): K and V halves of the last dim.
+        key_cache, value_cache = kv_cache.transpose(1, 2).split(self.head_size, dim=-1)
+        key_cache = canonicalize_singleton_dim_strides(key_cache)
+        value_cache = canonicalize_singleton_dim_strides(value_cache)
+        if getattr(self, "_qsa_kv_fp8", False) and key_cache.dtype == torch.uint8:
+            if query.dtype != torch.bfloat16:
+                raise NotImplementedError("Qwen3.8-Flash-Next QSA requires a BF16 query")
+            kernels.qsa_sparse_paged_attention_fp8(
+                query[:num_tokens],
+                key_cache.view(torch.float8_e4m3fn),
+                value_cache.view(torch.float8_e4m3fn),
+                float(getattr(layer, "_k_scale_float", 1.0)),
+                float(getattr(layer, "_v_scale_float", 1.0)),
+                logical_indices,
+                attn_metadata.block_table,
+                token_to_req,
+                output[:num_tokens],
+            )
+            return output
+        if key_cache.dtype != torch.bfloat16 or query.dtype != torch.bfloat16:
+            raise NotImplementedError("Qwen3.8-Flash-Next QSA requires BF16 Q/K/V")
+        kernels.qsa_sparse_paged_attention(
             query[:num_tokens],
-            key_data,
-            key_scale,
-            value_data,
-            value_scale,
-            float(getattr(layer, "_qsa_nvfp4_k_global", 1.0)),
-            float(getattr(layer, "_qsa_nvfp4_v_global", 1.0)),
+            key_cache,
+            value_cache,
             logical_indices,
             attn_metadata.block_table,
             token_to_req,

@@ -82,6 +82,10 @@ def _load():
         lib.orc_sparse_attention_fp8.argtypes = [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
                                                  I64, I64, I32, F, F,
                                                  P, I64, P, I64, I64, P, P, I64, I32, I32, P]
+        lib.orc_sparse_attention_bf16.restype = None
+        lib.orc_sparse_attention_bf16.argtypes = [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64,
+                                                  I64, I64, I32,
+                                                  P, I64, P, I64, I64, P, P, I64, I32, I32, P]
         lib.orc_norm_rope.restype = None
         lib.orc_norm_rope.argtypes = [P, I64, I64, I64, I32, I32, P, F, F, P, P, I64, I64, I32, I32, P, P]
         lib.orc_set_threads.restype = None
@@ -255,6 +259,34 @@ def sparse_attention_fp8(q_bits: np.ndarray, k_cache: np.ndarray, v_cache: np.nd
                                      _ptr(block_table), block_table.shape[0], block_table.shape[1],
                                      _ptr(token_to_request), _ptr(out), rows, qh, hd,
                                      _ptr(lse) if return_lse else None)
+    return (out, lse) if return_lse else out
+
+
+def sparse_attention_bf16(q_bits: np.ndarray, k_cache_bits: np.ndarray, v_cache_bits: np.ndarray,
+                          indices: np.ndarray, block_table: np.ndarray, token_to_request: np.ndarray,
+                          return_lse: bool = False):
+    """BF16 sibling reader (src/qsa_ref.py:12-52 on a bf16 cache) in float64; returns fp32 [rows, qh, hd].
+
+    ``k_cache_bits`` / ``v_cache_bits``: uint16 bf16 bit patterns [blocks, page, kv_heads, head_dim], any
+    strides with a contiguous last dim (e.g. the K and V halves of a [blocks, page, kv_heads, 2 * hd] array).
+    """
+    q_bits = np.ascontiguousarray(q_bits, dtype=np.uint16)
+    indices = np.ascontiguousarray(indices, dtype=np.int32)
+    block_table = np.ascontiguousarray(block_table, dtype=np.int32)
+    token_to_request = np.ascontiguousarray(token_to_request, dtype=np.int32)
+    for c in (k_cache_bits, v_cache_bits):
+        assert c.dtype == np.uint16 and c.ndim == 4 and c.strides[-1] == 2 and c.shape == k_cache_bits.shape
+    rows, qh, hd = q_bits.shape
+    blocks, page, kvh, _ = k_cache_bits.shape
+    out = np.zeros((rows, qh, hd), np.float32)
+    lse = np.full((rows, qh), -np.inf, np.float32)
+    topk = indices.shape[1] if indices.ndim == 2 else 0
+    ks, vs = k_cache_bits.strides, v_cache_bits.strides
+    _load().orc_sparse_attention_bf16(_ptr(q_bits), qh * hd, hd, k_cache_bits.ctypes.data, ks[0], ks[1], ks[2],
+                                      v_cache_bits.ctypes.data, vs[0], vs[1], vs[2], blocks, page, kvh,
+                                      _ptr(indices), topk, _ptr(block_table), block_table.shape[0],
+                                      block_table.shape[1], _ptr(token_to_request), _ptr(out), rows, qh, hd,
+                                      _ptr(lse) if return_lse else None)
     return (out, lse) if return_lse else out
 
 

@@ -314,6 +314,14 @@ static void attention_core(int fp8, const uint16_t* q, int64_t q_sr, int64_t q_s
         const uint8_t* vdr = vd + b * vd_sb + o * vd_st + h * vd_sh;
         const uint8_t* vsr = vs + b * vs_sb + o * vs_st + h * vs_sh;
         for (int d = 0; d < head_dim; ++d) {
+          if (fp8 == 2) { /* bf16 element (the BF16 sibling reader, integration/snapshot/qsa.py:352-366) */
+            uint16_t kb2, vb2;
+            memcpy(&kb2, kdr + 2 * d, 2);
+            memcpy(&vb2, vdr + 2 * d, 2);
+            K[t * head_dim + d] = (double)bf16_to_f32(kb2);
+            V[t * head_dim + d] = (double)bf16_to_f32(vb2);
+            continue;
+          }
           if (fp8) { /* one float8_e4m3fn byte per element (qsa_fp8_harness.py:139-158) */
             K[t * head_dim + d] = (double)orc_e4m3_to_f32(kdr[d]);
             V[t * head_dim + d] = (double)orc_e4m3_to_f32(vdr[d]);
@@ -396,6 +404,20 @@ void orc_sparse_attention_fp8(const uint16_t* q, int64_t q_sr, int64_t q_sh, con
                  vc_sb, vc_st, vc_sh, num_blocks, page_size, kv_heads, (double)k_scale, (double)v_scale, indices,
                  topk, block_table, num_requests, table_width, token_to_request, out, rows, query_heads, head_dim,
                  lse_out);
+}
+
+/* The BF16 sibling reader: bf16 K and V caches [blocks, page, kv_heads, head_dim]
+ * with byte strides; plain scale head_dim^-0.5 (src/qsa_ref.py:12-52 on a bf16
+ * cache).  Same masking, softmax and partial format as the NVFP4 reader. */
+void orc_sparse_attention_bf16(const uint16_t* q, int64_t q_sr, int64_t q_sh, const uint8_t* kc, int64_t kc_sb,
+                               int64_t kc_st, int64_t kc_sh, const uint8_t* vc, int64_t vc_sb, int64_t vc_st,
+                               int64_t vc_sh, int64_t num_blocks, int64_t page_size, int32_t kv_heads,
+                               const int32_t* indices, int64_t topk, const int32_t* block_table,
+                               int64_t num_requests, int64_t table_width, const int32_t* token_to_request,
+                               float* out, int64_t rows, int32_t query_heads, int32_t head_dim, float* lse_out) {
+  attention_core(2, q, q_sr, q_sh, kc, kc_sb, kc_st, kc_sh, kc, kc_sb, kc_st, kc_sh, vc, vc_sb, vc_st, vc_sh, vc,
+                 vc_sb, vc_st, vc_sh, num_blocks, page_size, kv_heads, 1.0, 1.0, indices, topk, block_table,
+                 num_requests, table_width, token_to_request, out, rows, query_heads, head_dim, lse_out);
 }
 
 void orc_set_threads(int n) {

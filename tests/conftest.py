@@ -45,5 +45,10 @@ def attention_cases():
 
 
 @pytest.fixture(scope="session")
+def bf16_attention_cases():
+    return _cases(GOLDEN / "bf16_attention_cases.npz")
+
+
+@pytest.fixture(scope="session")
 def decode_golden():
     return np.load(GOLDEN / "decode_config.npz")

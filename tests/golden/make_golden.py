@@ -13,7 +13,7 @@ scattering the reference encoder's per-(token, head) bytes into the
 [blocks, kv_heads, page, 288] layout of python/nvfp4_qsa/cache.py:20-24.
 
 Outputs: kat.json, codec_cases.npz, config_hashes.json, attention_cases.npz,
-decode_config.npz.  Re-running with the same reference reproduces them exactly.
+bf16_attention_cases.npz, decode_config.npz.  Re-running with the same reference reproduces them exactly.
 """
 from __future__ import annotations
 
@@ -239,6 +239,64 @@ def make_attention_cases(ref: Ref):
     return sorted({k.split("__")[0] for k in arrays})
 
 
+def make_bf16_attention_cases(ref: Ref):
+    """The BF16 sibling reader's pin: src/qsa_ref.py:qsa_reference on bf16 caches (no quantisation).
+
+    Each case stores the raw cache as vLLM allocates it, bf16 bits [blocks, kv_heads, page, 2 * 256] (K then V
+    per token), whose K / V views [blocks, page, kv_heads, 256] are what the reader takes.
+    """
+    arrays = {}
+    cells = [
+        ("bf16_fragmented", 32, 2, 5, "normal", 1, True, False, False),
+        ("bf16_ctx17_outliers", 17, 4, 17, "outliers", 1, False, False, False),
+        ("bf16_adversarial_multireq", 256, 4, 64, "normal", 2, True, True, False),
+        ("bf16_duplicates", 300, 3, 96, "normal", 1, False, False, True),
+        ("bf16_heavytail_topk_gt_ctx", 64, 2, 70, "heavytail", 1, True, False, False),
+    ]
+    for cell_seed, (name, ctx, rows, topk, dist, nreq, frag, adversarial, dup) in enumerate(cells, start=301):
+        crng = np.random.default_rng(cell_seed)
+        page = 16
+        table, blocks, req_slots = W.paged_requests(crng, [ctx] * nreq, page, extra_blocks=1, fragmented=frag)
+        toks = nreq * ctx
+        key = W.f32_to_bf16_bits(W.gen_values(crng, (toks, KVH, HD), dist))
+        value = W.f32_to_bf16_bits(W.gen_values(crng, (toks, KVH, HD), dist))
+        kv = np.zeros((blocks, KVH, page, 2 * HD), np.uint16)
+        slots = np.concatenate(req_slots)
+        kv[slots // page, :, slots % page, :HD] = key
+        kv[slots // page, :, slots % page, HD:] = value
+        q = W.f32_to_bf16_bits(W.gen_values(crng, (rows, QH, HD), "normal"))
+        t2r = (np.arange(rows) % nreq).astype(np.int32)
+        idx = np.full((rows, topk), -1, np.int32)
+        for r in range(rows):
+            forced = [0, 1, 15, 16, 17, ctx - 1]
+            pool = crng.permutation(ctx)[:topk]
+            sel = np.unique(np.concatenate([[f for f in forced if f < ctx], pool]))[:topk]
+            idx[r, :sel.size] = sel
+        if dup:
+            idx[0, :] = 5
+            idx[1, : topk // 2] = idx[1, topk // 2: 2 * (topk // 2)]
+        if adversarial:
+            idx[0, 0], idx[0, 1], idx[0, 2] = -1, ctx + 999, 2 ** 31 - 1
+            idx[1, :] = -1
+            t2r[3] = -1
+        cache = bits_to_tensor(kv).transpose(1, 2)  # [blocks, page, kvh, 512] view, as forward_qsa splits it
+        kc, vc = cache[..., :HD], cache[..., HD:]
+        qt = bits_to_tensor(q)
+        out = np.zeros((rows, QH, HD), np.float32)
+        for r in range(rows):  # rows with an out-of-range request are zeros
+            req = int(t2r[r])
+            if req < 0 or req >= table.shape[0]:
+                continue
+            res = ref.q.qsa_reference(qt[r:r + 1], kc, vc, torch.from_numpy(idx[r:r + 1].astype(np.int64)),
+                                      torch.from_numpy(table.astype(np.int64)), torch.tensor([req]), page)
+            out[r] = res["out"][0].numpy()
+        arrays.update({f"{name}__kv": kv, f"{name}__q": q, f"{name}__indices": idx,
+                       f"{name}__block_table": table.astype(np.int32), f"{name}__t2r": t2r,
+                       f"{name}__expected": out})
+    np.savez_compressed(HERE / "bf16_attention_cases.npz", **arrays)
+    return sorted({k.split("__")[0] for k in arrays})
+
+
 def make_decode_config(ref: Ref):
     case = W.decode_config(seed=2)
     storage = ref.storage(case.key, case.value, case.slots, case.blocks, case.page)
@@ -262,6 +320,7 @@ def main():
     manifest["codec_cases"] = make_codec_cases(ref)
     (HERE / "config_hashes.json").write_text(json.dumps(make_config_hashes(ref), indent=1) + "\n")
     manifest["attention_cases"] = make_attention_cases(ref)
+    manifest["bf16_attention_cases"] = make_bf16_attention_cases(ref)
     make_decode_config(ref)
     (HERE / "manifest.json").write_text(json.dumps(manifest, indent=1) + "\n")
     print(json.dumps(manifest, indent=1))

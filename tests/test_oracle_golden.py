@@ -113,6 +113,19 @@ def test_attention_cases_match_reference(attention_cases):
         np.testing.assert_allclose(out, data[f"{name}__expected"], rtol=0, atol=1e-5, err_msg=name)
 
 
+def test_bf16_attention_cases_match_reference(bf16_attention_cases):
+    # The BF16 sibling reader's oracle against the reference's qsa_reference on bf16 caches.
+    data, names = bf16_attention_cases
+    assert len(names) >= 5
+    for name in names:
+        kv = data[f"{name}__kv"]                      # [blocks, kv_heads, page, 512] as vLLM allocates it
+        cache = kv.transpose(0, 2, 1, 3)              # [blocks, page, kv_heads, 512] view (forward_qsa's split)
+        out = oracle.sparse_attention_bf16(data[f"{name}__q"], cache[..., :256], cache[..., 256:],
+                                           data[f"{name}__indices"], data[f"{name}__block_table"],
+                                           data[f"{name}__t2r"])
+        np.testing.assert_allclose(out, data[f"{name}__expected"], rtol=0, atol=1e-5, err_msg=name)
+
+
 def test_decode_config_matches_reference(decode_golden):
     case = W.decode_config(seed=2)
     storage = np.zeros((case.blocks, 2, case.page, 288), np.uint8)

@@ -138,6 +138,53 @@ def test_write_hook_hands_the_writer_the_reference_arguments(recorded):
     assert a[4].data_ptr() - cache.data_ptr() == 144 and a[3].shape == (4, 16, 2, 16)
 
 
+@pytest.fixture
+def recorded_siblings(monkeypatch):
+    calls = []
+    monkeypatch.setattr(kernels, "qsa_sparse_paged_attention_fp8", lambda *a: calls.append(("fp8", a)))
+    monkeypatch.setattr(kernels, "qsa_sparse_paged_attention", lambda *a: calls.append(("bf16", a)))
+    monkeypatch.setattr(kernels, "qsa_sparse_paged_attention_nvfp4", lambda *a: calls.append(("nvfp4", a)))
+    return calls
+
+
+def test_forward_bf16_cache_goes_to_the_bf16_reader(recorded_siblings):
+    # snapshot/qsa.py:323-366: K and V halves of a [blocks, kv_heads, page, 2 * 256] bf16 cache
+    layer, query, _, meta, out, t2r = _inputs(num_tokens=2)
+    cache = torch.zeros(4, 2, 16, 512, dtype=torch.bfloat16)
+    Impl(_qsa_kv_nvfp4=False).forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    (kind, a), = recorded_siblings
+    assert kind == "bf16" and len(a) == 7
+    q, kc, vc, idx, bt, tr, o = a
+    assert kc.shape == vc.shape == (4, 16, 2, 256)
+    assert vc.data_ptr() - cache.data_ptr() == 256 * 2 and kc.stride() == (2 * 16 * 512, 512, 16 * 512, 1)
+    assert q.shape[0] == 2 and o.shape[0] == 2 and bt is meta.block_table and torch.equal(idx, layer.topk_indices_buffer[:2])
+
+
+def test_forward_fp8_cache_goes_to_the_fp8_reader(recorded_siblings):
+    layer, query, _, meta, out, t2r = _inputs(num_tokens=3)
+    layer._k_scale_float, layer._v_scale_float = 0.5, 2.0
+    cache = torch.zeros(4, 2, 16, 512, dtype=torch.uint8)
+    Impl(_qsa_kv_nvfp4=False, _qsa_kv_fp8=True).forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    (kind, a), = recorded_siblings
+    assert kind == "fp8" and len(a) == 9
+    assert a[1].dtype == torch.float8_e4m3fn and a[1].shape == (4, 16, 2, 256) and a[3:5] == (0.5, 2.0)
+
+
+def test_forward_rejects_a_non_bf16_main_cache(recorded_siblings):
+    layer, query, _, meta, out, t2r = _inputs()
+    cache = torch.zeros(4, 2, 16, 512, dtype=torch.float16)
+    with pytest.raises(NotImplementedError, match="BF16 Q/K/V"):
+        Impl(_qsa_kv_nvfp4=False).forward_qsa(layer, query, None, None, cache, meta, out, t2r)
+    assert not recorded_siblings
+
+
+def test_singleton_dims_get_dense_strides():
+    t = torch.zeros(4, 1, 2, 256)[:, :, :, :]
+    odd = t.as_strided(t.shape, (512, 7, 256, 1))
+    fixed = vllm_hooks.canonicalize_singleton_dim_strides(odd)
+    assert fixed.stride() == (512, 512, 256, 1) and fixed.data_ptr() == odd.data_ptr()
+
+
 def test_hooks_module_calls_through_kernels_namespace():
     # the hooks look the raw ops up on nvfp4_qsa.kernels at call time (monkeypatch-able, one code path)
     assert vllm_hooks.kernels is kernels
