@@ -53,6 +53,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <atomic>
 #include <cstring>
 #include <type_traits>
