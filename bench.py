@@ -671,6 +671,33 @@ def bench_split_kv(args, device, world, rank, steps):
     sync_all()
     del graph
     fused_check = check()
+
+    # Where a layer's time goes (the same eager step, once, with the readers' %globaltimer stamps on):
+    # per (row, kv head) unit, averaged over layers and units, max over ranks.
+    units = KV_HEADS  # one row
+    stamps = torch.zeros(layers, units, kernels.STAMP_SLOTS, dtype=torch.int64, device=device)
+    for li, d in enumerate(L):
+        kernels.reset_stamps(stamps[li])
+        kernels.set_stamp_buffer(stamps[li])
+        if world > 1:
+            sk.attend_fused(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], exchange, block_table=d["table"])
+        else:
+            kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
+                                                     d["out"])
+    kernels.set_stamp_buffer(None)
+    torch.cuda.synchronize(device)
+    st = stamps.double()
+
+    def span(a, b):
+        return ((st[..., b] - st[..., a]).mean() / 1e3).item()
+
+    phases = torch.tensor([span(0, 1), span(1, 2), span(2, 3), span(3, 4) if world > 1 else 0.0,
+                           span(4, 5) if world > 1 else 0.0, span(5 if world > 1 else 3, 6), span(0, 6)],
+                          device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(phases, op=dist.ReduceOp.MAX)
+    stamp_us = dict(zip(["tiles", "parts_in", "local_merge", "push_to_peers", "peer_wait", "final_merge_store",
+                         "kernel"], [round(x, 2) for x in phases.tolist()]))
     nccl_secs, nccl_check = None, None
     if world > 1:
         for _ in range(3):
@@ -696,6 +723,10 @@ def bench_split_kv(args, device, world, rank, steps):
         "nccl_us_per_layer": nccl_secs / n / layers * 1e6 if nccl_secs is not None else None,
         "check": fused_check,
         "nccl_check": nccl_check,
+        "phases_us": {"what": "one eager step with the readers' %globaltimer stamps: first CTA entry -> last CTA done "
+                              "with its tiles -> last split part in -> local merge -> partial pushed to the peers -> "
+                              "every peer's partial seen -> stored; mean over layers and (row, kv head), max over "
+                              "ranks", **stamp_us},
     }
 
 

@@ -418,6 +418,19 @@ int nvqsa_decode_rows(
 
 
 /*
+ * Measurement aid, no counterpart in the reference: install (stamps != NULL)
+ * or remove (NULL) a device buffer of uint64 %globaltimer stamps for the
+ * current device.  While installed, every reader launch on that device
+ * writes, per (row, kv head) unit u, 8 slots at stamps + 8u: 0 first CTA
+ * entry (atomic min), 1 last CTA done with its tiles (atomic max), 2 last
+ * split part arrived, 3 local merge done, 4 partial pushed to every peer
+ * (split-KV across GPUs), 5 every peer's partial seen, 6 result stored.
+ * The caller fills slot 0 with all ones (and 1.. with zeros) before the
+ * launch.  Not for production launches: the stamps cost atomics.
+ */
+int nvqsa_set_stamp_buffer(void* stamps);
+
+/*
  * Same computation as nvqsa_sparse_attention, for callers that cannot
  * allocate device memory: code that runs where cudaMalloc is unavailable or
  * forbidden (a host that hands this library only fixed, pre-registered

@@ -123,6 +123,8 @@ struct AttnParams {
   int64_t o_stride_row, o_stride_head;
   float* part_out;               // [splits][rows][query_heads][256]
   float* part_lse;               // [splits][rows][query_heads]
+  // Optional timing stamps (nullptr: off), %globaltimer nanoseconds per (row, kv head) unit, kStampSlots each.
+  unsigned long long* stamps;
 };
 
 template <int REC, int STAGES>
@@ -150,6 +152,25 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }       // bit 0: an mbarrier wait ran out
 constexpr unsigned int kErrWaitTimeout = 1u;
+// Timing stamps of one (row, kv head) unit (all %globaltimer ns of the GPU that writes them):
+//   0 first CTA entry (min)      1 last CTA done with its tiles (max)   2 last part arrived at the unit counter
+//   3 local merge done           4 partial pushed to every peer, flags raised
+//   5 every peer's flag seen     6 result stored
+constexpr int kStampSlots = 8;
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void stamp_min(const AttnParams& p, int64_t unit, int slot) {
+  if (p.stamps) atomicMin(p.stamps + unit * kStampSlots + slot, globaltimer_ns());
+}
+__device__ __forceinline__ void stamp_max(const AttnParams& p, int64_t unit, int slot) {
+  if (p.stamps) atomicMax(p.stamps + unit * kStampSlots + slot, globaltimer_ns());
+}
+__device__ __forceinline__ void stamp_set(const AttnParams& p, int64_t unit, int slot) {
+  if (p.stamps) p.stamps[unit * kStampSlots + slot] = globaltimer_ns();
+}
 constexpr unsigned int kErrPeerTimeout = 2u;            // bit 1: another GPU's split-KV slot never arrived
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;  // 2 s
 
@@ -476,6 +497,7 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
       if (r == me) continue;
       asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(flag_of(p.xpeer[r], me)), "r"(1u) : "memory");
     }
+    stamp_set(p, unit, 4);
     // Wait for every other rank's slot: bounded by time, so a rank that never arrives cannot hang the GPU.
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -498,12 +520,14 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
       }
     }
     status = ok;
+    stamp_set(p, unit, 5);
   }
   __syncthreads();
   if (!status) return;
   merge_unit_parts(p, scratch, row, kvh, G, tid, mine, lse_of(mine), world, 0, nullptr, nullptr);
   __syncthreads();
   if (tid < world) *flag_of(mine, tid) = 0u;  // re-arm this parity for the call after next
+  if (tid == 0) stamp_set(p, unit, 6);
 }
 
 // Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
@@ -517,10 +541,15 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
   if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
   __syncthreads();
   if (!last) return;
+  const int64_t unit = row * p.kv_heads + kvh;
+  if (tid == 0) stamp_set(p, unit, 2);
   __threadfence();  // the other parts, counted before ours, are visible
   merge_unit_parts(p, scratch, row, kvh, G, tid, p.part_out, p.part_lse, nparts, p.final_mode, p.final_out,
                    p.final_lse);
+  __syncthreads();
+  if (tid == 0) stamp_set(p, unit, 3);
   if (p.xworld > 0) xrank_exchange(p, scratch, last, row, kvh, G, tid);
+  else if (tid == 0) stamp_set(p, unit, 6);
 }
 
 // GMODE: how records reach shared memory (0: tile::gather4 rows; 1: one bulk copy per
@@ -550,6 +579,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
   bid /= p.splits;
   const int kvh = (int)(bid % p.kv_heads);
   const int64_t row = bid / p.kv_heads;
+  if (tid == 0) stamp_min(p, row * p.kv_heads + kvh, 0);
 
   const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
   const int my_chunks = split < chunks ? (int)((chunks - 1 - split) / p.splits + 1) : 0;  // <= kMaxChunks
@@ -994,6 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
       mbar_wait(smem_u32(&sm.full_bar[warp][k2 % kStages]), (uint32_t)((k2 / kStages) & 1), kDrainSpinLimit);
   }
   __syncthreads();  // every warp left its loop: no bulk copy is in flight, the rings are free
+  if (tid == 0) stamp_max(p, row * p.kv_heads + kvh, 1);
   const bool aborted = sm.abort != 0;
   if (aborted && p.cluster <= 1) return;  // a cluster CTA still takes the cluster barriers below
 
@@ -1204,6 +1235,7 @@ bool record_map(const void* base, int64_t rows, CUtensorMap* out) {
   return true;
 }
 
+constexpr int kMaxDevicesStamps = 64;
 constexpr int kReaderCtasPerSm = 3;  // resident CTAs per SM of the full-width reader (registers and shared memory)
 constexpr int kBf16CtasPerSm = 2;    // resident CTAs per SM of the BF16 sibling reader (shared memory)
 
@@ -1293,6 +1325,9 @@ Workspace workspace_layout(const Plan& pl, int64_t rows, int query_heads, int kv
 size_t workspace_for(const Plan& pl, int64_t rows, int query_heads, int kv_heads) {
   return workspace_layout(pl, rows, query_heads, kv_heads).bytes;
 }
+
+// Timing stamp buffer of each device (nvqsa_set_stamp_buffer), handed to every reader launch; nullptr: off.
+std::atomic<unsigned long long*> g_stamps[kMaxDevicesStamps] = {};
 
 // Dynamic shared memory above 48 KB is opted into once per device.
 constexpr int kMaxDevices = 64;
@@ -1398,6 +1433,12 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     return NVQSA_ERR_UNSUPPORTED;
 
   AttnParams p;
+  p.stamps = nullptr;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevicesStamps)
+      p.stamps = g_stamps[dev].load(std::memory_order_relaxed);
+  }
   p.q = static_cast<const __nv_bfloat16*>(query);
   p.q_stride_row = q_stride_row;
   p.q_stride_head = q_stride_head;
@@ -1577,6 +1618,14 @@ extern "C" int nvqsa_read_error_flags(uint32_t* flags, int clear) {
     const unsigned int zero = 0;
     if (cudaMemcpyToSymbol(g_error_flags, &zero, sizeof(zero)) != cudaSuccess) return NVQSA_ERR_CUDA;
   }
+  return NVQSA_OK;
+}
+
+extern "C" int nvqsa_set_stamp_buffer(void* stamps) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevicesStamps) return NVQSA_ERR_CUDA;
+  if (stamps && !aligned_to(stamps, 8)) return NVQSA_ERR_MISALIGNED;
+  g_stamps[dev].store(static_cast<unsigned long long*>(stamps), std::memory_order_relaxed);
   return NVQSA_OK;
 }
 

@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
   bid /= p.splits;
   const int kvh = (int)(bid % p.kv_heads);
   const int64_t row = bid / p.kv_heads;
+  if (tid == 0) stamp_min(p, row * p.kv_heads + kvh, 0);
   const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
   const int my_chunks = split < chunks ? (int)((chunks - 1 - split) / p.splits + 1) : 0;  // <= kMaxChunks
   const int G = p.group;
@@ -442,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
       mbar_wait(smem_u32(&sm.full_bar[pair][k2 % kPairStages]), (uint32_t)((k2 / kPairStages) & 1), kDrainSpinLimit);
   }
   __syncthreads();  // every warp left its loop: no bulk copy is in flight, the rings are free
+  if (tid == 0) stamp_max(p, row * p.kv_heads + kvh, 1);
   const bool aborted = sm.abort != 0;
   if (aborted && p.cluster <= 1) return;  // a cluster CTA still takes the cluster barriers below
 

@@ -405,6 +405,28 @@ def qsa_sparse_paged_attention_fp8(
     return out
 
 
+STAMP_SLOTS = 8
+
+
+def set_stamp_buffer(stamps: torch.Tensor | None) -> None:
+    """Install (or, with None, remove) an int64 device buffer [units, 8] of %globaltimer stamps that every reader
+    launch on its device fills per (row, kv head) unit; see nvqsa_set_stamp_buffer.  A measurement aid."""
+    lib = _native.load()
+    if stamps is None:
+        _native.check(lib.nvqsa_set_stamp_buffer(None), "set_stamp_buffer")
+        return
+    if stamps.dtype != torch.int64 or not stamps.is_cuda or not stamps.is_contiguous():
+        raise ValueError("stamps must be a contiguous int64 CUDA tensor")
+    with _device_ctx(stamps.device):
+        _native.check(lib.nvqsa_set_stamp_buffer(stamps.data_ptr()), "set_stamp_buffer")
+
+
+def reset_stamps(stamps: torch.Tensor) -> None:
+    """Prepare a stamp buffer for one launch: slot 0 to all ones (it takes a minimum), the others to zero."""
+    stamps.zero_()
+    stamps.view(-1, STAMP_SLOTS)[:, 0] = -1
+
+
 def qsa_sparse_paged_attention(
     query,
     key_cache,

@@ -168,3 +168,32 @@ def test_peer_wait_times_out_and_reports_without_a_fault():
     finally:
         for b in bufs:
             lib.nvqsa_exchange_free(ctypes.c_void_p(b))
+
+
+def test_timing_stamps_are_ordered_and_leave_the_result_unchanged():
+    # The opt-in %globaltimer stamps (nvqsa_set_stamp_buffer) on a split plan that merges through the workspace:
+    # entry <= tiles done <= last part in <= local merge <= stored, and the output equals the unstamped launch.
+    dev = torch.device("cuda")
+    case = W.decode_config(seed=77, context=20000, topk=4096, page=3136, rows=1)
+    storage = torch.zeros(case.blocks, 2, case.page, 288, dtype=torch.uint8, device=dev)
+    regs = _regions(storage)
+    kernels.qsa_write_cache_nvfp4(_bits(case.key, dev), _bits(case.value, dev), *regs,
+                                  torch.from_numpy(case.slots).to(dev), 1.0, 1.0)
+    q = _bits(case.query, dev)
+    idx, bt, t2r = (torch.from_numpy(a).to(dev) for a in (case.indices, case.block_table, case.token_to_request))
+    plain = torch.empty_like(q)
+    kernels.qsa_sparse_paged_attention_nvfp4(q, *regs, 1.0, 1.0, idx, bt, t2r, plain)
+    stamps = torch.zeros(2, kernels.STAMP_SLOTS, dtype=torch.int64, device=dev)
+    kernels.reset_stamps(stamps)
+    kernels.set_stamp_buffer(stamps)
+    try:
+        out = torch.empty_like(q)
+        kernels.qsa_sparse_paged_attention_nvfp4(q, *regs, 1.0, 1.0, idx, bt, t2r, out)
+    finally:
+        kernels.set_stamp_buffer(None)
+    torch.cuda.synchronize()
+    assert torch.equal(out, plain)
+    st = stamps.cpu()
+    for u in range(2):
+        s0, s1, s2, s3, s6 = (int(st[u, i]) for i in (0, 1, 2, 3, 6))
+        assert 0 < s0 <= s1 <= s2 <= s3 <= s6, st[u].tolist()
