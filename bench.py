@@ -676,16 +676,35 @@ def bench_split_kv(args, device, world, rank, steps):
     # per (row, kv head) unit, averaged over layers and units, max over ranks.
     units = KV_HEADS  # one row
     stamps = torch.zeros(layers, units, kernels.STAMP_SLOTS, dtype=torch.int64, device=device)
-    for li, d in enumerate(L):
-        kernels.reset_stamps(stamps[li])
-        kernels.set_stamp_buffer(stamps[li])
-        if world > 1:
-            sk.attend_fused(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], exchange, block_table=d["table"])
-        else:
-            kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
-                                                     d["out"])
-    kernels.set_stamp_buffer(None)
+
+    def stamped_step():  # each layer's launch carries its own stamp buffer (read at launch / capture time)
+        for li, d in enumerate(L):
+            kernels.reset_stamps(stamps[li])
+            kernels.set_stamp_buffer(stamps[li])
+            if world > 1:
+                sk.attend_fused(d["q"], *d["regions"], 1.0, 1.0, d["idx"], t2r, d["out"], exchange,
+                                block_table=d["table"])
+            else:
+                kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"],
+                                                         t2r, d["out"])
+        kernels.set_stamp_buffer(None)
+
+    # steady state: the stamped step captured once and replayed like the timed graph
+    s2 = torch.cuda.Stream(device)
+    s2.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s2):
+        stamped_step()
+    torch.cuda.current_stream(device).wait_stream(s2)
+    sgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(sgraph):
+        stamped_step()
+    for _ in range(5):
+        sgraph.replay()
+    sync_all()
+    for _ in range(3):
+        sgraph.replay()
     torch.cuda.synchronize(device)
+    del sgraph
     st = stamps.double()
 
     def span(a, b):
@@ -723,7 +742,7 @@ def bench_split_kv(args, device, world, rank, steps):
         "nccl_us_per_layer": nccl_secs / n / layers * 1e6 if nccl_secs is not None else None,
         "check": fused_check,
         "nccl_check": nccl_check,
-        "phases_us": {"what": "one eager step with the readers' %globaltimer stamps: first CTA entry -> last CTA done "
+        "phases_us": {"what": "graph-replayed step with the readers' %globaltimer stamps: first CTA entry -> last CTA done "
                               "with its tiles -> last split part in -> local merge -> partial pushed to the peers -> "
                               "every peer's partial seen -> stored; mean over layers and (row, kv head), max over "
                               "ranks", **stamp_us},

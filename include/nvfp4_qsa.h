@@ -418,6 +418,22 @@ int nvqsa_decode_rows(
 
 
 /*
+ * QSA indexer top-k: the selection that fills the reader's logical_indices.
+ * The reference's QSA layer hands its (un-vendored) indexer the buffer
+ * topk_indices_buffer[:num_tokens], int32 [num_tokens, output_width], and
+ * requires that shape back (integration/snapshot/qsa.py:537-545, :605-616).
+ * For each row, among scores[row, 0 .. lengths[row]) (all `context` when
+ * lengths is NULL), the indices of the k largest, ascending; ties at the k-th
+ * value go to the lowest indices; NaN ranks above every number; a row with
+ * fewer than k valid positions gets 0 .. len - 1 followed by -1.
+ *
+ * scores : fp32 [rows, context], row stride score_stride_row >= context elements
+ * out    : int32 [rows, k], row stride out_stride_row >= k elements
+ */
+int nvqsa_topk_indices(const float* scores, int64_t score_stride_row, const int32_t* lengths, int64_t rows,
+                       int64_t context, int32_t k, int32_t* out, int64_t out_stride_row, void* stream);
+
+/*
  * Measurement aid, no counterpart in the reference: install (stamps != NULL)
  * or remove (NULL) a device buffer of uint64 %globaltimer stamps for the
  * current device.  While installed, every reader launch on that device

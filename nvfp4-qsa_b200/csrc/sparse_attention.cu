@@ -78,13 +78,17 @@ constexpr int kStageBytes = kTile * kRecordBytes;
 // FP8 sibling reader (gather mode 3): float8_e4m3 K and V rows of 256 bytes from two caches, staged as
 // K | V | 16 bytes of skew per token (the skew keeps the per-lane K and V reads bank-conflict free).
 constexpr int kGatherFp8 = 3;
-constexpr int kGatherBf16 = 4;   // BF16 sibling reader: bf16 K and V rows of 512 bytes (sparse_attention_bf16_kernel)
+constexpr int kGatherBf16 = 4;
+// NVFP4 regions whose bases or strides are not 16-byte multiples (the reference takes any strides with a
+// contiguous last dim, kernels.py:376-391): records copied with plain loads of copy_width bytes.
+constexpr int kGatherPlain = 5;   // BF16 sibling reader: bf16 K and V rows of 512 bytes (sparse_attention_bf16_kernel)
 constexpr int kFp8RecordBytes = 528;
 constexpr int kFp8Stages = 2;
 constexpr float kMaskedScore = -1.0e20f;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: P <= 2^8 between rescales
 constexpr uint32_t kSpinLimit = 1u << 22;        // bounded mbarrier waits
 constexpr uint32_t kDrainSpinLimit = 1u << 16;   // bounded waits while abandoning a CTA
+constexpr int kMaxClusterSplitsMerge = 8;       // CTAs of a split-KV cluster (portable cluster size)
 
 struct AttnParams {
   CUtensorMap rows_map;          // gather mode 0: [rows, 144] u16 view of the cache records
@@ -94,7 +98,9 @@ struct AttnParams {
   int64_t stride[4][3];          // block, token, head (bytes)
   int64_t num_blocks, page_size;
   int32_t kv_heads, group, query_heads;
-  int32_t gather_mode;           // 0: tile::gather4 rows; 1: one bulk copy per record; 2: four per record
+  int32_t gather_mode;           // 0: tile::gather4 rows; 1: one bulk copy per record; 2: four per record;
+                                 // 5: plain loads of copy_width bytes (unaligned bases or strides)
+  int32_t copy_width;            // gather mode 5: 1, 2, 4 or 8 (the largest that divides every base and stride)
   int32_t total_rows;            // gather mode 0: rows of the record matrix (out-of-range row = zero fill)
   float score_scale;             // head_dim^-0.5 * log2(e) / key_global_scale
   float inv_value_scale;         // 1 / value_global_scale
@@ -409,39 +415,62 @@ __device__ __noinline__ void merge_unit_parts(const AttnParams& p, float* scratc
       head_den[tid] = den;
     }
     __syncthreads();
-    // 3. outputs: item = (head j, 8 dims); loads of four parts in flight at a time (empty parts hold zeros)
-    for (int it = tid; it < G * 32; it += kThreads) {
-      const int j = it >> 5, d8 = it & 31;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      const float* base = part_out + (w0 + j) * kHeadDim + d8 * 8;
-      for (int q0 = 0; q0 < nparts; q0 += 4) {
-        float4 x[4], y[4];
-        float c[4];
+    // 3. outputs: item = (head j, 8 dims).  A thread takes up to three items per pass (one pass for
+    // G <= 12); each round issues the loads of three parts for all of the pass's items before any is used,
+    // so a round costs one L2 round trip and eighteen float4 are in flight per thread.
+    constexpr int kItemsPerThread = 3;
+    constexpr int kPartsPerRound = 3;
+    for (int it0 = 0; it0 < G * 32; it0 += kItemsPerThread * kThreads) {
+    float acc[kItemsPerThread][8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const bool in = q0 + u < nparts;
-          const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + u : 0) * items * kHeadDim);
-          x[u] = __ldcg(po);
-          y[u] = __ldcg(po + 1);
-          c[u] = in ? wt[(q0 + u) * 16 + j] : 0.0f;
-        }
+    for (int u = 0; u < kItemsPerThread; ++u)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          acc[0] += c[u] * x[u].x; acc[1] += c[u] * x[u].y; acc[2] += c[u] * x[u].z; acc[3] += c[u] * x[u].w;
-          acc[4] += c[u] * y[u].x; acc[5] += c[u] * y[u].y; acc[6] += c[u] * y[u].z; acc[7] += c[u] * y[u].w;
+      for (int i = 0; i < 8; ++i) acc[u][i] = 0.0f;
+    for (int q0 = 0; q0 < nparts; q0 += kPartsPerRound) {
+      float4 x[kItemsPerThread][kPartsPerRound], y[kItemsPerThread][kPartsPerRound];
+#pragma unroll
+      for (int u = 0; u < kItemsPerThread; ++u) {
+        const int it = it0 + tid + u * kThreads;
+        const int j = it >> 5, d8 = it & 31;
+        const float* base = part_out + (w0 + (it < G * 32 ? j : 0)) * kHeadDim + d8 * 8;
+#pragma unroll
+        for (int v = 0; v < kPartsPerRound; ++v) {
+          const bool in = q0 + v < nparts && it < G * 32;
+          const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + v : 0) * items * kHeadDim);
+          x[u][v] = in ? __ldcg(po) : make_float4(0.f, 0.f, 0.f, 0.f);
+          y[u][v] = in ? __ldcg(po + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+#pragma unroll
+      for (int u = 0; u < kItemsPerThread; ++u) {
+        const int it = it0 + tid + u * kThreads;
+        const int j = it < G * 32 ? it >> 5 : 0;
+#pragma unroll
+        for (int v = 0; v < kPartsPerRound; ++v) {
+          const float c = q0 + v < nparts ? wt[(q0 + v) * 16 + j] : 0.0f;
+          acc[u][0] += c * x[u][v].x; acc[u][1] += c * x[u][v].y; acc[u][2] += c * x[u][v].z;
+          acc[u][3] += c * x[u][v].w; acc[u][4] += c * y[u][v].x; acc[u][5] += c * y[u][v].y;
+          acc[u][6] += c * y[u][v].z; acc[u][7] += c * y[u][v].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kItemsPerThread; ++u) {
+      const int it = it0 + tid + u * kThreads;
+      if (it >= G * 32) continue;
+      const int j = it >> 5, d8 = it & 31;
+      float (&acc8)[8] = acc[u];
       const float den = head_den[j];
       const float inv = den > 0.0f ? 1.0f / den : 0.0f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] *= inv;
+      for (int i = 0; i < 8; ++i) acc8[i] *= inv;
       const int head = kvh * G + j;
       if (out_mode == 0) {
         __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
         uint32_t u4[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+          __nv_bfloat162 b = __floats2bfloat162_rn(acc8[2 * i], acc8[2 * i + 1]);
           u4[i] = *reinterpret_cast<uint32_t*>(&b);
         }
         if (p.vec_o) {
@@ -456,10 +485,11 @@ __device__ __noinline__ void merge_unit_parts(const AttnParams& p, float* scratc
         }
       } else {
         float4* op = reinterpret_cast<float4*>(f32_out + (w0 + j) * kHeadDim + d8 * 8);
-        op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        op[0] = make_float4(acc8[0], acc8[1], acc8[2], acc8[3]);
+        op[1] = make_float4(acc8[4], acc8[5], acc8[6], acc8[7]);
         if (d8 == 0) f32_lse[w0 + j] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
       }
+    }
     }
   }
 }
@@ -533,12 +563,14 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
 // Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
 // normalised partial and lse to the workspace; the last part to arrive at the unit's
 // counter merges all parts.  Called by every thread of the CTA.
+// `arrivals`: CTAs that arrive per unit -- every CTA when each stores a slice of its cluster's part (the
+// distributed cluster merge), one per part when a part's rank 0 stores it whole.
 __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratch, int& last, int64_t row, int kvh,
-                                              int G, int tid) {
+                                              int G, int tid, int arrivals) {
   const int nparts = p.splits / p.cluster;
-  __threadfence();  // this part is visible device-wide before its arrival is counted
+  __threadfence();  // this CTA's share of its part is visible device-wide before its arrival is counted
   __syncthreads();
-  if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(nparts - 1);
+  if (tid == 0) last = atomicAdd(p.counters + (row * p.kv_heads + kvh), 1u) == (unsigned int)(arrivals - 1);
   __syncthreads();
   if (!last) return;
   const int64_t unit = row * p.kv_heads + kvh;
@@ -550,6 +582,119 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
   if (tid == 0) stamp_set(p, unit, 3);
   if (p.xworld > 0) xrank_exchange(p, scratch, last, row, kvh, G, tid);
   else if (tid == 0) stamp_set(p, unit, 6);
+}
+
+// Split-KV merge inside a thread-block cluster of C CTAs, by threads of every rank.  Each CTA has
+// published its (O, m, l) in its own shared memory: accumulator float4 i (NFRAG of them) of slot q
+// (SLOTS of them) at comb[i * 64 + q], slot q's (m_r, m_r8, l_r, l_r8) at comb[NFRAG * 64 + q].  Float4
+// (i, q) holds, for lane (r, c) = (q & 31) / 4, (q & 31) % 4, dims D = 128 h + 32 c + k and D + 16 of
+// heads r and r + 8, where (h, k) = (i / 16, i % 16) when SLOTS = 32 (full-width reader) and (q / 32, i)
+// when SLOTS = 64 (warp pairs); so the 16 float4 of one (q, h) run cover 16 consecutive dims.  Work units
+// are GE consecutive float4 of a run (GE = 8, 4, 2 for clusters of <= 2, 4, 8): each rank takes every C-th
+// unit, loads the run's (m, l) and its GE float4 from every rank over distributed shared memory (all in
+// flight together), weights them by 2^(m_rank - max) and stores the merged, normalised dims as vectors
+// (bf16 output, or the fp32 partial and its lse).  Returns false (nothing stored) when a rank aborted.
+template <int NFRAG, int SLOTS, int GE>
+__device__ __forceinline__ void cluster_merge_units(const AttnParams& p, uint32_t base, int64_t row, int kvh, int G,
+                                                    int tid, int split) {
+  const int C = p.cluster, rank = split % C;
+  constexpr int kGroups = 16 / GE;
+  constexpr int kRanks = 16 / GE;       // largest cluster this unit width serves (C <= kRanks)
+  constexpr int kUnits = 64 * kGroups;  // (q, h) runs: 32 lanes x 2 halves, or 64 slots
+  for (int u = rank * kThreads + tid; u < kUnits; u += C * kThreads) {
+    const int run = u / kGroups, g = u % kGroups;
+    const int q = SLOTS == 32 ? run >> 1 : run;
+    const int h = SLOTS == 32 ? run & 1 : q >> 5;
+    const int i0 = (SLOTS == 32 ? 16 * h : 0) + g * GE;
+    float4 ml[kRanks], o[kRanks][GE];
+#pragma unroll
+    for (int rk = 0; rk < kRanks; ++rk) {
+      if (rk < C) {
+        const uint32_t rb = cluster_map(base, (uint32_t)rk);
+        ml[rk] = cluster_ld_f4(rb + (uint32_t)(NFRAG * 64 + q) * 16u);
+#pragma unroll
+        for (int e = 0; e < GE; ++e) o[rk][e] = cluster_ld_f4(rb + (uint32_t)((i0 + e) * 64 + q) * 16u);
+      }
+    }
+    float Ma = -INFINITY, Mb = -INFINITY;
+#pragma unroll
+    for (int rk = 0; rk < kRanks; ++rk)
+      if (rk < C) { Ma = fmaxf(Ma, ml[rk].x); Mb = fmaxf(Mb, ml[rk].y); }
+    float La = 0.f, Lb = 0.f;
+    float va[2][GE], vb[2][GE];  // [dim block (D, D + 16)][e] for head r (a) and r + 8 (b)
+#pragma unroll
+    for (int e = 0; e < GE; ++e) va[0][e] = va[1][e] = vb[0][e] = vb[1][e] = 0.0f;
+#pragma unroll
+    for (int rk = 0; rk < kRanks; ++rk) {
+      if (rk < C) {
+        const float wa = ex2(ml[rk].x - Ma), wb = ex2(ml[rk].y - Mb);
+        La += wa * ml[rk].z;
+        Lb += wb * ml[rk].w;
+#pragma unroll
+        for (int e = 0; e < GE; ++e) {
+          va[0][e] += wa * o[rk][e].x; va[1][e] += wa * o[rk][e].y;
+          vb[0][e] += wb * o[rk][e].z; vb[1][e] += wb * o[rk][e].w;
+        }
+      }
+    }
+    const int ln = q & 31, r = ln >> 2, c = ln & 3;
+    const int D = 128 * h + 32 * c + (i0 & 15);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = r + 8 * hh;
+      if (j >= G) continue;
+      const float L = hh ? Lb : La, M = hh ? Mb : Ma;
+      // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
+      const float inv = L > 0.0f ? p.inv_value_scale / fmaxf(L, 1.0e-20f) : 0.0f;
+      float(&v)[2][GE] = hh ? vb : va;
+      const int head = kvh * G + j;
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        const int d0 = D + 16 * blk;
+        if (p.mode == 0) {
+          __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d0;
+          uint32_t w[GE / 2];
+#pragma unroll
+          for (int e = 0; e < GE / 2; ++e) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[blk][2 * e] * inv, v[blk][2 * e + 1] * inv);
+            w[e] = *reinterpret_cast<uint32_t*>(&b2);
+          }
+          if (p.vec_o && GE == 8) {
+            *reinterpret_cast<uint4*>(op) = make_uint4(w[0], w[1 % (GE / 2)], w[2 % (GE / 2)], w[3 % (GE / 2)]);
+          } else if (p.vec_o && GE == 4) {
+            *reinterpret_cast<uint2*>(op) = make_uint2(w[0], w[1 % (GE / 2)]);
+          } else {
+            unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+            for (int e = 0; e < GE / 2; ++e) {
+              os[2 * e] = (unsigned short)(w[e] & 0xffffu);
+              os[2 * e + 1] = (unsigned short)(w[e] >> 16);
+            }
+          }
+        } else {
+          const int64_t slot = ((int64_t)(split / C) * p.rows + row) * p.query_heads + head;
+          float* op = p.part_out + slot * kHeadDim + d0;
+#pragma unroll
+          for (int e = 0; e < GE; e += 2) *reinterpret_cast<float2*>(op + e) = make_float2(v[blk][e] * inv, v[blk][e + 1] * inv);
+          if (d0 == 0) p.part_lse[slot] = L > 0.0f ? M + log2f(fmaxf(L, 1.0e-20f)) : -INFINITY;
+        }
+      }
+    }
+  }
+}
+
+template <int NFRAG, int SLOTS>
+__device__ __noinline__ bool cluster_merge_store(const AttnParams& p, const float4* comb, int64_t row, int kvh,
+                                                 int G, int tid, int split, const int* abort_flag) {
+  const int C = p.cluster;
+  bool ok = true;
+  for (int rk = 0; rk < C; ++rk) ok &= cluster_ld_s32(cluster_map(smem_u32(abort_flag), (uint32_t)rk)) == 0;
+  if (!ok) return false;  // the same for every thread: every rank published its abort flag before the barrier
+  const uint32_t base = smem_u32(comb);
+  if (C <= 2) cluster_merge_units<NFRAG, SLOTS, 8>(p, base, row, kvh, G, tid, split);
+  else if (C <= 4) cluster_merge_units<NFRAG, SLOTS, 4>(p, base, row, kvh, G, tid, split);
+  else cluster_merge_units<NFRAG, SLOTS, 2>(p, base, row, kvh, G, tid, split);
+  return true;
 }
 
 // GMODE: how records reach shared memory (0: tile::gather4 rows; 1: one bulk copy per
@@ -735,6 +880,31 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
         gather4_g2s(smem_u32(&sm.rec[warp][slot][lane * 4 * kRecordBytes]), &p.rows_map, rows[0], rows[1], rows[2],
                     rows[3], bar);
       }
+      return;
+    }
+    if constexpr (GMODE == kGatherPlain) {
+      // Synchronous plain loads: the warp copies the tile's records region by region, copy_width bytes per
+      // lane and step, then completes the slot's barrier phase with a plain arrive.
+      const int w = p.copy_width;
+      for (int t = 0; t < count; ++t) {
+        const int2 e = sm.sel[j0 + t];
+        uint8_t* d = sm.rec[warp][slot] + soff(t);
+        const uint32_t dofs[4] = {0, 128, 144, 272};
+        const int size[4] = {128, 16, 128, 16};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint8_t* src = p.region[g] + (int64_t)e.x * p.stride[g][0] + (int64_t)e.y * p.stride[g][1] +
+                               (int64_t)kvh * p.stride[g][2];
+          for (int b = lane * w; b < size[g]; b += 32 * w) {
+            if (w == 8) *reinterpret_cast<uint2*>(d + dofs[g] + b) = __ldg(reinterpret_cast<const uint2*>(src + b));
+            else if (w == 4) *reinterpret_cast<uint32_t*>(d + dofs[g] + b) = __ldg(reinterpret_cast<const uint32_t*>(src + b));
+            else if (w == 2) *reinterpret_cast<uint16_t*>(d + dofs[g] + b) = __ldg(reinterpret_cast<const uint16_t*>(src + b));
+            else d[dofs[g] + b] = __ldg(src + b);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
       return;
     }
     if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(count * (kFp8 ? 2 * kHeadDim : kRecordBytes)));
@@ -1065,44 +1235,58 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     __syncthreads();
   }
 
-  if (p.cluster > 1) {
-    // Split-KV inside a thread-block cluster (the CTA's rank is its split): every CTA publishes
-    // warp 0's (O, m, l) in its own shared memory, rank 0 merges the other ranks' over distributed
-    // shared memory and stores the result; no global workspace, no counters.
+  if (p.cluster > 2) {
+    // Split-KV inside a thread-block cluster (the CTA's rank is its split): every CTA publishes warp 0's
+    // (O, m, l) in its own shared memory; then threads of every rank merge and store one slice each.
     if (warp == 0 && !aborted) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) comb[i * 64 + lane] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
       comb_ml[lane] = make_float4(m_r, m_r8, l_r, l_r8);
     }
     cluster_sync();
-    bool ok = !aborted;
-    if (split % p.cluster == 0 && warp == 0 && ok) {
-      for (int rk = 1; rk < p.cluster; ++rk) {
-        if (cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk))) {
-          ok = false;
-          continue;
-        }
-        const uint32_t cb = cluster_map(smem_u32(comb), (uint32_t)rk);
-        const float4 ml = cluster_ld_f4(cb + (uint32_t)(32 * 64 + lane) * 16u);
-        const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
-        const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
-        const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
-        l_r = l_r * a0 + ml.z * b0;
-        l_r8 = l_r8 * a1 + ml.w * b1;
-        m_r = M_r;
-        m_r8 = M_r8;
+    const bool ok = cluster_merge_store<32, 32>(p, comb, row, kvh, G, tid, split, &sm.abort);
+    cluster_sync();  // every rank keeps its shared memory until all ranks have read it; slices are stored
+    if (!ok) return;
+    if (p.fuse) {
+      fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid, p.splits);
+    } else if (p.xworld > 0 && split % p.cluster == 0) {
+      xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+    } else if (tid == 0 && split % p.cluster == 0) {
+      stamp_set(p, row * p.kv_heads + kvh, 6);
+    }
+    return;
+  }
+  if (p.cluster == 2) {
+    // A pair of CTAs: warp 0 of rank 0 reads its peer's (O, m, l) over distributed shared memory (one
+    // round of loads) and stores the merged result like an unsplit CTA.
+    if (warp == 0 && !aborted) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float4 v = cluster_ld_f4(cb + (uint32_t)(i * 64 + lane) * 16u);
-          oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
-          oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
-          oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
-          oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
-        }
+      for (int i = 0; i < 32; ++i) comb[i * 64 + lane] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
+      comb_ml[lane] = make_float4(m_r, m_r8, l_r, l_r8);
+    }
+    cluster_sync();
+    bool ok = !aborted && cluster_ld_s32(cluster_map(smem_u32(&sm.abort), 1u ^ (uint32_t)(split & 1))) == 0;
+    if ((split & 1) == 0 && warp == 0 && ok) {
+      const uint32_t cb = cluster_map(smem_u32(comb), 1u);
+      const float4 ml = cluster_ld_f4(cb + (uint32_t)(32 * 64 + lane) * 16u);
+      const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
+      const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
+      const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
+      l_r = l_r * a0 + ml.z * b0;
+      l_r8 = l_r8 * a1 + ml.w * b1;
+      m_r = M_r;
+      m_r8 = M_r8;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float4 v = cluster_ld_f4(cb + (uint32_t)(i * 64 + lane) * 16u);
+        oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
+        oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
+        oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
+        oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
       }
     }
-    cluster_sync();  // ranks > 0 keep their shared memory until rank 0 has read it
-    if (split % p.cluster != 0 || !ok) return;  // rank 0 carries on with the cluster's merged (O, m, l)
+    cluster_sync();  // rank 1 keeps its shared memory until rank 0 has read it
+    if ((split & 1) != 0 || !ok) return;  // rank 0 carries on with the pair's merged (O, m, l)
   }
 
   if (warp == 0) {
@@ -1162,7 +1346,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     if (p.xworld > 0) xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
     return;
   }
-  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid, p.splits / p.cluster);
 }
 
 // One warp per (row, query head): log-sum-exp merge of `splits` partials, split s
@@ -1343,6 +1527,8 @@ ReaderKernel reader_kernel(int gather_mode, bool pair) {
     return {reinterpret_cast<const void*>(sparse_attention_bf16_kernel), sizeof(SmemBf) + 128};
   if (gather_mode == kGatherFp8)
     return {reinterpret_cast<const void*>(sparse_attention_kernel<kGatherFp8>), sizeof(SmemFp8) + 128};
+  if (gather_mode == kGatherPlain)
+    return {reinterpret_cast<const void*>(sparse_attention_kernel<kGatherPlain>), sizeof(Smem) + 128};
   if (pair) {
     switch (gather_mode) {
       case 0: return {reinterpret_cast<const void*>(sparse_attention_pair_kernel<0>), sizeof(SmemPair<0>) + 128};
@@ -1362,8 +1548,9 @@ int configure_smem() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NVQSA_ERR_CUDA;
   if (!smem_configured[dev]) {
-    for (int k = 0; k < 8; ++k) {
-      const ReaderKernel rk = k == 7   ? reader_kernel(kGatherBf16, false)
+    for (int k = 0; k < 9; ++k) {
+      const ReaderKernel rk = k == 8   ? reader_kernel(kGatherPlain, false)
+                              : k == 7 ? reader_kernel(kGatherBf16, false)
                               : k == 6 ? reader_kernel(kGatherFp8, false)
                                        : reader_kernel(k % 3, k >= 3);
       if (cudaFuncSetAttribute(rk.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rk.smem) != cudaSuccess ||
@@ -1407,12 +1594,16 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   if (!query || !token_to_request || (!output && !partial_mode) || (partial_mode && !partial_lse))
     return NVQSA_ERR_NULL_POINTER;
   if (topk > 0 && !logical_indices) return NVQSA_ERR_NULL_POINTER;
+  // The widest power of two (<= 16 bytes) dividing every region base and stride: 16 allows TMA and bulk
+  // copies; narrower layouts (NVFP4 only) take plain loads of that width.
+  int align = 16;
   for (int i = 0; i < 4; ++i) {
     if (!region[i]) return NVQSA_ERR_NULL_POINTER;
-    if (!aligned_to(region[i], 16)) return NVQSA_ERR_MISALIGNED;
+    while (align > 1 && !aligned_to(region[i], (uintptr_t)align)) align >>= 1;
     for (int j = 0; j < 3; ++j)
-      if (strides[i][j] % 16) return NVQSA_ERR_MISALIGNED;
+      while (align > 1 && strides[i][j] % align) align >>= 1;
   }
+  if (align < 16 && (fp8 || bf16)) return NVQSA_ERR_MISALIGNED;  // the sibling readers keep the 16-byte rule
   if (!aligned_to(query, 2) || (partial_mode ? !aligned_to(partial_out, 16) || !aligned_to(partial_lse, 4)
                                              : !aligned_to(output, 2)))
     return NVQSA_ERR_MISALIGNED;
@@ -1458,9 +1649,11 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
       for (int j = 0; j < 3; ++j) rec = rec && p.stride[i][j] == p.stride[0][j];
     p.gather_mode = rec ? 1 : 2;
     p.total_rows = 0;
+    p.copy_width = align >= 8 ? 8 : align;
+    if (align < 16) p.gather_mode = kGatherPlain;
     // Canonical storage [blocks, kv_heads, page, 288]: records are rows of one matrix.
     const int64_t rows = num_blocks * kv_heads * page_size;
-    if (rec && p.stride[0][1] == kRecordBytes && p.stride[0][2] == page_size * kRecordBytes &&
+    if (align == 16 && rec && p.stride[0][1] == kRecordBytes && p.stride[0][2] == page_size * kRecordBytes &&
         p.stride[0][0] == kv_heads * page_size * kRecordBytes && rows > 0 && rows < 0x7fffffffLL &&
         record_map(b, rows, &p.rows_map)) {
       p.gather_mode = 0;
@@ -1575,6 +1768,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
                          rows, query_heads, head_dim, workspace, workspace_bytes, stream, xpeers, xworld, xrank,
                          xparity, 1);
   }
+  if (p.gather_mode == kGatherPlain) pl.pair = false;  // plain loads run on the full-width reader only
   const ReaderKernel rk = reader_kernel(p.gather_mode, pl.pair);
   cudaStream_t s = as_stream(stream);
   if (p.fuse && cudaMemsetAsync(p.counters, 0, (size_t)rows * kv_heads * sizeof(unsigned int), s) != cudaSuccess)

@@ -441,5 +441,5 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_bf16_kernel(cons
     if (p.xworld > 0) xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
     return;
   }
-  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid, p.splits / p.cluster);
 }

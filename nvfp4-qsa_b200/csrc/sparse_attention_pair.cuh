@@ -38,7 +38,6 @@ struct __align__(128) SmemPair {
   int cnt[kCompactIters][kWarps];
   int total;
   int abort;
-  int bad;   // the cluster merge saw an aborted rank: no store
   int last;
 };
 
@@ -82,7 +81,6 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
       for (int b = 0; b < kPairStages; ++b) mbar_init(smem_u32(&sm.full_bar[q][b]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     sm.abort = 0;
-    sm.bad = 0;
   }
 
   // ---------------- prologue: all independent global loads first ----------------
@@ -480,45 +478,25 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
   }
 
   if (p.cluster > 1) {
-    // Split-KV inside a thread-block cluster: pair 0 of every CTA publishes its (O, m, l) halves in its
-    // own shared memory, pair 0 of rank 0 merges the other ranks' over distributed shared memory.
+    // Split-KV inside a thread-block cluster: pair 0 of every CTA publishes its (O, m, l) halves in its own
+    // shared memory; then every thread of every rank merges and stores one slice.
     if (pair == 0 && !aborted) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) comb[i * 64 + q] = make_float4(oacc[i][0], oacc[i][1], oacc[i][2], oacc[i][3]);
       comb_ml[q] = make_float4(m_r, m_r8, l_r, l_r8);
     }
     cluster_sync();
-    bool ok = !aborted;
-    if (split % p.cluster == 0 && pair == 0 && ok) {
-      for (int rk = 1; rk < p.cluster; ++rk) {
-        if (cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)rk))) {
-          ok = false;
-          continue;
-        }
-        const uint32_t cb = cluster_map(smem_u32(comb), (uint32_t)rk);
-        const float4 ml = cluster_ld_f4(cb + (uint32_t)(16 * 64 + q) * 16u);
-        const float M_r = fmaxf(m_r, ml.x), M_r8 = fmaxf(m_r8, ml.y);
-        const float a0 = ex2(m_r - M_r), b0 = ex2(ml.x - M_r);
-        const float a1 = ex2(m_r8 - M_r8), b1 = ex2(ml.y - M_r8);
-        l_r = l_r * a0 + ml.z * b0;
-        l_r8 = l_r8 * a1 + ml.w * b1;
-        m_r = M_r;
-        m_r8 = M_r8;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 v = cluster_ld_f4(cb + (uint32_t)(i * 64 + q) * 16u);
-          oacc[i][0] = oacc[i][0] * a0 + v.x * b0;
-          oacc[i][1] = oacc[i][1] * a0 + v.y * b0;
-          oacc[i][2] = oacc[i][2] * a1 + v.z * b1;
-          oacc[i][3] = oacc[i][3] * a1 + v.w * b1;
-        }
-      }
+    const bool ok = cluster_merge_store<16, 64>(p, comb, row, kvh, G, tid, split, &sm.abort);
+    cluster_sync();  // every rank keeps its shared memory until all ranks have read it; slices are stored
+    if (!ok) return;
+    if (p.fuse) {
+      fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid, p.splits);
+    } else if (p.xworld > 0 && split % p.cluster == 0) {
+      xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+    } else if (tid == 0 && split % p.cluster == 0) {
+      stamp_set(p, row * p.kv_heads + kvh, 6);
     }
-    cluster_sync();  // ranks > 0 keep their shared memory until rank 0 has read it
-    if (split % p.cluster != 0) return;  // the same for every thread of the CTA
-    if (pair == 0 && !ok && lane == 0) sm.bad = 1;
-    __syncthreads();
-    if (sm.bad) return;  // CTA-uniform
+    return;
   }
 
   if (pair == 0) {
@@ -575,5 +553,5 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
     if (p.xworld > 0) xrank_exchange(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
     return;
   }
-  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid);
+  fused_part_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), sm.last, row, kvh, G, tid, p.splits / p.cluster);
 }

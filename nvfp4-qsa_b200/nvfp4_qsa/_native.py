@@ -35,6 +35,7 @@ _SIGNATURES = {
     "nvqsa_abi_version": (c_int, []),
     "nvqsa_read_error_flags": (c_int, [POINTER(ctypes.c_uint32), c_int]),
     "nvqsa_set_stamp_buffer": (c_int, [_P]),
+    "nvqsa_topk_indices": (c_int, [_P, _I64, _P, _I64, _I64, _I32, _P, _I64, _P]),
     "nvqsa_write_cache": (c_int, [
         _P, _I64, _I64,
         _P, _I64, _I64,

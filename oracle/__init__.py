@@ -290,6 +290,23 @@ def sparse_attention_bf16(q_bits: np.ndarray, k_cache_bits: np.ndarray, v_cache_
     return (out, lse) if return_lse else out
 
 
+def topk_indices(scores: np.ndarray, k: int, lengths=None) -> np.ndarray:
+    """The indexer top-k contract in NumPy: per row, the indices of the k largest of scores[row, :len] in
+    ascending order, ties at the k-th value to the lowest indices, NaN highest, -1 padding past len."""
+    scores = np.asarray(scores, dtype=np.float32)
+    rows, context = scores.shape
+    out = np.full((rows, k), -1, np.int32)
+    for r in range(rows):
+        n = context if lengths is None else int(min(max(lengths[r], 0), context))
+        s = scores[r, :n].astype(np.float64)
+        key = np.where(np.isnan(s), np.inf, s)
+        # largest first; equal keys in index order (stable sort on -key); NaN (inf here) above +inf
+        order = np.lexsort((np.arange(n), -key, ~np.isnan(s)))
+        sel = np.sort(order[:k])
+        out[r, :sel.size] = sel
+    return out
+
+
 def merge_partials(part_out: np.ndarray, part_lse: np.ndarray) -> np.ndarray:
     """Log-sum-exp merge of split partials (src/qsa_fp8_harness.py:308-321 semantics).
 

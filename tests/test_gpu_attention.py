@@ -247,3 +247,25 @@ def test_no_device_error_flags_raised():
     from nvfp4_qsa import _native
     torch.cuda.synchronize()
     assert _native.read_error_flags(clear=True) == 0
+
+
+@pytest.mark.parametrize("record", [289, 290, 292, 296])
+def test_reader_takes_strides_that_are_not_16_byte_multiples(record):
+    # The reference's raw op takes any block/token/head strides with a contiguous last dim
+    # (python/nvfp4_qsa/kernels.py:376-391): records padded to 289/290/292/296 bytes give strides whose widest
+    # common alignment is 1/2/4/8 bytes; the reader copies them with plain loads of that width.
+    case = W.decode_config(seed=60 + record, context=5000, topk=700, page=64, rows=3)
+    compact = torch.zeros(case.blocks, 2, case.page, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(compact, bits_to_cuda(case.key), bits_to_cuda(case.value), torch.from_numpy(case.slots).cuda())
+    padded = torch.zeros(case.blocks, 2, case.page, record, dtype=torch.uint8, device="cuda")
+    view = padded[..., :288]
+    view.copy_(compact)
+    kd, ks, vd, vs = regions(view)
+    assert kd.stride(1) == record
+    q = bits_to_cuda(case.query)
+    idx, bt, t2r = (torch.from_numpy(a).cuda() for a in (case.indices, case.block_table, case.token_to_request))
+    out = torch.full_like(q, float("nan"))
+    kernels.qsa_sparse_paged_attention_nvfp4(q, kd, ks, vd, vs, 1.0, 1.0, idx, bt, t2r, out)
+    assert_attention_close(out, oracle_attention(compact, q, idx, bt, t2r), f"record {record}")
+    aligned = gpu_attend(compact, q, idx, bt, t2r)
+    assert (out.float() - aligned.float()).abs().max().item() <= 2e-3  # same kernel arithmetic, other copy path
