@@ -558,6 +558,39 @@ def bench_bf16(args, device, steps):
     }
 
 
+def bench_topk(device, steps):
+    """Indexer top-k (nvqsa_topk_indices): the decode selection of config 5a (96 rows x 131,072 scores) and of
+    config 5b (1 row x 169,984), k = 2,048, eight rotating score buffers (more than L2 for 5a).  Algorithmic bytes:
+    the scores (4 B each) read once and the indices (4 B each) written."""
+    import torch
+    from nvfp4_qsa import indexer
+
+    res = {}
+    for name, rows, ctx in (("5a", 96, 131072), ("5b", 1, 169984)):
+        gen = torch.Generator(device=device).manual_seed(11)
+        bufs = [torch.randn(rows, ctx, device=device, generator=gen) for _ in range(8)]
+        out = torch.empty(rows, 2048, dtype=torch.int32, device=device)
+        for b in bufs:
+            indexer.qsa_select_topk(b, out)
+        torch.cuda.synchronize(device)
+        reps = max(40, steps)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(reps):
+            indexer.qsa_select_topk(bufs[i % 8], out)
+        end.record()
+        end.synchronize()
+        per = start.elapsed_time(end) / 1e3 / reps
+        algo = rows * ctx * 4 + rows * 2048 * 4
+        res[name] = {"rows": rows, "context": ctx, "k": 2048, "us_per_call": per * 1e6, "gb_per_s": algo / per / 1e9}
+    peak, kind = measured_peaks()
+    a = res["5a"]
+    res["roofline"] = {"bound": "hbm", "achieved": a["gb_per_s"], "peak": peak, "unit": "GB/s",
+                       "frac": a["gb_per_s"] / peak, "peak_kind": kind, "kernel": "topk_indices_kernel (96 rows)"}
+    res["gpu_launches"] = 2 * (max(40, steps) + 8)
+    return res
+
+
 def bench_split_kv(args, device, world, rank, steps):
     """Config 5b: one 169,984-token sequence, 8,192 selected per row, 12 layers, split-KV over the ranks.
 
@@ -973,6 +1006,7 @@ def main_ours(args):
     mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
     fp8 = bench_fp8(args, device, args.steps) if world == 1 and not args.skip_fp8 else None
     bf16 = bench_bf16(args, device, args.steps) if world == 1 and not args.skip_bf16 else None
+    topk = bench_topk(device, args.steps) if world == 1 else None
     del graph
     result = None
     if rank == 0:
@@ -1021,6 +1055,8 @@ def main_ours(args):
             result["fp8"] = fp8
         if bf16 is not None:
             result["bf16"] = bf16
+        if topk is not None:
+            result["topk"] = topk
         if world == 1 and not args.skip_cpu:
             result["cpu_baseline"] = cpu_baseline_read(args, args.cpu_seconds)
             write["cpu_baseline"] = cpu_baseline_write(False, 3.0)
