@@ -402,6 +402,36 @@ def bench_mtp(args, device, steps):
         reps = max(20, steps)
         times[group] = timed(graph.replay, reps, device) / reps / layers
         del graph
+    # where a grouped layer's time goes: %globaltimer stamps per (group, kv head), one graph-replayed step
+    units = seqs * KV_HEADS
+    stamps = torch.zeros(layers, units, kernels.STAMP_SLOTS, dtype=torch.int64, device=device)
+
+    def stamped():
+        for li, d in enumerate(L):
+            kernels.reset_stamps(stamps[li])
+            kernels.set_stamp_buffer(stamps[li])
+            kernels.qsa_sparse_paged_attention_nvfp4(d["q"], *d["regions"], 1.0, 1.0, d["idx"], d["table"], t2r,
+                                                     d["out"], rows_per_group=4)
+        kernels.set_stamp_buffer(None)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        stamped()
+    torch.cuda.current_stream(device).wait_stream(side)
+    sgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(sgraph):
+        stamped()
+    for _ in range(4):
+        sgraph.replay()
+    torch.cuda.synchronize(device)
+    del sgraph
+    st = stamps.double()
+    layer_start = st[..., 0].min(dim=1).values  # first CTA of the launch
+    phases = {"prologue": ((st[..., 2] - st[..., 0]).mean() / 1e3).item(),
+              "tiles": ((st[..., 1] - st[..., 2]).mean() / 1e3).item(),
+              "cluster_merge_store": ((st[..., 6] - st[..., 1]).mean() / 1e3).item(),
+              "launch_span": ((st[..., 6].max(dim=1).values - layer_start).mean() / 1e3).item()}
     records = seqs * KV_HEADS * topk * RECORD
     algo = records + rows * topk * 4 + 2 * rows * QUERY_HEADS * HEAD_DIM * 2
     peak, kind = measured_peaks()
@@ -416,6 +446,10 @@ def bench_mtp(args, device, steps):
         "per_row_us_per_layer": g1 * 1e6,
         "per_row_gb_per_s": algo / g1 / 1e9,
         "speedup_vs_per_row": g1 / g4,
+        "phases_us": {"what": "grouped reader, graph-replayed step with %globaltimer stamps per (group, kv head): "
+                              "first CTA entry -> last CTA past its prologue -> last CTA done with its tiles -> "
+                              "last CTA stored; mean over layers and units; launch_span = first entry to last store",
+                      **{k: round(v, 2) for k, v in phases.items()}},
         "roofline": {"bound": "hbm", "achieved": algo / g4 / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": algo / g4 / 1e9 / peak, "peak_kind": kind,
                      "kernel": "sparse_attention_mtp_kernel (one layer, splits merged in a cluster)",

@@ -520,7 +520,8 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
     for (int i = tid; i < G * (kHeadDim / 4); i += kThreads) dst_o[i] = __ldcg(src_o + i);
     if (tid < G) lse_of(p.xpeer[r])[(int64_t)me * items + w0 + tid] = __ldcg(src_l + tid);
   }
-  __threadfence_system();
+  // Every thread's peer stores precede thread 0's release below in causality order (the barrier), so the
+  // system-scope release store of each flag makes them visible to the peer that acquires the flag.
   __syncthreads();
   if (tid == 0) {
     for (int r = 0; r < world; ++r) {

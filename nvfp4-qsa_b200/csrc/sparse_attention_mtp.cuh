@@ -84,6 +84,8 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
   const int kvh = (int)(bid % p.kv_heads);
   const int64_t grp = bid / p.kv_heads;
   const int64_t row_lo = grp * p.group_rows;
+  const int64_t unit = grp * p.kv_heads + kvh;  // timing stamps: 0 entry, 2 prologue done, 1 tiles done, 6 stored
+  if (tid == 0) stamp_min(p, unit, 0);
   const int nrows = (int)min((int64_t)p.group_rows, p.rows - row_lo);
 
   const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
@@ -249,6 +251,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     __syncthreads();
     const int n = sm.total;
     const int ntiles = (n + kTile - 1) / kTile;
+    if (tid == 0 && pass == 0) stamp_max(p, unit, 2);
 
     // ---------------- CTA-wide gather ring: warp 0 issues, every warp consumes ----------------
     auto issue_tile = [&](int k) {
@@ -503,6 +506,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     }
     __syncthreads();  // (m, l) visible; no copy in flight, the ring is free
     aborted = sm.abort != 0;
+    if (tid == 0 && pass == passes - 1) stamp_max(p, unit, 1);
 
     // bf16 output of packed head `head` (< act * G), dims d0 and d1
     auto out_ptr = [&](int head) {
@@ -622,4 +626,5 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     }
     __syncthreads();  // the next pass rewrites shared memory
   }
+  if (tid == 0) stamp_max(p, unit, 6);
 }

@@ -60,6 +60,7 @@ struct WriteParams {
   // 1: both global scales in [2^-6, 2^28] (see the encoder's fast path)
   int32_t plain;
   int32_t lut_by_scaling;  // 1: scale table by power-of-two scaling of g / k (see build_out_scale_lut)
+  int32_t byte_store;      // 1: packed data rows not aligned to the lane's store width: store bytes one by one
   // K-norm and RoPE ahead of the encoder (nvqsa_norm_rope_write_cache only).
   const int64_t* positions;      // [num_tokens]
   const __nv_bfloat16* cos_sin;  // [max_position, >= rot_dim]: cos in [0, rot/2), sin in [rot/2, rot)
@@ -176,6 +177,12 @@ __device__ __forceinline__ void encode_row(const uint32_t (&w)[EPL / 2], float s
 #pragma unroll
     for (int i = 0; i < EPL / 2; ++i) packed[0] |= cvt_e2m1x2(y[2 * i + 1], y[2 * i]) << (8 * i);
   }
+}
+
+template <int EPL>
+__device__ __forceinline__ void store_lane_bytes(uint8_t* row, int lane, const uint32_t (&packed)[(EPL + 7) / 8]) {
+#pragma unroll
+  for (int j = 0; j < EPL / 2; ++j) row[lane * (EPL / 2) + j] = (uint8_t)(packed[j >> 2] >> (8 * (j & 3)));
 }
 
 template <int EPL>
@@ -307,7 +314,10 @@ __device__ __forceinline__ void write_item(const WriteParams& p, const float (*o
         encode_row<EPL, SLOW>(x[q], os[q], p.zero, packed);
         const int64_t hstep_d = RECORD ? (int64_t)p.rec_head32 : p.data_stride[r][2];
         const int64_t hstep_s = RECORD ? (int64_t)p.rec_head32 : p.scale_stride[r][2];
-        store_lane<EPL>(drow[r] + (hh ? hstep_d : 0), lane, packed);
+        if (p.byte_store)
+          store_lane_bytes<EPL>(drow[r] + (hh ? hstep_d : 0), lane, packed);
+        else
+          store_lane<EPL>(drow[r] + (hh ? hstep_d : 0), lane, packed);
         if ((lane % LPG) == 0) (srow[r] + (hh ? hstep_s : 0))[lane / LPG] = (uint8_t)sb[q];
       }
     }
@@ -840,13 +850,14 @@ static int prepare_write(
   p.plain = (plain(key_global_scale) && plain(value_global_scale)) ? 1 : 0;
   p.lut_by_scaling = (scalable(key_global_scale) && scalable(value_global_scale)) ? 1 : 0;
 
-  // Packed-row stores are (head_dim/64)-byte words: rows and strides must be
-  // aligned to that width.
+  // Packed-row stores are (head_dim/64)-byte words when rows and strides are aligned to that width; any
+  // other layout (the reference takes any strides with a contiguous last dim) stores bytes.
   const int store_bytes = head_dim / 64;
+  p.byte_store = 0;
   for (int r = 0; r < 2; ++r) {
-    if (!aligned_to(p.data[r], store_bytes)) return NVQSA_ERR_MISALIGNED;
+    if (!aligned_to(p.data[r], store_bytes)) p.byte_store = 1;
     for (int i = 0; i < 3; ++i)
-      if (p.data_stride[r][i] % store_bytes) return NVQSA_ERR_MISALIGNED;
+      if (p.data_stride[r][i] % store_bytes) p.byte_store = 1;
   }
   // Source rows: 2-byte aligned always (bf16); vector loads when 16-byte aligned.
   const int vec_bytes = head_dim >= 256 ? 16 : head_dim / 16;  // bytes per lane load

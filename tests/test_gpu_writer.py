@@ -330,3 +330,18 @@ def test_record_layout_with_other_head_counts(kv_heads):
     cache.write(bits_to_cuda(key), bits_to_cuda(value), torch.from_numpy(slots).cuda())
     torch.cuda.synchronize()
     np.testing.assert_array_equal(cache.storage.cpu().numpy(), oracle_storage(key, value, slots, blocks, page))
+
+
+@pytest.mark.parametrize("record", [289, 290, 292, 296])
+def test_writer_takes_strides_that_are_not_word_multiples(record):
+    # The reference's writer takes any block/token/head strides with a contiguous last dim
+    # (python/nvfp4_qsa/kernels.py:132-150); records padded to 289..296 bytes make the packed rows unaligned to
+    # the lane's 4-byte store, so the writer stores bytes.  The bytes must equal the canonical layout's.
+    k, v, slots = W.prefill_config(seed=9, tokens=1024, blocks=8, page=256)
+    compact = torch.zeros(8, 2, 256, 288, dtype=torch.uint8, device="cuda")
+    gpu_write(compact, bits_to_cuda(k), bits_to_cuda(v), torch.from_numpy(slots).cuda())
+    padded = torch.zeros(8, 2, 256, record, dtype=torch.uint8, device="cuda")
+    gpu_write(padded[..., :288], bits_to_cuda(k), bits_to_cuda(v), torch.from_numpy(slots).cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(padded[..., :288], compact)
+    assert not padded[..., 288:].any()
