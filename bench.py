@@ -82,6 +82,7 @@ NCU_TRAFFIC = {
     "fp8": 210388736,          # sparse_attention_kernel<3>, 96 rows x top-2048, FP8 K/V
     "write": 16863744,         # write_cache_group_kernel, 8,192 tokens into 64 x 3,136
     "fused_write": 18579712,   # write_cache_kernel<256,...,FUSE>, 8,192 tokens
+    "bf16": 413479424,         # sparse_attention_bf16_kernel, 96 rows x top-2048 (48-row capture x 2)
 }
 
 

@@ -68,7 +68,6 @@ constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kTile = 16;                        // tokens per warp tile (one m16n8k16 K-step of P V)
 constexpr int kWarpStages = 3;                   // private ring slots per warp
-constexpr int kAhead = kWarpStages - 1;          // tiles in flight ahead of the one being consumed
 constexpr int kMaxRange = 1024;                  // selections per CTA
 constexpr int kChunk = 32;                       // index positions per interleaved chunk (one warp load)
 constexpr int kMaxChunks = kMaxRange / kChunk;   // chunks per CTA
@@ -88,7 +87,6 @@ constexpr float kMaskedScore = -1.0e20f;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units: P <= 2^8 between rescales
 constexpr uint32_t kSpinLimit = 1u << 22;        // bounded mbarrier waits
 constexpr uint32_t kDrainSpinLimit = 1u << 16;   // bounded waits while abandoning a CTA
-constexpr int kMaxClusterSplitsMerge = 8;       // CTAs of a split-KV cluster (portable cluster size)
 
 struct AttnParams {
   CUtensorMap rows_map;          // gather mode 0: [rows, 144] u16 view of the cache records
@@ -156,8 +154,8 @@ __device__ unsigned int g_error_flags;
 __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-}       // bit 0: an mbarrier wait ran out
-constexpr unsigned int kErrWaitTimeout = 1u;
+}
+constexpr unsigned int kErrWaitTimeout = 1u;            // bit 0: an mbarrier wait ran out
 // Timing stamps of one (row, kv head) unit (all %globaltimer ns of the GPU that writes them):
 //   0 first CTA entry (min)      1 last CTA done with its tiles (max)   2 last part arrived at the unit counter
 //   3 local merge done           4 partial pushed to every peer, flags raised
@@ -1467,24 +1465,30 @@ Plan make_plan(int64_t rows, int kv_heads, int64_t topk, int sms, int ctas_per_s
   return pl;
 }
 
-// Grouped (MTP) reader plan: groups of rows_per_group consecutive rows, power-of-two splits (one cluster
-// of at most 16 per group, each CTA at most 1024 selections) until the launch fills the SMs' three
-// resident CTAs: a group's tiles are processed in order by its CTA, so more splits mean shorter chains.
+// Grouped (MTP) reader plan: groups of rows_per_group consecutive rows, each split into one cluster of
+// at most 8 CTAs (each CTA at most 1024 selections); the most splits whose clusters are all resident at
+// once (cap[s]: resident clusters of s CTAs on this device, or the SM count when unknown): a group's tiles
+// are processed in order by its CTA, so more splits mean shorter chains, but clusters that do not fit on
+// the GPCs run as a second wave.
 struct MtpPlan {
   bool use;
   int splits;
   int64_t grid;
 };
-MtpPlan make_mtp_plan(int64_t rows, int kv_heads, int64_t topk, int G, int rows_per_group, int sms) {
+MtpPlan make_mtp_plan(int64_t rows, int kv_heads, int64_t topk, int G, int rows_per_group, int sms,
+                      const int* cap) {
   MtpPlan mp{false, 1, 0};
   if (rows_per_group < 2 || rows_per_group * G > kMtpHeads || topk < 1) return mp;
   const int64_t units = (rows + rows_per_group - 1) / rows_per_group * kv_heads;
   const int64_t chunks = (topk + kChunk - 1) / kChunk;
-  int64_t splits = 1;
-  while (splits * kMaxChunks < chunks) splits *= 2;
-  if (splits > kMtpMaxCluster) return mp;
-  const int64_t target = 3 * (int64_t)(sms > 0 ? sms : 148);
-  while (splits < kMtpMaxCluster && splits * 2 <= chunks && units * splits * 2 <= target) splits *= 2;
+  const int64_t min_splits = (chunks + kMaxChunks - 1) / kMaxChunks;
+  if (min_splits > kMtpMaxCluster) return mp;
+  const int64_t target = sms > 0 ? sms : 148;
+  int64_t splits = min_splits;
+  for (int64_t s = min_splits + 1; s <= kMtpMaxCluster && s <= chunks; ++s) {
+    const int c = cap ? cap[s] : 0;
+    if (c > 0 ? units <= c : units * s <= target) splits = s;
+  }
   if (units * splits > 0x7fffffffLL) return mp;
   mp.use = true;
   mp.splits = (int)splits;
@@ -1570,6 +1574,36 @@ int configure_smem() {
   return NVQSA_OK;
 }
 
+// Resident clusters of s grouped-reader CTAs (s = 1..8) on each device, queried once; -1 when unknown.
+std::atomic<int> g_mtp_capacity[kMaxDevices][kMtpMaxCluster + 1] = {};
+int mtp_cluster_capacity(int s) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  int v = g_mtp_capacity[dev][s].load(std::memory_order_relaxed);
+  if (v == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)s, 1, 1);
+    cfg.blockDim = dim3(kMtpThreads, 1, 1);
+    cfg.dynamicSmemBytes = sizeof(SmemMtp) + 128;
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeClusterDimension;
+    a.val.clusterDim.x = (unsigned)s;
+    a.val.clusterDim.y = 1;
+    a.val.clusterDim.z = 1;
+    cfg.attrs = &a;
+    cfg.numAttrs = 1;
+    if (configure_smem() != NVQSA_OK ||
+        cudaOccupancyMaxActiveClusters(&v, reinterpret_cast<const void*>(sparse_attention_mtp_kernel), &cfg) !=
+            cudaSuccess ||
+        v <= 0) {
+      (void)cudaGetLastError();
+      v = -1;
+    }
+    g_mtp_capacity[dev][s].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
 int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head, const void* const region[4],
                   const int64_t strides[4][3], int64_t num_blocks, int64_t page_size, int32_t kv_heads,
                   float key_global_scale, float value_global_scale, const int32_t* logical_indices, int64_t topk,
@@ -1613,7 +1647,11 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
   if (sms <= 0) return NVQSA_ERR_CUDA;
   if (rows_per_group < 1 || rows_per_group > kMtpRows) return NVQSA_ERR_BAD_SHAPE;
   const bool sibling = fp8 || bf16;
-  const MtpPlan mp = sibling ? MtpPlan{false, 1, 0} : make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms);
+  int cap[kMtpMaxCluster + 1] = {};
+  if (!sibling && rows_per_group >= 2)
+    for (int s = 1; s <= kMtpMaxCluster; ++s) cap[s] = mtp_cluster_capacity(s);
+  const MtpPlan mp =
+      sibling ? MtpPlan{false, 1, 0} : make_mtp_plan(rows, kv_heads, topk, G, rows_per_group, sms, cap);
   Plan pl = mp.use ? Plan{} : make_plan(rows, kv_heads, topk, sms, bf16 ? kBf16CtasPerSm : kReaderCtasPerSm);
   if (sibling) pl.pair = false;  // the FP8 and BF16 rows run on their full-width readers only
   const Workspace wl = mp.use ? Workspace{0, 0, 0} : workspace_layout(pl, rows, query_heads, kv_heads);
@@ -1741,7 +1779,7 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
     p.group_rows = rows_per_group;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)mp.grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(kMtpThreads, 1, 1);
     cfg.dynamicSmemBytes = sizeof(SmemMtp) + 128;
     cfg.stream = as_stream(stream);
     cudaLaunchAttribute attr[2], cluster_attr;

@@ -5,60 +5,70 @@
 // sparse_attention.cu inside namespace nvqsa::{anonymous}; uses its parameter
 // block, barrier, copy, conversion and cluster helpers.
 //
-// One CTA = (group of up to 4 consecutive rows, kv head, split); the CTA
-// gathers each selected record ONCE into a CTA-wide ring (tile::gather4) and
-// all four warps use it:
-//   * K: warp w dequantises dims [64w, 64w + 64) of the tile's 16 records into
-//     a shared f16 tile (exact: e2m1 x e4m3);
-//   * S = Q K^T: warp w computes the scores of row w of the group (its query
-//     heads in one m16 tile) over all 256 dims, K fragments by ldmatrix, and
-//     runs that row's online softmax; P goes to a shared tile of the group's
-//     packed heads (row-major, up to 48 = 3 m16 tiles);
-//   * O += P V: warp w accumulates dims [64w, 64w + 64) of every packed head
-//     (96 fp32 registers), V dequantised in registers once per tile.
-// So the gather and the dequantisation are paid once per record for all rows
-// of the group instead of once per row.
+// One CTA of 8 warps = (group of up to 4 consecutive rows, kv head, split),
+// one CTA per SM.  Each selected record is gathered ONCE (tile::gather4) into a
+// CTA-wide ring of 16 tiles of 16 records that runs up to 7 steps ahead, and
+// a step of 32 tokens (two tiles) goes through the warps in one CTA barrier:
+//   * warps 0-3 (S warps): warp w computes the scores of row w of the group
+//     (its query heads in one m16 tile) over the step's dequantised K tile,
+//     runs that row's online softmax and writes P into a shared tile of the
+//     group's packed heads (up to 48 = 3 m16 tiles);
+//   * warps 4-7 (K warps), meanwhile: dequantise the NEXT step's K into the
+//     other half of a double-buffered f16 tile (exact: e2m1 x e4m3; warp
+//     4 + j owns dims [64j, 64j + 64)); warp 4 also refills the ring;
+//   * barrier; then every warp w accumulates O += P V over dims
+//     [32w, 32w + 32) of every packed head (12 m16n8 fragments), V
+//     dequantised in registers from the ring.
+// The P and K tiles are double-buffered, so the step's only barrier orders
+// everything: S of step i+1 and K of step i+2 may start while other warps are
+// still in P V of step i.  The gather and the dequantisation are paid once per
+// record for all rows of the group instead of once per row.
 //
 // Sharing is verified on the device, never assumed: each CTA compares the
 // rows' request and the index positions of its chunks against the group's
 // first row, and the CTAs of a cluster agree on the result.  A group that does
 // not share is processed row by row (one pass per row, one active S warp).
+// The ring is filled from the first row's selections before that check
+// completes, so the first copies overlap it and the Q preparation.
 //
-// Splits of a group form one thread-block cluster (1, 2, 4, 8 or 16 CTAs):
-// every rank publishes its (O, m, l) in shared memory, then every rank merges
-// one slice of the output fragments of all ranks over distributed shared
-// memory and stores it.
+// Splits of a group form one thread-block cluster (up to 8 CTAs): every rank
+// publishes its (O, m, l) in shared memory, then every rank merges one slice
+// of the output fragments of all ranks over distributed shared memory and
+// stores it.
 
-constexpr int kMtpStages = 4;     // ring stages of 16 records (two tiles in use, two being filled)
-constexpr int kMtpStep = 2 * kTile;  // tokens per step: two tiles per pair of CTA barriers
-constexpr int kMtpHeads = 48;     // packed query heads of a group (rows x group size)
-constexpr int kMtpMTiles = 3;     // m16 tiles of packed heads
-constexpr int kKhStride = 264;    // halfs per token row of the dequantised K tile (256 + 8: ldmatrix conflict-free)
-constexpr int kPhStride = 40;     // halfs per head row of the P tile (32 + 8: ldmatrix conflict-free)
-constexpr int kMtpRows = 4;       // rows per group (one S warp each)
-constexpr int kMtpMaxCluster = 8;   // splits of a group: one portable cluster
+constexpr int kMtpWarps = 8;
+constexpr int kMtpThreads = 32 * kMtpWarps;
+constexpr int kMtpRing = 16;          // ring stages (tiles of 16 records): 8 steps
+constexpr int kMtpStep = 2 * kTile;   // tokens per step: two tiles per CTA barrier
+constexpr int kMtpHeads = 48;         // packed query heads of a group (rows x group size)
+constexpr int kMtpMTiles = 3;         // m16 tiles of packed heads
+constexpr int kMtpNT = 4;             // n8 tiles of P V per warp (32 dims)
+constexpr int kMtpFrags = kMtpMTiles * kMtpNT;  // O fragments per warp
+constexpr int kKhStride = 264;        // halfs per token row of the dequantised K tile (256 + 8: ldmatrix conflict-free)
+constexpr int kPhStride = 40;         // halfs per head row of the P tile (32 + 8: ldmatrix conflict-free)
+constexpr int kMtpRows = 4;           // rows per group (one S warp each)
+constexpr int kMtpMaxCluster = 8;     // splits of a group: one portable cluster
+constexpr int kMtpCompactIters = kMaxRange / kMtpThreads;
 
 struct __align__(128) SmemMtp {
-  // rec, kh and qf are contiguous: after the last tile they hold the cluster merge's published O.
-  uint8_t rec[kMtpStages][kStageBytes];   // gather ring, CTA-wide
+  uint8_t rec[kMtpRing][kStageBytes];     // gather ring; after the last tile it holds the published O
   __half kh[2][kMtpStep][kKhStride];      // dequantised K of a step, double-buffered
   uint4 qf[kMtpRows][16][33];             // Q A-fragments of each row: [row][k-step][lane] (+1: conflict-free stores)
   __half ph[2][kMtpHeads][kPhStride];     // P of a step (packed heads x tokens), double-buffered
-  int32_t sel[kMaxRange];                 // record rows (gather4) of the valid shared selections
+  int32_t sel[kMaxRange];                 // record rows (gather4) of the valid selections of the pass
   float alpha[2][kMtpHeads];              // rescale factor of each packed head (read only when its row rescaled)
-  int resc[2][kMtpRows];                  // row rescaled its running max in this tile
+  int resc[2][kMtpRows];                  // row rescaled its running max in this step
   float smul[kMtpHeads];
   float m_s[kMtpHeads];
   float l_s[kMtpHeads];
-  unsigned long long full_bar[kMtpStages];
-  int cnt[kCompactIters][kWarps];
+  unsigned long long full_bar[kMtpRing];
+  int cnt[kMtpCompactIters][kMtpWarps];
   int total;
   int abort;
   int shared_ok;
 };
-static_assert(sizeof(float4) * kWarps * 24 * 32 <=
-                  sizeof(SmemMtp::rec) + sizeof(SmemMtp::kh) + sizeof(SmemMtp::qf),
-              "published O must fit the ring, K and Q space");
+static_assert(sizeof(float4) * kMtpWarps * kMtpFrags * 32 <= sizeof(SmemMtp::rec), "published O must fit the ring");
+static_assert(sizeof(float) * kMtpMaxCluster * kMtpHeads <= sizeof(SmemMtp::ph), "merge weights must fit the P tile");
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
@@ -66,7 +76,7 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d
                : "r"(addr));
 }
 
-__global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(const __grid_constant__ AttnParams p) {
   pdl_enter();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   SmemMtp& sm = *reinterpret_cast<SmemMtp*>(smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u));
@@ -90,34 +100,33 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
 
   const int64_t chunks = (p.topk + kChunk - 1) / kChunk;
   const int my_chunks = split < chunks ? (int)((chunks - 1 - split) / p.splits + 1) : 0;  // <= kMaxChunks
-  const int iters = (my_chunks + kWarps - 1) / kWarps;
+  const int iters = (my_chunks + kMtpWarps - 1) / kMtpWarps;
 
   if (tid == 0) {
 #pragma unroll
-    for (int b = 0; b < kMtpStages; ++b) mbar_init(smem_u32(&sm.full_bar[b]), 1);
+    for (int b = 0; b < kMtpRing; ++b) mbar_init(smem_u32(&sm.full_bar[b]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     sm.abort = 0;
   }
 
   // Selections of row `prow` for this CTA's chunks -> record rows (gather4), -1 when masked
-  // (kernels.py:236-257).  Pass 0 always follows the group's first row, shared or not, so its
-  // selections and block-table entries are loaded before the sharing check below.
+  // (kernels.py:236-257).
   const bool huge_page = p.page_size > 0x7fffffffLL;
-  int32_t rowid[kCompactIters];
+  int32_t rowid[kMtpCompactIters];
   auto load_selections = [&](int64_t prow) {
     const int32_t req = __ldg(p.token_to_request + prow);
     const int32_t* idx_row = p.indices + prow * p.topk;
-    int32_t iv[kCompactIters];
+    int32_t iv[kMtpCompactIters];
 #pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
-      const int lc = it * kWarps + warp;
+    for (int it = 0; it < kMtpCompactIters; ++it) {
+      const int lc = it * kMtpWarps + warp;
       const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
       iv[it] = (lc < my_chunks && pos < p.topk) ? __ldg(idx_row + pos) : -1;
     }
     const bool req_ok = req >= 0 && (int64_t)req < p.num_requests;
     const int32_t* bt_row = p.block_table + (req_ok ? (int64_t)req * p.table_width : 0);
 #pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
+    for (int it = 0; it < kMtpCompactIters; ++it) {
       rowid[it] = -1;
       const int32_t idx = iv[it];
       if (req_ok && idx >= 0) {
@@ -130,7 +139,71 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
       }
     }
   };
+  // The valid selections, in chunk order, into sm.sel; returns their count (two CTA barriers).
+  auto compact = [&]() -> int {
+    uint32_t vmask = 0;
+    int pre[kMtpCompactIters];
+#pragma unroll
+    for (int it = 0; it < kMtpCompactIters; ++it) {
+      pre[it] = 0;
+      if (it < iters) {
+        const bool valid = rowid[it] >= 0;
+        const uint32_t b = __ballot_sync(0xffffffffu, valid);
+        pre[it] = __popc(b & ((1u << lane) - 1u));
+        if (valid) vmask |= 1u << it;
+        if (lane == 0) sm.cnt[it][warp] = __popc(b);
+      }
+    }
+    __syncthreads();
+    int base_all = 0;
+#pragma unroll
+    for (int it = 0; it < kMtpCompactIters; ++it) {
+      if (it < iters) {
+        int base = base_all;
+        for (int w = 0; w < warp; ++w) base += sm.cnt[it][w];
+        if (vmask & (1u << it)) sm.sel[base + pre[it]] = rowid[it];
+#pragma unroll
+        for (int w = 0; w < kMtpWarps; ++w) base_all += sm.cnt[it][w];
+      }
+    }
+    __syncthreads();
+    return base_all;
+  };
+
+  // Ring: tile k of a pass is global tile tiles_done + k, in stage (that) % kMtpRing.  Warp 4 issues.
+  int tiles_done = 0;  // tiles consumed in earlier passes: ring stage and phase carry over
+  auto issue_tile = [&](int k, int n) {
+    const int g = tiles_done + k;
+    const int st = g % kMtpRing;
+    const uint32_t bar = smem_u32(&sm.full_bar[st]);
+    const int j0 = k * kTile;
+    const int count = min(kTile, n - j0);
+    // the stage was last read by generic loads (ordered before the barrier that let us here)
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
+    __syncwarp();
+    if (lane < kTile / 4) {
+      int32_t rw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = group_token(lane, j);
+        rw[j] = t < count ? sm.sel[j0 + t] : p.total_rows;  // out of range: zero fill
+      }
+      gather4_g2s(smem_u32(&sm.rec[st][lane * 4 * kRecordBytes]), &p.rows_map, rw[0], rw[1], rw[2], rw[3], bar);
+    }
+  };
+  auto tile_wait = [&](int k) -> bool {
+    const int g = tiles_done + k;
+    return mbar_wait(smem_u32(&sm.full_bar[g % kMtpRing]), (uint32_t)((g / kMtpRing) & 1));
+  };
+
+  // pass 0 always follows the group's first row: its copies start before the sharing check
   load_selections(row_lo);
+  int n = compact();
+  if (warp == 4) {
+    const int nt = (n + kTile - 1) / kTile;
+    for (int k = 0; k < kMtpRing && k < nt; ++k) issue_tile(k, n);
+  }
 
   // ---------------- do the group's rows share request and selections (this CTA's chunks)? ----------------
   bool same = true;
@@ -139,8 +212,8 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     for (int i = 1; i < nrows; ++i) same &= __ldg(p.token_to_request + row_lo + i) == req0;
     const int32_t* idx0 = p.indices + row_lo * p.topk;
 #pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
-      const int lc = it * kWarps + warp;
+    for (int it = 0; it < kMtpCompactIters; ++it) {
+      const int lc = it * kMtpWarps + warp;
       const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
       if (lc < my_chunks && pos < p.topk) {
         const int32_t v0 = __ldg(idx0 + pos);
@@ -162,48 +235,87 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     cluster_sync();  // no rank rewrites shared_ok before every rank has read it
   }
   const int passes = same ? 1 : nrows;
-  int tiles_done = 0;  // tiles consumed in earlier passes: ring stage and phase carry over
+  bool aborted = false;
 
+  // ldmatrix row addresses: K (tokens x dims) for B of S, P (heads x tokens) for A of P V
+  const uint32_t kh_lane = (uint32_t)(((((lane >> 4) << 3) + (lane & 7)) * kKhStride + ((lane >> 3) & 1) * 8) * 2);
+  const uint32_t ph_lane = (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kPhStride + (lane >> 4) * 8) * 2);
+  const int vtok[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  const bool kwarp = warp >= kMtpRows;
+
+  // K warp 4 + j: dequantise dims [64j, 64j + 64) of tile kk (lane -> token lane/2, dims 64j + 32 (lane % 2) + [0, 32))
+  // into rows [16u, 16u + 16) of kh[buf]
+  auto dequant_k = [&](int kk, int buf, int u) {
+    const int j = warp - kMtpRows;
+    const int t = lane >> 1, h = lane & 1;
+    const uint8_t* rec = sm.rec[(tiles_done + kk) % kMtpRing] + slot_off(t);
+    const uint4 kb = *reinterpret_cast<const uint4*>(rec + 32 * j + 16 * h);
+    const uint32_t sc = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 4 * j + 2 * h));
+    const uint32_t s0 = dup_lo(sc), s1 = dup_hi(sc);
+    const uint32_t wd[4] = {kb.x, kb.y, kb.z, kb.w};
+    uint32_t o[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t sg = q < 2 ? s0 : s1;
+      o[4 * q + 0] = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(wd[q]), sg);
+      o[4 * q + 1] = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(wd[q]), sg);
+      o[4 * q + 2] = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(wd[q]), sg);
+      o[4 * q + 3] = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(wd[q]), sg);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(&sm.kh[buf][kTile * u + t][64 * j + 32 * h]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+  };
+
+  // Every rank of a cluster takes every pass (their cluster barriers must pair up), aborted or not.
   for (int pass = 0; pass < passes; ++pass) {
     const int64_t prow = same ? row_lo : row_lo + pass;  // row whose selections the gather follows
     const int act = same ? nrows : 1;                    // active S warps (rows) of this pass
-    bool aborted = sm.abort != 0;
-
-    // ---------------- prologue: selections (pass 0: loaded above), Q of the active rows ----------------
-    if (pass > 0) load_selections(prow);  // a group that does not share: row prow alone, on warp 0
-    // warp w loads row w's heads: lane L holds dims [8L, 8L + 8) of each head
-    uint32_t qw[16][4];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
-      if (warp < act && j < G) {
-        const __nv_bfloat16* qrow =
-            p.q + (prow + warp) * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
-        if (p.vec_q) {
-          const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
-          qw[j][0] = v.x; qw[j][1] = v.y; qw[j][2] = v.z; qw[j][3] = v.w;
-        } else {
-          const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
-#pragma unroll
-          for (int t = 0; t < 4; ++t) qw[j][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
-        }
+    const bool live = !aborted;                          // this pass issues copies
+    if (pass > 0 && live) {  // a group that does not share: row prow alone, on S warp 0
+      load_selections(prow);
+      n = compact();
+      if (warp == 4) {
+        const int nt = (n + kTile - 1) / kTile;
+        for (int k = 0; k < kMtpRing && k < nt; ++k) issue_tile(k, n);
       }
     }
-    // Q: per-head power-of-two pre-scale (exact) into f16 A-fragments of the row's m16 tile (natural
-    // dim order: k-step s covers dims [16s, 16s + 16)); heads >= G stay zero.
-    if (warp < kMtpRows) {
+    const int ntiles = (n + kTile - 1) / kTile;
+    const int nsteps = (ntiles + 1) / 2;
+
+    // ---------------- S warps: Q of their row; K warps: K of step 0 ----------------
+    bool ok = true;
+    if (!kwarp) {
+      // lane L holds dims [8L, 8L + 8) of each head of row `warp`
+      uint32_t qw[16][4];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
+        if (warp < act && j < G) {
+          const __nv_bfloat16* qrow =
+              p.q + (prow + warp) * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
+          if (p.vec_q) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
+            qw[j][0] = v.x; qw[j][1] = v.y; qw[j][2] = v.z; qw[j][3] = v.w;
+          } else {
+            const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) qw[j][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
+          }
+        }
+      }
+      // per-head power-of-two pre-scale (exact) into f16 A-fragments of the row's m16 tile (natural dim
+      // order: k-step s covers dims [16s, 16s + 16)); heads >= G stay zero
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         uint32_t amax = 0;
 #pragma unroll
         for (int t = 0; t < 4; ++t) amax = max(amax, max((qw[j][t] << 16) & 0x7fffffffu, qw[j][t] & 0x7fff0000u));
-#pragma unroll
-        for (int m = 16; m; m >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+        amax = __reduce_max_sync(0xffffffffu, amax);
         // scale 2^e brings the head's amax to [2^14, 2^15); |e| <= 100 keeps both products exact
         int e = 0;
         if (amax >= 0x00800000u && amax < 0x7f800000u) e = max(-100, min(100, 14 - ((int)(amax >> 23) - 127)));
-        if (lane == 0 && j < G && warp < act)
-          sm.smul[warp * G + j] = p.score_scale * __int_as_float((127 - e) << 23);
+        if (lane == 0 && j < G && warp < act) sm.smul[warp * G + j] = p.score_scale * __int_as_float((127 - e) << 23);
         const float mul = __int_as_float((127 + e) << 23);
         // lane L holds dims 8L..8L+7 = k-step L/2, columns 8(L%2)..+7: pairs (2cc, 2cc+1) of half L%2
         const int s = lane >> 1, hi = lane & 1;
@@ -215,133 +327,59 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
           f[((j & 7) * 4 + cc) * 4 + 2 * hi + (j >> 3)] = pack_half2(bf16_lo(x) * mul, bf16_hi(x) * mul);
         }
       }
-    }
-
-    // compact the valid selections
-    uint32_t vmask = 0;
-    int pre[kCompactIters];
-#pragma unroll
-    for (int it = 0; it < kCompactIters; ++it) {
-      pre[it] = 0;
-      if (it < iters) {
-        const bool valid = rowid[it] >= 0;
-        const uint32_t b = __ballot_sync(0xffffffffu, valid);
-        pre[it] = __popc(b & ((1u << lane) - 1u));
-        if (valid) vmask |= 1u << it;
-        if (lane == 0) sm.cnt[it][warp] = __popc(b);
+      // P rows of inactive heads stay zero for the whole pass
+      for (int i = tid; i < 2 * kMtpHeads * kPhStride / 2; i += 32 * kMtpRows)
+        reinterpret_cast<uint32_t*>(&sm.ph[0][0][0])[i] = 0u;
+    } else if (ntiles > 0 && live) {
+      ok &= tile_wait(0);
+      if (ok) dequant_k(0, 0, 0);
+      if (ntiles > 1) {
+        ok &= tile_wait(1);
+        if (ok) dequant_k(1, 0, 1);
       }
     }
-    // P rows of inactive heads stay zero for the whole pass
-    for (int i = tid; i < 2 * kMtpHeads * kPhStride / 2; i += kThreads) reinterpret_cast<uint32_t*>(&sm.ph[0][0][0])[i] = 0u;
-    __syncthreads();
-    {
-      int base_all = 0;
-#pragma unroll
-      for (int it = 0; it < kCompactIters; ++it) {
-        if (it < iters) {
-          int base = base_all;
-          for (int w = 0; w < warp; ++w) base += sm.cnt[it][w];
-          if (vmask & (1u << it)) sm.sel[base + pre[it]] = rowid[it];
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) base_all += sm.cnt[it][w];
-        }
-      }
-      if (tid == 0) sm.total = base_all;
+    if (!__syncthreads_and(ok)) {
+      aborted = true;
+      if (tid == 0) sm.abort = 1;
     }
-    __syncthreads();
-    const int n = sm.total;
-    const int ntiles = (n + kTile - 1) / kTile;
     if (tid == 0 && pass == 0) stamp_max(p, unit, 2);
 
-    // ---------------- CTA-wide gather ring: warp 0 issues, every warp consumes ----------------
-    auto issue_tile = [&](int k) {
-      const int st = (tiles_done + k) % kMtpStages;
-      const uint32_t bar = smem_u32(&sm.full_bar[st]);
-      const int j0 = k * kTile;
-      const int count = min(kTile, n - j0);
-      // the stage was last read by generic loads (ordered before the barrier that let us here)
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)kStageBytes);
-      __syncwarp();
-      if (lane < kTile / 4) {
-        int32_t rows[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int t = group_token(lane, j);
-          rows[j] = t < count ? sm.sel[j0 + t] : p.total_rows;  // out of range: zero fill
-        }
-        gather4_g2s(smem_u32(&sm.rec[st][lane * 4 * kRecordBytes]), &p.rows_map, rows[0], rows[1], rows[2], rows[3],
-                    bar);
-      }
-    };
-    if (warp == 0 && !aborted) {
-      for (int k = 0; k < 2 && k < ntiles; ++k) issue_tile(k);
-    }
-
-    float oacc[kMtpMTiles][8][4];
+    float oacc[kMtpMTiles][kMtpNT][4];
 #pragma unroll
     for (int t = 0; t < kMtpMTiles; ++t)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) oacc[t][j][0] = oacc[t][j][1] = oacc[t][j][2] = oacc[t][j][3] = 0.0f;
-    const bool srow = warp < act;  // this warp runs a row's scores and softmax
+      for (int j = 0; j < kMtpNT; ++j) oacc[t][j][0] = oacc[t][j][1] = oacc[t][j][2] = oacc[t][j][3] = 0.0f;
+    const bool srow = !kwarp && warp < act;  // this warp runs a row's scores and softmax
     const float smul_r = (srow && r < G) ? sm.smul[warp * G + r] : 1.0f;
     const float smul_r8 = (srow && r + 8 < G) ? sm.smul[warp * G + r + 8] : 1.0f;
     float m_r = kMaskedScore, m_r8 = kMaskedScore;
     float l_r = 0.0f, l_r8 = 0.0f;
-    // ldmatrix row addresses: K (tokens x dims) for B of S, P (heads x tokens) for A of P V
-    const uint32_t kh_lane = (uint32_t)(((((lane >> 4) << 3) + (lane & 7)) * kKhStride + ((lane >> 3) & 1) * 8) * 2);
-    const uint32_t ph_lane = (uint32_t)((((lane & 7) + ((lane >> 3) & 1) * 8) * kPhStride + (lane >> 4) * 8) * 2);
-    const int vtok[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
 
-    // Steps of two tiles (32 tokens): tile k sits in ring stage (tiles_done + k) % kMtpStages.  After the
-    // step's first barrier every warp is past the previous step's P V, so warp 0 refills those two stages
-    // with the next step's tiles.
-    const int nsteps = (ntiles + 1) / 2;
+    // Step i: S warps score tiles 2i, 2i+1 from kh[i & 1]; K warps dequantise tiles 2i+2, 2i+3 into
+    // kh[(i + 1) & 1] (warp 4 first refills the stages of step i-2, which every warp left before the
+    // previous barrier); barrier; every warp P V over tiles 2i, 2i+1.
     int i = 0;
     for (; i < nsteps && !aborted; ++i) {
       const int k0 = 2 * i;
       const bool two = k0 + 1 < ntiles;
       const int buf = i & 1;
-      bool ok = true;
-      // ---- K: warp w dequantises dims [64w, 64w + 64); lane -> token lane/2 of each tile, dims 64w + 32 (lane % 2) + [0, 32) ----
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        if (u == 1 && !two) break;
-        const int kk = k0 + u;
-        const int st = (tiles_done + kk) % kMtpStages;
-        ok &= mbar_wait(smem_u32(&sm.full_bar[st]), (uint32_t)(((tiles_done + kk) / kMtpStages) & 1));
-        const int t = lane >> 1, h = lane & 1;
-        const uint8_t* rec = sm.rec[st] + slot_off(t);
-        const uint4 kb = *reinterpret_cast<const uint4*>(rec + 32 * warp + 16 * h);
-        const uint32_t sc = cvt_e4m3x2_f16x2(*reinterpret_cast<const uint16_t*>(rec + 128 + 4 * warp + 2 * h));
-        const uint32_t s0 = dup_lo(sc), s1 = dup_hi(sc);
-        const uint32_t wd[4] = {kb.x, kb.y, kb.z, kb.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t sg = q < 2 ? s0 : s1;
-          o[4 * q + 0] = hmul2_u32(cvt_e2m1x2_f16x2_byte<0>(wd[q]), sg);
-          o[4 * q + 1] = hmul2_u32(cvt_e2m1x2_f16x2_byte<1>(wd[q]), sg);
-          o[4 * q + 2] = hmul2_u32(cvt_e2m1x2_f16x2_byte<2>(wd[q]), sg);
-          o[4 * q + 3] = hmul2_u32(cvt_e2m1x2_f16x2_byte<3>(wd[q]), sg);
+      bool okk = true;
+      if (kwarp) {
+        if (warp == 4 && i >= 2) {
+          if (k0 + kMtpRing - 4 < ntiles) issue_tile(k0 + kMtpRing - 4, n);
+          if (k0 + kMtpRing - 3 < ntiles) issue_tile(k0 + kMtpRing - 3, n);
         }
-        uint4* dst = reinterpret_cast<uint4*>(&sm.kh[buf][kTile * u + t][64 * warp + 32 * h]);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) dst[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-      }
-      if (!__syncthreads_and(ok)) {  // (A) K of the step complete; every warp is past the previous step's P V
-        if (tid == 0) sm.abort = 1;
-        aborted = true;
-        break;
-      }
-      if (warp == 0) {
-        if (k0 + 2 < ntiles) issue_tile(k0 + 2);  // into the stages of tiles k0 - 2 and k0 - 1
-        if (k0 + 3 < ntiles) issue_tile(k0 + 3);
-      }
-
-      // ---- S = Q K^T for row `warp` over the step's 32 tokens, online softmax, P into the packed tile ----
-      // (a missing second tile leaves stale K rows: their scores are masked below)
-      if (srow) {
+        for (int u = 0; u < 2; ++u) {
+          const int kk = k0 + 2 + u;
+          if (kk < ntiles) {
+            okk &= tile_wait(kk);
+            if (okk) dequant_k(kk, buf ^ 1, u);
+          }
+        }
+      } else if (srow) {
+        // ---- S = Q K^T for row `warp` over the step's 32 tokens, online softmax, P into the packed tile ----
+        // (a missing second tile leaves stale K rows: their scores are masked below)
         float sacc[4][4];
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
@@ -422,9 +460,13 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
       } else if (lane == 0) {
         sm.resc[buf][warp] = 0;
       }
-      __syncthreads();  // (B) P and the rescale factors of every row are in place
+      if (!__syncthreads_and(okk)) {  // P of step i and K of step i+1 in place; every warp past P V of step i-1
+        if (tid == 0) sm.abort = 1;
+        aborted = true;
+        break;
+      }
 
-      // ---- O += P V over dims [64w, 64w + 64) of every packed head, one k-step per tile ----
+      // ---- O += P V over dims [32w, 32w + 32) of every packed head, one k-step per tile ----
       {
         const int any = sm.resc[buf][0] | sm.resc[buf][1] | sm.resc[buf][2] | sm.resc[buf][3];
         if (any) {
@@ -436,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
               const int hrow = head / G;
               const float a = (head < act * G && sm.resc[buf][hrow]) ? sm.alpha[buf][head] : 1.0f;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
+              for (int j = 0; j < kMtpNT; ++j) {
                 oacc[t][j][2 * hh] *= a;
                 oacc[t][j][2 * hh + 1] *= a;
               }
@@ -446,28 +488,28 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           if (u == 1 && !two) break;  // no stale V enters O
-          const uint8_t* stage = sm.rec[(tiles_done + k0 + u) % kMtpStages];
+          const uint8_t* stage = sm.rec[(tiles_done + k0 + u) % kMtpRing];
           uint32_t pa[kMtpMTiles][4];
           const uint32_t paddr = smem_u32(&sm.ph[buf][0][0]) + ph_lane + (uint32_t)(kTile * 2 * u);
 #pragma unroll
           for (int t = 0; t < kMtpMTiles; ++t)
             ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
-          // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9} of the tile, dims 64w + 8r + [0, 8)
+          // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9} of the tile, dims 32w + 4r + [0, 4) (two bytes of V codes)
           uint32_t vw[4], vsb[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint8_t* rec = stage + slot_off(vtok[q]);
-            vw[q] = *reinterpret_cast<const uint32_t*>(rec + 144 + 32 * warp + 4 * r);
-            vsb[q] = rec[272 + 4 * warp + (r >> 1)];
+            vw[q] = *reinterpret_cast<const uint16_t*>(rec + 144 + 16 * warp + 2 * r);
+            vsb[q] = rec[272 + 2 * warp + (r >> 2)];
           }
           const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
           const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
           // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
-          const uint32_t x01 = (vw[0] & 0x0f0f0f0fu) | ((vw[1] & 0x0f0f0f0fu) << 4);
-          const uint32_t y01 = ((vw[0] >> 4) & 0x0f0f0f0fu) | (vw[1] & 0xf0f0f0f0u);
-          const uint32_t x23 = (vw[2] & 0x0f0f0f0fu) | ((vw[3] & 0x0f0f0f0fu) << 4);
-          const uint32_t y23 = ((vw[2] >> 4) & 0x0f0f0f0fu) | (vw[3] & 0xf0f0f0f0u);
-          // n-tile 2B + x, column n <-> dim 64w + 8n + 2B + x
+          const uint32_t x01 = (vw[0] & 0x0f0fu) | ((vw[1] & 0x0f0fu) << 4);
+          const uint32_t y01 = ((vw[0] >> 4) & 0x0f0fu) | (vw[1] & 0xf0f0u);
+          const uint32_t x23 = (vw[2] & 0x0f0fu) | ((vw[3] & 0x0f0fu) << 4);
+          const uint32_t y23 = ((vw[2] >> 4) & 0x0f0fu) | (vw[3] & 0xf0f0u);
+          // n-tile 2B + x, column n <-> dim 32w + 4n + 2B + x
 #define NVQSA_MTP_PV_BYTE(B)                                                                     \
   {                                                                                              \
     const uint32_t bx0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x01), s01);                         \
@@ -481,17 +523,17 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
   }
           NVQSA_MTP_PV_BYTE(0)
           NVQSA_MTP_PV_BYTE(1)
-          NVQSA_MTP_PV_BYTE(2)
-          NVQSA_MTP_PV_BYTE(3)
 #undef NVQSA_MTP_PV_BYTE
         }
       }
     }
-    if (aborted && warp == 0) {
+    if (aborted && live && warp == 4) {
       // let copies still in flight land (bounded) before the ring is reused or released
-      for (int k2 = 2 * i; k2 < ntiles && k2 < 2 * i + 2; ++k2)
-        mbar_wait(smem_u32(&sm.full_bar[(tiles_done + k2) % kMtpStages]),
-                  (uint32_t)(((tiles_done + k2) / kMtpStages) & 1), kDrainSpinLimit);
+      // tiles below 2i were waited for; warp 4 issued up to tile max(16, 2i + 14) - 1
+      for (int k2 = 2 * i; k2 < ntiles && k2 < max(kMtpRing, 2 * i + kMtpRing - 2); ++k2) {
+        const int g = tiles_done + k2;
+        mbar_wait(smem_u32(&sm.full_bar[g % kMtpRing]), (uint32_t)((g / kMtpRing) & 1), kDrainSpinLimit);
+      }
     }
     tiles_done += ntiles;
 
@@ -508,22 +550,23 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
     aborted = sm.abort != 0;
     if (tid == 0 && pass == passes - 1) stamp_max(p, unit, 1);
 
-    // bf16 output of packed head `head` (< act * G), dims d0 and d1
+    // bf16 output of packed head `head` (< act * G)
     auto out_ptr = [&](int head) {
       const int hrow = head / G, j = head - hrow * G;
       return p.out + (prow + hrow) * p.o_stride_row + (int64_t)(kvh * G + j) * p.o_stride_head;
     };
     if (p.cluster > 1) {
       // Every rank publishes its (O, m, l); then every rank merges one slice of the O fragments of all ranks
-      // (fragment f = 8t + n-tile of each warp, slice [24 rank / cluster, 24 (rank + 1) / cluster)) over
+      // (fragment f = 4t + n-tile of each warp, slice [12 rank / cluster, 12 (rank + 1) / cluster)) over
       // distributed shared memory and stores it, with per-head weights 2^(m_rank - M) / sum computed once.
-      float4* pub = reinterpret_cast<float4*>(&sm.rec[0][0]);  // [warp][24][32]
+      float4* pub = reinterpret_cast<float4*>(&sm.rec[0][0]);  // [warp][12][32]
       if (!aborted) {
 #pragma unroll
         for (int t = 0; t < kMtpMTiles; ++t)
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            pub[(warp * 24 + t * 8 + j) * 32 + lane] = make_float4(oacc[t][j][0], oacc[t][j][1], oacc[t][j][2], oacc[t][j][3]);
+          for (int j = 0; j < kMtpNT; ++j)
+            pub[(warp * kMtpFrags + t * kMtpNT + j) * 32 + lane] =
+                make_float4(oacc[t][j][0], oacc[t][j][1], oacc[t][j][2], oacc[t][j][3]);
       }
       cluster_sync();
       const int rank = split % p.cluster;
@@ -555,35 +598,43 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
           if (rk < p.cluster) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
       }
       if (!__syncthreads_or(bad_rank)) {  // weights in place; no rank gave up
-        const int f_lo = rank * 24 / p.cluster, f_hi = (rank + 1) * 24 / p.cluster;
-        for (int f = f_lo; f < f_hi; ++f) {
-          const int t = f >> 3, jn = f & 7;
-          const int h0 = 16 * t + r, h1 = h0 + 8;
-          const bool l0 = h0 < act * G, l1 = h1 < act * G;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          const uint32_t off = (uint32_t)((warp * 24 + f) * 32 + lane) * 16u;
-          float4 v[kMtpMaxCluster];
+        const int f_lo = rank * kMtpFrags / p.cluster, f_hi = (rank + 1) * kMtpFrags / p.cluster;
+        for (int f0 = f_lo; f0 < f_hi; f0 += 2) {  // two fragments' loads of every rank in flight at once
+          float4 v[2][kMtpMaxCluster];
 #pragma unroll
-          for (int rk = 0; rk < kMtpMaxCluster; ++rk)  // every rank's fragment in flight at once
-            v[rk] = rk < p.cluster ? cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int q = 0; q < 2; ++q) {
+            const uint32_t off = (uint32_t)((warp * kMtpFrags + min(f0 + q, f_hi - 1)) * 32 + lane) * 16u;
 #pragma unroll
-          for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
-            if (rk >= p.cluster) break;
-            const float w0 = l0 ? wts[rk * kMtpHeads + h0] : 0.0f, w1 = l1 ? wts[rk * kMtpHeads + h1] : 0.0f;
-            acc.x += w0 * v[rk].x; acc.y += w0 * v[rk].y; acc.z += w1 * v[rk].z; acc.w += w1 * v[rk].w;
+            for (int rk = 0; rk < kMtpMaxCluster; ++rk)
+              v[q][rk] = rk < p.cluster ? cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
           }
-          // n-tile jn, columns 2c and 2c+1: dims 64w + 16c + jn and 64w + 16c + 8 + jn
-          const int d = 64 * warp + 16 * c + jn;
-          if (l0) {
-            __nv_bfloat16* op = out_ptr(h0);
-            op[d] = __float2bfloat16_rn(acc.x);
-            op[d + 8] = __float2bfloat16_rn(acc.y);
-          }
-          if (l1) {
-            __nv_bfloat16* op = out_ptr(h1);
-            op[d] = __float2bfloat16_rn(acc.z);
-            op[d + 8] = __float2bfloat16_rn(acc.w);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int f = f0 + q;
+            if (f >= f_hi) break;
+            const int t = f / kMtpNT, jn = f - t * kMtpNT;
+            const int h0 = 16 * t + r, h1 = h0 + 8;
+            const bool l0 = h0 < act * G, l1 = h1 < act * G;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
+              if (rk >= p.cluster) break;
+              const float w0 = l0 ? wts[rk * kMtpHeads + h0] : 0.0f, w1 = l1 ? wts[rk * kMtpHeads + h1] : 0.0f;
+              acc.x += w0 * v[q][rk].x; acc.y += w0 * v[q][rk].y; acc.z += w1 * v[q][rk].z; acc.w += w1 * v[q][rk].w;
+            }
+            // n-tile jn, columns 2c and 2c+1: dims 32w + 8c + jn and 32w + 8c + 4 + jn
+            const int d = 32 * warp + 8 * c + jn;
+            if (l0) {
+              __nv_bfloat16* op = out_ptr(h0);
+              op[d] = __float2bfloat16_rn(acc.x);
+              op[d + 4] = __float2bfloat16_rn(acc.y);
+            }
+            if (l1) {
+              __nv_bfloat16* op = out_ptr(h1);
+              op[d] = __float2bfloat16_rn(acc.z);
+              op[d + 4] = __float2bfloat16_rn(acc.w);
+            }
           }
         }
       }
@@ -599,27 +650,19 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_attention_mtp_kernel(const
           const float l = sm.l_s[head];
           // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
           const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
-          // dims 64w + 16c + i (n = 2c, n-tile i) and 64w + 16c + 8 + i (n = 2c + 1)
-          uint32_t wv[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            __nv_bfloat162 lo2 = __floats2bfloat162_rn(oacc[t][2 * i][2 * hh] * inv, oacc[t][2 * i + 1][2 * hh] * inv);
-            __nv_bfloat162 hi2 =
-                __floats2bfloat162_rn(oacc[t][2 * i][2 * hh + 1] * inv, oacc[t][2 * i + 1][2 * hh + 1] * inv);
-            wv[i] = *reinterpret_cast<uint32_t*>(&lo2);
-            wv[4 + i] = *reinterpret_cast<uint32_t*>(&hi2);
-          }
-          __nv_bfloat16* op = out_ptr(head) + 64 * warp + 16 * c;
+          // dims 32w + 8c + j (column 2c of n-tile j) and 32w + 8c + 4 + j (column 2c + 1)
+          __nv_bfloat162 w2[4];
+          w2[0] = __floats2bfloat162_rn(oacc[t][0][2 * hh] * inv, oacc[t][1][2 * hh] * inv);
+          w2[1] = __floats2bfloat162_rn(oacc[t][2][2 * hh] * inv, oacc[t][3][2 * hh] * inv);
+          w2[2] = __floats2bfloat162_rn(oacc[t][0][2 * hh + 1] * inv, oacc[t][1][2 * hh + 1] * inv);
+          w2[3] = __floats2bfloat162_rn(oacc[t][2][2 * hh + 1] * inv, oacc[t][3][2 * hh + 1] * inv);
+          __nv_bfloat16* op = out_ptr(head) + 32 * warp + 8 * c;
           if (p.vec_o) {
-            reinterpret_cast<uint4*>(op)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            reinterpret_cast<uint4*>(op)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            *reinterpret_cast<uint4*>(op) = *reinterpret_cast<const uint4*>(w2);
           } else {
-            unsigned short* os = reinterpret_cast<unsigned short*>(op);
+            const unsigned short* ws = reinterpret_cast<const unsigned short*>(w2);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              os[2 * i] = (unsigned short)(wv[i] & 0xffffu);
-              os[2 * i + 1] = (unsigned short)(wv[i] >> 16);
-            }
+            for (int q = 0; q < 8; ++q) reinterpret_cast<unsigned short*>(op)[q] = ws[q];
           }
         }
       }

@@ -9,19 +9,28 @@
 // scores of positions [0, length) -- its causal context -- the indices of the k
 // largest, written in ascending index order; ties at the k-th value go to the
 // lowest indices; a context shorter than k yields 0 .. length - 1 and -1 after.
-// NaN ranks above every number (torch.topk's order).
+// NaN ranks above every number (torch.topk's order); -0 equals +0.
 //
-// One CTA of 512 threads per row, everything in one launch:
-//   1. radix select on an order-preserving 32-bit key of each score: three
-//      histogram passes over digits of 11, 11 and 10 bits (shared-memory
-//      histograms), each narrowing the candidates to the bin that holds the
-//      k-th largest key, give that key T exactly and the count of keys above it;
-//   2. one ordered collection pass: in rounds of 512 consecutive positions,
-//      a position is selected when its key is above T, or equal to T while the
-//      tie budget lasts; warp ballots and a block scan place each selected
-//      index at its rank, so the output comes out sorted with no sort.
-// Reads are coalesced (position = round * 512 + thread); the row's later passes
-// are served from L2.
+// One CTA of 32 warps per row; warp w owns the w-th of 32 consecutive
+// position ranges of the row (a multiple of 32 positions each), so position
+// order is warp order.  On an order-preserving 32-bit key of each score:
+//   1. the CTA histograms the top 11 bits and finds the bin b1 holding the
+//      k-th largest key (shared atomics into 8 sub-histograms, one per four
+//      warps: score distributions put most keys in a few top-bit bins, and
+//      one shared histogram serialises its hot bins);
+//   2. every warp re-reads its range (from L2): it counts the keys above b1
+//      and keeps the keys inside b1 in a per-warp candidate list, while the
+//      CTA histograms their next 11 bits -> bin b2;
+//   3. the candidates inside (b1, b2) histogram their last 10 bits -> the k-th
+//      largest key T exactly, and how many keys equal to T are selected;
+//   4. per-warp counts of keys above T and equal to T, scanned over the
+//      warps, give every warp its output offset and its share of the ties
+//      (lowest positions first);
+//   5. every warp re-reads its range in order and writes the selected
+//      positions with warp ballots: the output comes out sorted with no sort.
+// A warp whose candidates overflow its list recomputes steps 3 and 4 from its
+// range in global memory instead (many equal scores); the result is the same.
+// Every output store is bounds-checked against k.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -30,28 +39,48 @@
 namespace nvqsa {
 namespace {
 
-constexpr int kTopkThreads = 512;
-constexpr int kTopkWarps = kTopkThreads / 32;
-constexpr int kMaxBins = 2048;
+constexpr int kTkThreads = 1024;
+constexpr int kTkWarps = kTkThreads / 32;
+constexpr int kTkBins = 2048;          // 11-bit digits (the last digit has 10 bits)
+constexpr int kTkCandPerWarp = 192;    // candidate keys kept per warp
+constexpr int kTkUnroll = 8;           // loads in flight per lane
+constexpr int kTkSubHists = 8;         // histogram copies (warp w adds into copy w / 4)
 
 struct TopkParams {
   const float* scores;
-  int64_t score_stride;  // elements between rows
+  int64_t score_stride;    // elements between rows
   const int32_t* lengths;  // [rows] valid positions per row, or nullptr: all `context`
   int64_t rows, context;
   int32_t k;
   int32_t* out;
-  int64_t out_stride;    // elements between rows
+  int64_t out_stride;      // elements between rows
 };
 
-// Order-preserving key: a larger float gives a larger unsigned key; NaN gets the largest key.
+struct TopkSmem {
+  int hist[kTkSubHists][kTkBins];
+  uint32_t ckey[kTkWarps][kTkCandPerWarp];
+  int warp_sums[kTkWarps];
+  int wgt[kTkWarps];   // keys above T, per warp
+  int weq[kTkWarps];   // keys equal to T, per warp
+  uint32_t s_bin;
+  int s_need;
+};
+
+// Order-preserving key: a larger float gives a larger unsigned key; NaN gets the largest key; -0 equals +0.
 __device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t b = __float_as_uint(f);
+  uint32_t b = __float_as_uint(f);
   if ((b & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
+  if (b == 0x80000000u) b = 0u;
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Exclusive prefix sum over the block of one value per thread; returns the thread's prefix, `total` the sum.
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int m = 16; m; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Exclusive prefix sum over the block of one value per thread; `total` gets the sum.
 __device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int x = v;
@@ -63,124 +92,215 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int& total) {
   if (lane == 31) warp_sums[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = lane < kTopkWarps ? warp_sums[lane] : 0;
+    int w = warp_sums[lane];
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, w, d);
       if (lane >= d) w += y;
     }
-    if (lane < kTopkWarps) warp_sums[lane] = w;  // inclusive warp prefix
+    warp_sums[lane] = w;  // inclusive prefix over the warps
   }
   __syncthreads();
-  total = warp_sums[kTopkWarps - 1];
+  total = warp_sums[kTkWarps - 1];
   const int before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
-  __syncthreads();  // warp_sums may be reused by the caller's next scan
+  __syncthreads();  // warp_sums may be reused by the next scan
   return before;
 }
 
-__global__ void __launch_bounds__(kTopkThreads) topk_indices_kernel(const TopkParams p) {
-  __shared__ int hist[kMaxBins];
-  __shared__ int warp_sums[kTopkWarps];
-  __shared__ uint32_t s_prefix;
-  __shared__ int s_need;       // rank of the k-th key among the candidates of the current pass (1-based)
-  __shared__ int s_above;      // keys known to be above every remaining candidate
-
-  const int64_t row = blockIdx.x;
+// Finds the bin of hist[0, nbins) holding the need-th largest key, counting from the top bin down; returns it
+// and leaves the key's rank inside the bin in s_need.
+__device__ __forceinline__ uint32_t select_bin(TopkSmem& sm, int nbins, int need) {
   const int tid = threadIdx.x;
+  const int per = nbins / kTkThreads;  // 2 or 1: thread t owns bins [nbins - (t + 1) per, nbins - t per)
+  int c0 = 0, c1 = 0;
+#pragma unroll
+  for (int h = 0; h < kTkSubHists; ++h) {
+    c0 += sm.hist[h][nbins - 1 - tid * per];
+    if (per > 1) c1 += sm.hist[h][nbins - 2 - tid * per];
+  }
+  int total;
+  const int before = block_scan(c0 + c1, sm.warp_sums, total);  // keys in the bins above this thread's
+  if (before < need && before + c0 + c1 >= need) {
+    if (before + c0 >= need) {
+      sm.s_bin = (uint32_t)(nbins - 1 - tid * per);
+      sm.s_need = need - before;
+    } else {
+      sm.s_bin = (uint32_t)(nbins - 2 - tid * per);
+      sm.s_need = need - before - c0;
+    }
+  }
+  __syncthreads();
+  return sm.s_bin;
+}
+
+__global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkParams p) {
+  extern __shared__ __align__(16) uint8_t tk_smem_raw[];
+  TopkSmem& sm = *reinterpret_cast<TopkSmem*>(tk_smem_raw);
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
   const float* srow = p.scores + row * p.score_stride;
   int32_t* orow = p.out + row * p.out_stride;
-  int64_t len = p.lengths ? (int64_t)p.lengths[row] : p.context;
+  int64_t len = p.lengths ? (int64_t)__ldg(p.lengths + row) : p.context;
   len = len < 0 ? 0 : (len > p.context ? p.context : len);
   const int k = p.k;
 
   if (len <= k) {  // everything valid is selected, in order; the rest is padding
-    for (int64_t i = tid; i < k; i += kTopkThreads) orow[i] = i < len ? (int32_t)i : -1;
+    for (int64_t i = tid; i < k; i += kTkThreads) orow[i] = i < len ? (int32_t)i : -1;
     return;
   }
 
-  // ---------------- 1. radix select: digits of 11, 11 and 10 bits from the top ----------------
-  uint32_t prefix = 0, pmask = 0;
-  if (tid == 0) {
-    s_need = k;
-    s_above = 0;
-  }
-  const int shifts[3] = {21, 10, 0};
-  const int widths[3] = {11, 11, 10};
-#pragma unroll 1
-  for (int pass = 0; pass < 3; ++pass) {
-    const int shift = shifts[pass], bins = 1 << widths[pass];
-    for (int i = tid; i < bins; i += kTopkThreads) hist[i] = 0;
-    __syncthreads();
-    for (int64_t i = tid; i < len; i += kTopkThreads) {
-      const uint32_t key = order_key(__ldg(srow + i));
-      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & (bins - 1)], 1);
+  // this warp's positions [lo, hi): the warp-th of 32 ranges of a multiple of 32 positions
+  const int64_t span = (((len + kTkWarps - 1) / kTkWarps) + 31) & ~(int64_t)31;
+  const int64_t lo = min(len, (int64_t)warp * span);
+  const int64_t hi = min(len, lo + span);
+  int* hist = sm.hist[warp / (kTkWarps / kTkSubHists)];
+
+  for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
+  __syncthreads();
+
+  // ---- 1. top 11 bits ----
+  for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+    float v[kTkUnroll];
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const int64_t pos = b + u * 32 + lane;
+      v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
     }
-    __syncthreads();
-    // Counts from the top bin down: thread t owns bins [bins - (t + 1) * per, bins - t * per).
-    const int per = bins / kTopkThreads;  // 4 or 2
-    int mine = 0;
-    for (int j = 0; j < per; ++j) mine += hist[bins - 1 - (tid * per + j)];
-    const int need = s_need;  // read before the scan's barriers: the winner below rewrites it
-    int total;
-    const int before = block_scan(mine, warp_sums, total);  // keys in bins above this thread's range
-    if (before < need && before + mine >= need) {
-      // the k-th candidate lies in this thread's range: walk it from the top
-      int acc = before;
-      for (int j = 0; j < per; ++j) {
-        const int bin = bins - 1 - (tid * per + j);
-        const int c = hist[bin];
-        if (acc + c >= need) {
-          s_prefix = prefix | ((uint32_t)bin << shift);
-          s_need = need - acc;
-          s_above += acc;
-          break;
-        }
-        acc += c;
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u)
+      if (b + u * 32 + lane < hi) atomicAdd(&hist[order_key(v[u]) >> 21], 1);
+  }
+  __syncthreads();
+  const uint32_t b1 = select_bin(sm, kTkBins, k);
+  const int need1 = sm.s_need;
+  for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
+  __syncthreads();
+
+  // ---- 2. keys above b1 counted, keys inside b1 kept as candidates; their next 11 bits ----
+  int gt = 0, ncand = 0;
+  for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+    float v[kTkUnroll];
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const int64_t pos = b + u * 32 + lane;
+      v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const bool valid = b + u * 32 + lane < hi;
+      const uint32_t key = order_key(v[u]);
+      const uint32_t d1 = key >> 21;
+      gt += (valid && d1 > b1) ? 1 : 0;
+      const bool in = valid && d1 == b1;
+      const uint32_t m = __ballot_sync(0xffffffffu, in);
+      if (in) {
+        const int idx = ncand + __popc(m & lt_mask);
+        if (idx < kTkCandPerWarp) sm.ckey[warp][idx] = key;
+        atomicAdd(&hist[(key >> 10) & (kTkBins - 1)], 1);
+      }
+      ncand += __popc(m);
+    }
+  }
+  gt = warp_sum(gt);
+  __syncthreads();
+  const uint32_t b2 = select_bin(sm, kTkBins, need1);
+  const int need2 = sm.s_need;
+  for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
+  __syncthreads();
+  const uint32_t prefix22 = (b1 << 11) | b2;
+  const bool listed = ncand <= kTkCandPerWarp;  // warp-uniform
+
+  // ---- 3. last 10 bits of the candidates inside (b1, b2) ----
+  if (listed) {
+    for (int i = lane; i < ncand; i += 32) {
+      const uint32_t key = sm.ckey[warp][i];
+      if ((key >> 10) == prefix22) atomicAdd(&hist[key & 1023u], 1);
+    }
+  } else {
+    for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+      float v[kTkUnroll];
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const int64_t pos = b + u * 32 + lane;
+        v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const uint32_t key = order_key(v[u]);
+        if (b + u * 32 + lane < hi && (key >> 10) == prefix22) atomicAdd(&hist[key & 1023u], 1);
       }
     }
-    __syncthreads();
-    prefix = s_prefix;
-    pmask |= (uint32_t)(bins - 1) << shift;
   }
-  const uint32_t T = prefix;     // the k-th largest key
-  const int ties = s_need;       // how many keys equal to T are selected (the lowest positions)
+  __syncthreads();
+  const uint32_t T = (prefix22 << 10) | select_bin(sm, 1024, need2);
+  const int ties = sm.s_need;  // keys equal to T that are selected: the lowest positions
 
-  // ---------------- 2. ordered collection ----------------
-  const int lane = tid & 31, warp = tid >> 5;
-  int base = 0, ties_used = 0;   // block-uniform running counts
-#pragma unroll 1
-  for (int64_t r0 = 0; r0 < len; r0 += kTopkThreads) {
-    const int64_t i = r0 + tid;
-    uint32_t key = 0;
-    if (i < len) key = order_key(__ldg(srow + i));
-    const bool gt = i < len && key > T;
-    const bool eq = i < len && key == T;
-    // ties in index order: rank among this round's ties, offset by the ties already taken
-    const uint32_t eq_b = __ballot_sync(0xffffffffu, eq);
-    const uint32_t gt_b = __ballot_sync(0xffffffffu, gt);
-    if (lane == 0) {
-      hist[warp] = __popc(eq_b);
-      hist[kTopkWarps + warp] = __popc(gt_b);
+  // ---- 4. per-warp counts above and at T; offsets over the warps ----
+  int wg = 0, we = 0;
+  if (listed) {
+    for (int i = lane; i < ncand; i += 32) {
+      const uint32_t key = sm.ckey[warp][i];
+      wg += key > T ? 1 : 0;
+      we += key == T ? 1 : 0;
     }
-    __syncthreads();
-    int eq_before = 0, gt_before = 0, eq_round = 0, gt_round = 0;
-    for (int w = 0; w < kTopkWarps; ++w) {
-      const int e = hist[w], g = hist[kTopkWarps + w];
-      if (w < warp) { eq_before += e; gt_before += g; }
-      eq_round += e;
-      gt_round += g;
+    wg = gt + warp_sum(wg);
+  } else {
+    for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+      float v[kTkUnroll];
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const int64_t pos = b + u * 32 + lane;
+        v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const bool valid = b + u * 32 + lane < hi;
+        const uint32_t key = order_key(v[u]);
+        wg += (valid && key > T) ? 1 : 0;
+        we += (valid && key == T) ? 1 : 0;
+      }
     }
-    __syncthreads();  // hist is rewritten by the next round
-    const uint32_t below = (1u << lane) - 1u;
-    const int my_eq_rank = ties_used + eq_before + __popc(eq_b & below);
-    const bool take = gt || (eq && my_eq_rank < ties);
-    // selected before this position in this round: all gt before it, ties before it within the budget
-    const int eq_taken_before = min(max(ties - ties_used, 0), eq_before + __popc(eq_b & below));
-    if (take) orow[base + gt_before + __popc(gt_b & below) + eq_taken_before] = (int32_t)i;
-    const int eq_taken_round = min(max(ties - ties_used, 0), eq_round);
-    base += gt_round + eq_taken_round;
-    ties_used += eq_taken_round;
-    if (base >= k) break;
+    wg = warp_sum(wg);
+  }
+  we = warp_sum(we);
+  if (lane == 0) {
+    sm.wgt[warp] = wg;
+    sm.weq[warp] = we;
+  }
+  __syncthreads();
+  int64_t gt_before = 0, eq_before = 0;
+  for (int w = 0; w < warp; ++w) {
+    gt_before += sm.wgt[w];
+    eq_before += sm.weq[w];
+  }
+  const int64_t sel_before = gt_before + min((int64_t)ties, eq_before);
+  const int64_t take_ties = max((int64_t)0, min((int64_t)we, (int64_t)ties - eq_before));
+  const int64_t sel = (int64_t)wg + take_ties;
+
+  // ---- 5. selected positions in order: ballots over 32 consecutive positions ----
+  int64_t written = 0, eq_seen = eq_before;
+  for (int64_t b = lo; b < hi && written < sel; b += 32 * kTkUnroll) {
+    float v[kTkUnroll];
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const int64_t pos = b + u * 32 + lane;
+      v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kTkUnroll; ++u) {
+      const int64_t pos = b + u * 32 + lane;
+      const uint32_t key = order_key(v[u]);
+      const bool valid = pos < hi;
+      const bool g = valid && key > T, e = valid && key == T;
+      const uint32_t em = __ballot_sync(0xffffffffu, e);
+      const bool take = g || (e && eq_seen + __popc(em & lt_mask) < ties);
+      const uint32_t tm = __ballot_sync(0xffffffffu, take);
+      const int64_t oi = sel_before + written + __popc(tm & lt_mask);
+      if (take && oi < k) orow[oi] = (int32_t)pos;
+      written += __popc(tm);
+      eq_seen += __popc(em);
+    }
   }
 }
 
@@ -195,7 +315,7 @@ extern "C" int nvqsa_topk_indices(const float* scores, int64_t score_stride_row,
     return NVQSA_ERR_BAD_SHAPE;
   if (rows == 0) return NVQSA_OK;
   if (!out || (!scores && context > 0)) return NVQSA_ERR_NULL_POINTER;
-  if (rows > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;
+  if (rows > 0x7fffffffLL || context > 0x7fffffffLL) return NVQSA_ERR_BAD_SHAPE;  // grid and int32 positions
   TopkParams p;
   p.scores = scores;
   p.score_stride = score_stride_row;
@@ -205,6 +325,15 @@ extern "C" int nvqsa_topk_indices(const float* scores, int64_t score_stride_row,
   p.k = k;
   p.out = out;
   p.out_stride = out_stride_row;
-  topk_indices_kernel<<<(unsigned)rows, kTopkThreads, 0, as_stream(stream)>>>(p);
+  static std::atomic<bool> configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NVQSA_ERR_CUDA;
+  if (!configured[dev].load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(topk_indices_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TopkSmem)) != cudaSuccess)
+      return NVQSA_ERR_CUDA;
+    configured[dev].store(true, std::memory_order_relaxed);
+  }
+  topk_indices_kernel<<<(unsigned)rows, kTkThreads, sizeof(TopkSmem), as_stream(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }

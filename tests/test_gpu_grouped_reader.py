@@ -67,6 +67,21 @@ def test_grouped_reader_matches_oracle_and_per_row(sequences, rows_per_seq, topk
     _check(storage, q, indices, table, t2r, rows_per_seq, f"grouped {sequences}x{rows_per_seq} topk={topk}")
 
 
+@pytest.mark.parametrize("heads,rows_per_seq", [(16, 4), (32, 3), (2, 4)])
+def test_grouped_reader_head_counts_and_strided_output(heads, rows_per_seq):
+    # 8, 16 and 1 query heads per kv head; the output in a padded buffer (row stride not a multiple of 8)
+    storage, q, indices, table, t2r = _mtp_case(90 + heads, 5, rows_per_seq, 4096, 15000, 2048, heads=heads)
+    idx, bt, t2rd = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (indices, table, t2r))
+    kd, ks, vd, vs = regions(storage)
+    buf = torch.full((q.shape[0], heads, 260), float("nan"), dtype=torch.bfloat16, device="cuda")
+    out = buf[..., :256]
+    kernels.qsa_sparse_paged_attention_nvfp4(q, kd, ks, vd, vs, 1.0, 1.0, idx, bt, t2rd, out,
+                                             rows_per_group=rows_per_seq)
+    torch.cuda.synchronize()
+    assert torch.isnan(buf[..., 256:].float()).all()
+    assert_attention_close(out.contiguous(), oracle_attention(storage, q, idx, bt, t2rd), f"heads {heads}")
+
+
 def test_grouped_reader_ragged_last_group():
     # 10 rows in groups of 4: the last group has two rows
     storage, q, indices, table, t2r = _mtp_case(51, 5, 2, 4096, 12000, 2048)

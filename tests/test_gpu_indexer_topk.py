@@ -40,11 +40,38 @@ def test_topk_ties_nan_inf_and_lengths_match_the_contract():
     s[1, 100] = float("nan")
     s[1, 4000] = float("inf")
     s[2, :] = 0.0
+    s[2, 1::2] = -0.0  # equal to +0: ties in index order regardless of sign
     s[3, 50:60] = float("-inf")
     lengths = torch.tensor([5000, 4500, 3000, 2048, 10, 0], dtype=torch.int32, device="cuda")
     got = _select(s, 2048, lengths)
     want = oracle.topk_indices(s.cpu().numpy(), 2048, lengths.cpu().numpy())
     assert np.array_equal(got.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("rows,context,levels", [(8, 131072, 5), (1, 169984, 3), (3, 40000, 1)])
+def test_topk_heavy_ties_at_decode_sizes(rows, context, levels):
+    # few distinct values: the candidate lists overflow and the selection takes the re-scan path
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + levels)
+    s = torch.randint(0, levels, (rows, context), device="cuda", generator=g).float()
+    s[0, 12345] = 9.0
+    lengths = torch.full((rows,), context, dtype=torch.int32, device="cuda")
+    lengths[-1] = context - 777
+    got = _select(s, 2048, lengths)
+    want = oracle.topk_indices(s.cpu().numpy(), 2048, lengths.cpu().numpy())
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
+def test_topk_unaligned_rows_and_padded_output():
+    # rows that start off a 16-byte boundary (scalar loads) and an output buffer wider than its rows' k
+    g = torch.Generator(device="cuda").manual_seed(11)
+    base = torch.randn(5, 20011, device="cuda", generator=g)
+    s = base[:, 3:20003]  # row stride 20011: no row 16-byte aligned except by chance
+    buf = torch.full((5, 2100), -9, dtype=torch.int32, device="cuda")
+    indexer.qsa_select_topk(s, buf[:, :2048])
+    torch.cuda.synchronize()
+    want = torch.topk(s, 2048, dim=1).indices.sort(dim=1).values.to(torch.int32)
+    assert torch.equal(buf[:, :2048], want)
+    assert (buf[:, 2048:] == -9).all()
 
 
 def test_selection_drives_the_reader():

@@ -24,6 +24,8 @@ def test_oracle_tie_nan_and_length_rules():
     s = np.array([[2, 7, 7, 7, 1, 7], [np.nan, 0, np.inf, -np.inf, np.nan, 3]], np.float32)
     assert oracle.topk_indices(s, 3).tolist() == [[1, 2, 3], [0, 2, 4]]
     assert oracle.topk_indices(s, 4, lengths=[3, 0]).tolist() == [[0, 1, 2, -1], [-1, -1, -1, -1]]
+    z = np.array([[0.0, -0.0, 0.0, -0.0, -1.0]], np.float32)  # -0 equals +0: index order decides
+    assert oracle.topk_indices(z, 3).tolist() == [[0, 1, 2]]
 
 
 def test_wrapper_rejects_bad_buffers():
