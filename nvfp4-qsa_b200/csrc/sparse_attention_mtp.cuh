@@ -7,22 +7,22 @@
 //
 // One CTA of 8 warps = (group of up to 4 consecutive rows, kv head, split),
 // one CTA per SM.  Each selected record is gathered ONCE (tile::gather4) into a
-// CTA-wide ring of 16 tiles of 16 records that runs up to 7 steps ahead, and
-// a step of 32 tokens (two tiles) goes through the warps in one CTA barrier:
+// CTA-wide ring of 16 tiles of 16 records that runs up to 6 steps ahead.  A
+// step is 32 tokens (two tiles); in iteration i, between two CTA barriers:
 //   * warps 0-3 (S warps): warp w computes the scores of row w of the group
-//     (its query heads in one m16 tile) over the step's dequantised K tile,
+//     (its query heads in one m16 tile) over step i's dequantised K tile,
 //     runs that row's online softmax and writes P into a shared tile of the
 //     group's packed heads (up to 48 = 3 m16 tiles);
-//   * warps 4-7 (K warps), meanwhile: dequantise the NEXT step's K into the
-//     other half of a double-buffered f16 tile (exact: e2m1 x e4m3; warp
-//     4 + j owns dims [64j, 64j + 64)); warp 4 also refills the ring;
-//   * barrier; then every warp w accumulates O += P V over dims
-//     [32w, 32w + 32) of every packed head (12 m16n8 fragments), V
-//     dequantised in registers from the ring.
-// The P and K tiles are double-buffered, so the step's only barrier orders
-// everything: S of step i+1 and K of step i+2 may start while other warps are
-// still in P V of step i.  The gather and the dequantisation are paid once per
-// record for all rows of the group instead of once per row.
+//   * warps 4-7 (K warps), at the same time: warp 4 + j dequantises dims
+//     [64j, 64j + 64) of step i+1's K into the other half of a double-buffered
+//     f16 tile (exact: e2m1 x e4m3), then accumulates O += P V of step i-1
+//     over the same dims of every packed head (24 m16n8 fragments, 96 fp32
+//     registers), V dequantised in registers from the ring; warp 4 also
+//     refills the ring.
+// K, P and the rescale factors are double-buffered, so one barrier per step
+// orders everything and the scores of a step overlap the P V of the one before.
+// The gather and the dequantisation are paid once per record for all rows of
+// the group instead of once per row.
 //
 // Sharing is verified on the device, never assumed: each CTA compares the
 // rows' request and the index positions of its chunks against the group's
@@ -42,13 +42,15 @@ constexpr int kMtpRing = 16;          // ring stages (tiles of 16 records): 8 st
 constexpr int kMtpStep = 2 * kTile;   // tokens per step: two tiles per CTA barrier
 constexpr int kMtpHeads = 48;         // packed query heads of a group (rows x group size)
 constexpr int kMtpMTiles = 3;         // m16 tiles of packed heads
-constexpr int kMtpNT = 4;             // n8 tiles of P V per warp (32 dims)
-constexpr int kMtpFrags = kMtpMTiles * kMtpNT;  // O fragments per warp
 constexpr int kKhStride = 264;        // halfs per token row of the dequantised K tile (256 + 8: ldmatrix conflict-free)
 constexpr int kPhStride = 40;         // halfs per head row of the P tile (32 + 8: ldmatrix conflict-free)
 constexpr int kMtpRows = 4;           // rows per group (one S warp each)
 constexpr int kMtpMaxCluster = 8;     // splits of a group: one portable cluster
 constexpr int kMtpCompactIters = kMaxRange / kMtpThreads;
+#ifndef NVQSA_MTP_SUNROLL
+#define NVQSA_MTP_SUNROLL 16
+#endif
+constexpr int kMtpSUnroll = NVQSA_MTP_SUNROLL;
 
 struct __align__(128) SmemMtp {
   uint8_t rec[kMtpRing][kStageBytes];     // gather ring; after the last tile it holds the published O
@@ -67,7 +69,7 @@ struct __align__(128) SmemMtp {
   int abort;
   int shared_ok;
 };
-static_assert(sizeof(float4) * kMtpWarps * kMtpFrags * 32 <= sizeof(SmemMtp::rec), "published O must fit the ring");
+static_assert(sizeof(float4) * kMtpRows * kMtpMTiles * 8 * 32 <= sizeof(SmemMtp::rec), "published O must fit the ring");
 static_assert(sizeof(float) * kMtpMaxCluster * kMtpHeads <= sizeof(SmemMtp::ph), "merge weights must fit the P tile");
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
@@ -197,6 +199,29 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
     return mbar_wait(smem_u32(&sm.full_bar[g % kMtpRing]), (uint32_t)((g / kMtpRing) & 1));
   };
 
+  // Q of row `qrow0 + warp` for an S warp: lane L holds dims [8L, 8L + 8) of each head (zero past the active
+  // rows and heads).  Pass 0's are loaded first, so their latency overlaps the selection loads.
+  uint32_t qw[16][4];
+  auto load_q = [&](int64_t qrow0, int act) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
+      if (warp < act && j < G) {
+        const __nv_bfloat16* qrow =
+            p.q + (qrow0 + warp) * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
+        if (p.vec_q) {
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
+          qw[j][0] = v.x; qw[j][1] = v.y; qw[j][2] = v.z; qw[j][3] = v.w;
+        } else {
+          const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) qw[j][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
+        }
+      }
+    }
+  };
+  if (warp < kMtpRows) load_q(row_lo, nrows);
+
   // pass 0 always follows the group's first row: its copies start before the sharing check
   load_selections(row_lo);
   int n = compact();
@@ -205,36 +230,41 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
     for (int k = 0; k < kMtpRing && k < nt; ++k) issue_tile(k, n);
   }
 
-  // ---------------- do the group's rows share request and selections (this CTA's chunks)? ----------------
-  bool same = true;
+  // ---------- do the group's rows share request and selections? (this CTA's chunks; verdict deferred) ----------
+  // Pass 0 runs speculatively as if they did: the ring follows the first row's selections, whose S warp 0
+  // result is right either way, and S warps 1-3 score their rows against the same records.  The loads below
+  // are compared once the pass's first copies are on their way; the CTA's verdict is taken at the end of the
+  // pass and the cluster's at its merge barrier.  A group that does not share keeps only row 0's output of
+  // pass 0 and processes its other rows one per pass.
+  int32_t shv[kMtpCompactIters][kMtpRows];
+  int32_t shr[kMtpRows];
   {
-    const int32_t req0 = __ldg(p.token_to_request + row_lo);
-    for (int i = 1; i < nrows; ++i) same &= __ldg(p.token_to_request + row_lo + i) == req0;
     const int32_t* idx0 = p.indices + row_lo * p.topk;
+#pragma unroll
+    for (int i = 0; i < kMtpRows; ++i) shr[i] = i < nrows ? __ldg(p.token_to_request + row_lo + i) : 0;
 #pragma unroll
     for (int it = 0; it < kMtpCompactIters; ++it) {
       const int lc = it * kMtpWarps + warp;
       const int64_t pos = ((int64_t)split + (int64_t)lc * p.splits) * kChunk + lane;
-      if (lc < my_chunks && pos < p.topk) {
-        const int32_t v0 = __ldg(idx0 + pos);
-        int32_t vi[kMtpRows - 1];
+      const bool in = lc < my_chunks && pos < p.topk;
 #pragma unroll
-        for (int i = 1; i < kMtpRows; ++i) vi[i - 1] = i < nrows ? __ldg(idx0 + (int64_t)i * p.topk + pos) : v0;
-#pragma unroll
-        for (int i = 1; i < kMtpRows; ++i) same &= vi[i - 1] == v0;
-      }
+      for (int i = 0; i < kMtpRows; ++i) shv[it][i] = (in && i < nrows) ? __ldg(idx0 + (int64_t)i * p.topk + pos) : 0;
     }
   }
-  same = __syncthreads_and(same) != 0;
-  if (p.cluster > 1) {
-    // every rank of the cluster takes the same passes
-    if (tid == 0) sm.shared_ok = same ? 1 : 0;
-    cluster_sync();
-    const int mine = tid < p.cluster ? cluster_ld_s32(cluster_map(smem_u32(&sm.shared_ok), (uint32_t)tid)) : 1;
-    same = __syncthreads_and(mine) != 0;
-    cluster_sync();  // no rank rewrites shared_ok before every rank has read it
-  }
-  const int passes = same ? 1 : nrows;
+  auto shares = [&]() -> bool {
+    bool ok = true;
+#pragma unroll
+    for (int i = 1; i < kMtpRows; ++i) {
+      if (i >= nrows) break;
+      ok &= shr[i] == shr[0];
+#pragma unroll
+      for (int it = 0; it < kMtpCompactIters; ++it) ok &= shv[it][i] == shv[it][0];
+    }
+    return ok;
+  };
+  bool same_local = true;  // this thread's share of the check (set during pass 0's prologue)
+  bool same = true;        // the cluster's verdict (known at the end of pass 0)
+  int passes = nrows;      // 1 once pass 0 finds that the group shares
   bool aborted = false;
 
   // ldmatrix row addresses: K (tokens x dims) for B of S, P (heads x tokens) for A of P V
@@ -269,8 +299,8 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
 
   // Every rank of a cluster takes every pass (their cluster barriers must pair up), aborted or not.
   for (int pass = 0; pass < passes; ++pass) {
-    const int64_t prow = same ? row_lo : row_lo + pass;  // row whose selections the gather follows
-    const int act = same ? nrows : 1;                    // active S warps (rows) of this pass
+    const int64_t prow = row_lo + pass;     // row whose selections the gather follows
+    const int act = pass == 0 ? nrows : 1;  // active S warps (rows) of this pass (pass 0: speculatively all)
     const bool live = !aborted;                          // this pass issues copies
     if (pass > 0 && live) {  // a group that does not share: row prow alone, on S warp 0
       load_selections(prow);
@@ -286,23 +316,10 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
     // ---------------- S warps: Q of their row; K warps: K of step 0 ----------------
     bool ok = true;
     if (!kwarp) {
-      // lane L holds dims [8L, 8L + 8) of each head of row `warp`
-      uint32_t qw[16][4];
+      if (pass > 0) load_q(prow, act);
+      if (warp >= act) {  // pass 0 loaded every row of the group; a row-by-row pass keeps only its own
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
-        if (warp < act && j < G) {
-          const __nv_bfloat16* qrow =
-              p.q + (prow + warp) * p.q_stride_row + (int64_t)(kvh * G + j) * p.q_stride_head + lane * 8;
-          if (p.vec_q) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(qrow));
-            qw[j][0] = v.x; qw[j][1] = v.y; qw[j][2] = v.z; qw[j][3] = v.w;
-          } else {
-            const unsigned short* qs = reinterpret_cast<const unsigned short*>(qrow);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) qw[j][t] = (uint32_t)__ldg(qs + 2 * t) | ((uint32_t)__ldg(qs + 2 * t + 1) << 16);
-          }
-        }
+        for (int j = 0; j < 16; ++j) qw[j][0] = qw[j][1] = qw[j][2] = qw[j][3] = 0u;
       }
       // per-head power-of-two pre-scale (exact) into f16 A-fragments of the row's m16 tile (natural dim
       // order: k-step s covers dims [16s, 16s + 16)); heads >= G stay zero
@@ -327,6 +344,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
           f[((j & 7) * 4 + cc) * 4 + 2 * hi + (j >> 3)] = pack_half2(bf16_lo(x) * mul, bf16_hi(x) * mul);
         }
       }
+      if (pass == 0) same_local = shares();
       // P rows of inactive heads stay zero for the whole pass
       for (int i = tid; i < 2 * kMtpHeads * kPhStride / 2; i += 32 * kMtpRows)
         reinterpret_cast<uint32_t*>(&sm.ph[0][0][0])[i] = 0u;
@@ -338,33 +356,33 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
         if (ok) dequant_k(1, 0, 1);
       }
     }
+    if (kwarp && pass == 0) same_local = shares();
     if (!__syncthreads_and(ok)) {
       aborted = true;
       if (tid == 0) sm.abort = 1;
     }
     if (tid == 0 && pass == 0) stamp_max(p, unit, 2);
 
-    float oacc[kMtpMTiles][kMtpNT][4];
+    // O accumulators (K warps): dims [64j, 64j + 64) of every packed head, j = warp - 4
+    float oacc[kMtpMTiles][8][4];
 #pragma unroll
     for (int t = 0; t < kMtpMTiles; ++t)
 #pragma unroll
-      for (int j = 0; j < kMtpNT; ++j) oacc[t][j][0] = oacc[t][j][1] = oacc[t][j][2] = oacc[t][j][3] = 0.0f;
+      for (int j = 0; j < 8; ++j) oacc[t][j][0] = oacc[t][j][1] = oacc[t][j][2] = oacc[t][j][3] = 0.0f;
     const bool srow = !kwarp && warp < act;  // this warp runs a row's scores and softmax
     const float smul_r = (srow && r < G) ? sm.smul[warp * G + r] : 1.0f;
     const float smul_r8 = (srow && r + 8 < G) ? sm.smul[warp * G + r + 8] : 1.0f;
     float m_r = kMaskedScore, m_r8 = kMaskedScore;
     float l_r = 0.0f, l_r8 = 0.0f;
 
-    // Step i: S warps score tiles 2i, 2i+1 from kh[i & 1]; K warps dequantise tiles 2i+2, 2i+3 into
-    // kh[(i + 1) & 1] (warp 4 first refills the stages of step i-2, which every warp left before the
-    // previous barrier); barrier; every warp P V over tiles 2i, 2i+1.
+    // Iteration i: S warps score step i (tiles 2i, 2i+1) from kh[i & 1] and write P into ph[i & 1]; K warps
+    // dequantise step i+1 into kh[(i + 1) & 1] (warp 4 first refills the stages of step i-2, whose last read
+    // was P V of step i-2 in the previous iteration) and accumulate P V of step i-1; one CTA barrier.
     int i = 0;
-    for (; i < nsteps && !aborted; ++i) {
-      const int k0 = 2 * i;
-      const bool two = k0 + 1 < ntiles;
-      const int buf = i & 1;
+    for (; i <= nsteps && !aborted; ++i) {
       bool okk = true;
       if (kwarp) {
+        const int k0 = 2 * i;
         if (warp == 4 && i >= 2) {
           if (k0 + kMtpRing - 4 < ntiles) issue_tile(k0 + kMtpRing - 4, n);
           if (k0 + kMtpRing - 3 < ntiles) issue_tile(k0 + kMtpRing - 3, n);
@@ -374,142 +392,57 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
           const int kk = k0 + 2 + u;
           if (kk < ntiles) {
             okk &= tile_wait(kk);
-            if (okk) dequant_k(kk, buf ^ 1, u);
+            if (okk) dequant_k(kk, (i + 1) & 1, u);
           }
         }
-      } else if (srow) {
-        // ---- S = Q K^T for row `warp` over the step's 32 tokens, online softmax, P into the packed tile ----
-        // (a missing second tile leaves stale K rows: their scores are masked below)
-        float sacc[4][4];
+        if (i >= 1 && okk) {
+          // ---- O += P V of step i-1 over dims [64j, 64j + 64) of every packed head, one k-step per tile ----
+          const int kw = warp - kMtpRows;
+          const int pb = (i - 1) & 1;
+          const int kp = 2 * (i - 1);
+          const bool two = kp + 1 < ntiles;
+          const int any = sm.resc[pb][0] | sm.resc[pb][1] | sm.resc[pb][2] | sm.resc[pb][3];
+          if (any) {
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-        const uint32_t kaddr = smem_u32(&sm.kh[buf][0][0]) + kh_lane;
+            for (int t = 0; t < kMtpMTiles; ++t) {
 #pragma unroll
-        for (int s = 0; s < 16; ++s) {
-          uint32_t b0, b1, b2, b3, b4, b5, b6, b7;
-          ldsm_x4(kaddr + 32u * s, b0, b1, b2, b3);
-          ldsm_x4(kaddr + (uint32_t)(kTile * kKhStride * 2) + 32u * s, b4, b5, b6, b7);
-          const uint4 qa = sm.qf[warp][s][lane];
-          mma_f16(sacc[0], qa.x, qa.y, qa.z, qa.w, b0, b1);
-          mma_f16(sacc[1], qa.x, qa.y, qa.z, qa.w, b2, b3);
-          mma_f16(sacc[2], qa.x, qa.y, qa.z, qa.w, b4, b5);
-          mma_f16(sacc[3], qa.x, qa.y, qa.z, qa.w, b6, b7);
-        }
-        const int tok_base = i * kMtpStep;
-        const bool tail = tok_base + kMtpStep > n;
-        if (tail) {
+              for (int hh = 0; hh < 2; ++hh) {
+                const int head = 16 * t + r + 8 * hh;
+                const int hrow = head / G;
+                const float a = (head < act * G && sm.resc[pb][hrow]) ? sm.alpha[pb][head] : 1.0f;
 #pragma unroll
-          for (int nt = 0; nt < 4; ++nt) {
-            const int t0 = tok_base + 8 * nt + 2 * c;
-            if (t0 >= n) { sacc[nt][0] = -1.0e30f; sacc[nt][2] = -1.0e30f; }
-            if (t0 + 1 >= n) { sacc[nt][1] = -1.0e30f; sacc[nt][3] = -1.0e30f; }
-          }
-        }
-        float mx_r = fmaxf(fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1])),
-                           fmaxf(fmaxf(sacc[2][0], sacc[2][1]), fmaxf(sacc[3][0], sacc[3][1])));
-        float mx_r8 = fmaxf(fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3])),
-                            fmaxf(fmaxf(sacc[2][2], sacc[2][3]), fmaxf(sacc[3][2], sacc[3][3])));
-        mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 1));
-        mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 2));
-        mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 1));
-        mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 2));
-        mx_r *= smul_r;
-        mx_r8 *= smul_r8;
-        const bool up_r = mx_r > m_r + kRescaleThreshold;
-        const bool up_r8 = mx_r8 > m_r8 + kRescaleThreshold;
-        const bool up = __any_sync(0xffffffffu, up_r || up_r8);
-        if (up) {
-          const float mn_r = up_r ? mx_r : m_r, mn_r8 = up_r8 ? mx_r8 : m_r8;
-          const float a_r = ex2(m_r - mn_r), a_r8 = ex2(m_r8 - mn_r8);
-          m_r = mn_r;
-          m_r8 = mn_r8;
-          l_r *= a_r;
-          l_r8 *= a_r8;
-          if (c == 0) {
-            if (r < G) sm.alpha[buf][warp * G + r] = a_r;
-            if (r + 8 < G) sm.alpha[buf][warp * G + r + 8] = a_r8;
-          }
-        }
-        if (lane == 0) sm.resc[buf][warp] = up ? 1 : 0;
-        float pv[4][4];
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          pv[nt][0] = ex2(fmaf(sacc[nt][0], smul_r, -m_r));
-          pv[nt][1] = ex2(fmaf(sacc[nt][1], smul_r, -m_r));
-          pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
-          pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
-        }
-        if (tail) {  // masked scores must not count even while the running max is still -1e20
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt) {
-            const int t0 = tok_base + 8 * nt + 2 * c;
-            if (t0 >= n) { pv[nt][0] = 0.0f; pv[nt][2] = 0.0f; }
-            if (t0 + 1 >= n) { pv[nt][1] = 0.0f; pv[nt][3] = 0.0f; }
-          }
-        }
-        l_r += ((pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1])) + ((pv[2][0] + pv[2][1]) + (pv[3][0] + pv[3][1]));
-        l_r8 += ((pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3])) + ((pv[2][2] + pv[2][3]) + (pv[3][2] + pv[3][3]));
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          if (r < G)
-            *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r][8 * nt + 2 * c]) = pack_half2(pv[nt][0], pv[nt][1]);
-          if (r + 8 < G)
-            *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r + 8][8 * nt + 2 * c]) =
-                pack_half2(pv[nt][2], pv[nt][3]);
-        }
-      } else if (lane == 0) {
-        sm.resc[buf][warp] = 0;
-      }
-      if (!__syncthreads_and(okk)) {  // P of step i and K of step i+1 in place; every warp past P V of step i-1
-        if (tid == 0) sm.abort = 1;
-        aborted = true;
-        break;
-      }
-
-      // ---- O += P V over dims [32w, 32w + 32) of every packed head, one k-step per tile ----
-      {
-        const int any = sm.resc[buf][0] | sm.resc[buf][1] | sm.resc[buf][2] | sm.resc[buf][3];
-        if (any) {
-#pragma unroll
-          for (int t = 0; t < kMtpMTiles; ++t) {
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-              const int head = 16 * t + r + 8 * hh;
-              const int hrow = head / G;
-              const float a = (head < act * G && sm.resc[buf][hrow]) ? sm.alpha[buf][head] : 1.0f;
-#pragma unroll
-              for (int j = 0; j < kMtpNT; ++j) {
-                oacc[t][j][2 * hh] *= a;
-                oacc[t][j][2 * hh + 1] *= a;
+                for (int j = 0; j < 8; ++j) {
+                  oacc[t][j][2 * hh] *= a;
+                  oacc[t][j][2 * hh + 1] *= a;
+                }
               }
             }
           }
-        }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          if (u == 1 && !two) break;  // no stale V enters O
-          const uint8_t* stage = sm.rec[(tiles_done + k0 + u) % kMtpRing];
-          uint32_t pa[kMtpMTiles][4];
-          const uint32_t paddr = smem_u32(&sm.ph[buf][0][0]) + ph_lane + (uint32_t)(kTile * 2 * u);
+          for (int u = 0; u < 2; ++u) {
+            if (u == 1 && !two) break;  // no stale V enters O
+            const uint8_t* stage = sm.rec[(tiles_done + kp + u) % kMtpRing];
+            uint32_t pa[kMtpMTiles][4];
+            const uint32_t paddr = smem_u32(&sm.ph[pb][0][0]) + ph_lane + (uint32_t)(kTile * 2 * u);
 #pragma unroll
-          for (int t = 0; t < kMtpMTiles; ++t)
-            ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
-          // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9} of the tile, dims 32w + 4r + [0, 4) (two bytes of V codes)
-          uint32_t vw[4], vsb[4];
+            for (int t = 0; t < kMtpMTiles; ++t)
+              ldsm_x4(paddr + (uint32_t)(16 * kPhStride * 2 * t), pa[t][0], pa[t][1], pa[t][2], pa[t][3]);
+            // lane (r, c): tokens {2c, 2c+1, 2c+8, 2c+9} of the tile, dims 64j + 8r + [0, 8)
+            uint32_t vw[4], vsb[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint8_t* rec = stage + slot_off(vtok[q]);
-            vw[q] = *reinterpret_cast<const uint16_t*>(rec + 144 + 16 * warp + 2 * r);
-            vsb[q] = rec[272 + 2 * warp + (r >> 2)];
-          }
-          const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
-          const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
-          // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
-          const uint32_t x01 = (vw[0] & 0x0f0fu) | ((vw[1] & 0x0f0fu) << 4);
-          const uint32_t y01 = ((vw[0] >> 4) & 0x0f0fu) | (vw[1] & 0xf0f0u);
-          const uint32_t x23 = (vw[2] & 0x0f0fu) | ((vw[3] & 0x0f0fu) << 4);
-          const uint32_t y23 = ((vw[2] >> 4) & 0x0f0fu) | (vw[3] & 0xf0f0u);
-          // n-tile 2B + x, column n <-> dim 32w + 4n + 2B + x
+            for (int q = 0; q < 4; ++q) {
+              const uint8_t* rec = stage + slot_off(vtok[q]);
+              vw[q] = *reinterpret_cast<const uint32_t*>(rec + 144 + 32 * kw + 4 * r);
+              vsb[q] = rec[272 + 4 * kw + (r >> 1)];
+            }
+            const uint32_t s01 = cvt_e4m3x2_f16x2(vsb[0] | (vsb[1] << 8));
+            const uint32_t s23 = cvt_e4m3x2_f16x2(vsb[2] | (vsb[3] << 8));
+            // low nibbles (even dims) of two tokens interleaved into one byte; high nibbles (odd dims) likewise
+            const uint32_t x01 = (vw[0] & 0x0f0f0f0fu) | ((vw[1] & 0x0f0f0f0fu) << 4);
+            const uint32_t y01 = ((vw[0] >> 4) & 0x0f0f0f0fu) | (vw[1] & 0xf0f0f0f0u);
+            const uint32_t x23 = (vw[2] & 0x0f0f0f0fu) | ((vw[3] & 0x0f0f0f0fu) << 4);
+            const uint32_t y23 = ((vw[2] >> 4) & 0x0f0f0f0fu) | (vw[3] & 0xf0f0f0f0u);
+            // n-tile 2B + x, column n <-> dim 64j + 8n + 2B + x
 #define NVQSA_MTP_PV_BYTE(B)                                                                     \
   {                                                                                              \
     const uint32_t bx0 = hmul2_u32(cvt_e2m1x2_f16x2_byte<B>(x01), s01);                         \
@@ -521,10 +454,103 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
       mma_f16(oacc[t][2 * (B) + 1], pa[t][0], pa[t][1], pa[t][2], pa[t][3], by0, by1);           \
     }                                                                                            \
   }
-          NVQSA_MTP_PV_BYTE(0)
-          NVQSA_MTP_PV_BYTE(1)
+            NVQSA_MTP_PV_BYTE(0)
+            NVQSA_MTP_PV_BYTE(1)
+            NVQSA_MTP_PV_BYTE(2)
+            NVQSA_MTP_PV_BYTE(3)
 #undef NVQSA_MTP_PV_BYTE
+          }
         }
+      } else if (i < nsteps) {
+        const int buf = i & 1;
+        if (srow) {
+          // ---- S = Q K^T for row `warp` over the step's 32 tokens, online softmax, P into the packed tile ----
+          // (a missing second tile leaves stale K rows: their scores are masked below)
+          float sacc[4][4];
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
+          const uint32_t kaddr = smem_u32(&sm.kh[buf][0][0]) + kh_lane;
+#pragma unroll kMtpSUnroll
+          for (int s = 0; s < 16; ++s) {
+            uint32_t b0, b1, b2, b3, b4, b5, b6, b7;
+            ldsm_x4(kaddr + 32u * s, b0, b1, b2, b3);
+            ldsm_x4(kaddr + (uint32_t)(kTile * kKhStride * 2) + 32u * s, b4, b5, b6, b7);
+            const uint4 qa = sm.qf[warp][s][lane];
+            mma_f16(sacc[0], qa.x, qa.y, qa.z, qa.w, b0, b1);
+            mma_f16(sacc[1], qa.x, qa.y, qa.z, qa.w, b2, b3);
+            mma_f16(sacc[2], qa.x, qa.y, qa.z, qa.w, b4, b5);
+            mma_f16(sacc[3], qa.x, qa.y, qa.z, qa.w, b6, b7);
+          }
+          const int tok_base = i * kMtpStep;
+          const bool tail = tok_base + kMtpStep > n;
+          if (tail) {
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+              const int t0 = tok_base + 8 * nt + 2 * c;
+              if (t0 >= n) { sacc[nt][0] = -1.0e30f; sacc[nt][2] = -1.0e30f; }
+              if (t0 + 1 >= n) { sacc[nt][1] = -1.0e30f; sacc[nt][3] = -1.0e30f; }
+            }
+          }
+          float mx_r = fmaxf(fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1])),
+                             fmaxf(fmaxf(sacc[2][0], sacc[2][1]), fmaxf(sacc[3][0], sacc[3][1])));
+          float mx_r8 = fmaxf(fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3])),
+                              fmaxf(fmaxf(sacc[2][2], sacc[2][3]), fmaxf(sacc[3][2], sacc[3][3])));
+          mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 1));
+          mx_r = fmaxf(mx_r, __shfl_xor_sync(0xffffffffu, mx_r, 2));
+          mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 1));
+          mx_r8 = fmaxf(mx_r8, __shfl_xor_sync(0xffffffffu, mx_r8, 2));
+          mx_r *= smul_r;
+          mx_r8 *= smul_r8;
+          const bool up_r = mx_r > m_r + kRescaleThreshold;
+          const bool up_r8 = mx_r8 > m_r8 + kRescaleThreshold;
+          const bool up = __any_sync(0xffffffffu, up_r || up_r8);
+          if (up) {
+            const float mn_r = up_r ? mx_r : m_r, mn_r8 = up_r8 ? mx_r8 : m_r8;
+            const float a_r = ex2(m_r - mn_r), a_r8 = ex2(m_r8 - mn_r8);
+            m_r = mn_r;
+            m_r8 = mn_r8;
+            l_r *= a_r;
+            l_r8 *= a_r8;
+            if (c == 0) {
+              if (r < G) sm.alpha[buf][warp * G + r] = a_r;
+              if (r + 8 < G) sm.alpha[buf][warp * G + r + 8] = a_r8;
+            }
+          }
+          if (lane == 0) sm.resc[buf][warp] = up ? 1 : 0;
+          float pv[4][4];
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            pv[nt][0] = ex2(fmaf(sacc[nt][0], smul_r, -m_r));
+            pv[nt][1] = ex2(fmaf(sacc[nt][1], smul_r, -m_r));
+            pv[nt][2] = ex2(fmaf(sacc[nt][2], smul_r8, -m_r8));
+            pv[nt][3] = ex2(fmaf(sacc[nt][3], smul_r8, -m_r8));
+          }
+          if (tail) {  // masked scores must not count even while the running max is still -1e20
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+              const int t0 = tok_base + 8 * nt + 2 * c;
+              if (t0 >= n) { pv[nt][0] = 0.0f; pv[nt][2] = 0.0f; }
+              if (t0 + 1 >= n) { pv[nt][1] = 0.0f; pv[nt][3] = 0.0f; }
+            }
+          }
+          l_r += ((pv[0][0] + pv[0][1]) + (pv[1][0] + pv[1][1])) + ((pv[2][0] + pv[2][1]) + (pv[3][0] + pv[3][1]));
+          l_r8 += ((pv[0][2] + pv[0][3]) + (pv[1][2] + pv[1][3])) + ((pv[2][2] + pv[2][3]) + (pv[3][2] + pv[3][3]));
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            if (r < G)
+              *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r][8 * nt + 2 * c]) = pack_half2(pv[nt][0], pv[nt][1]);
+            if (r + 8 < G)
+              *reinterpret_cast<uint32_t*>(&sm.ph[buf][warp * G + r + 8][8 * nt + 2 * c]) =
+                  pack_half2(pv[nt][2], pv[nt][3]);
+          }
+        } else if (lane == 0) {
+          sm.resc[buf][warp] = 0;
+        }
+      }
+      if (!__syncthreads_and(okk)) {  // step i's P and step i+1's K in place; P V of step i-1 done
+        if (tid == 0) sm.abort = 1;
+        aborted = true;
+        break;
       }
     }
     if (aborted && live && warp == 4) {
@@ -546,43 +572,68 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
       if (r < G) { sm.m_s[warp * G + r] = m_r; sm.l_s[warp * G + r] = l_r; }
       if (r + 8 < G) { sm.m_s[warp * G + r + 8] = m_r8; sm.l_s[warp * G + r + 8] = l_r8; }
     }
-    __syncthreads();  // (m, l) visible; no copy in flight, the ring is free
+    // (m, l) visible; no copy in flight, the ring is free; pass 0: this CTA's sharing verdict
+    const bool cta_same = __syncthreads_and(pass == 0 ? same_local : true) != 0;
     aborted = sm.abort != 0;
-    if (tid == 0 && pass == passes - 1) stamp_max(p, unit, 1);
+    if (pass == 0 && p.cluster <= 1) {
+      same = cta_same;
+      passes = same ? 1 : nrows;
+    }
 
-    // bf16 output of packed head `head` (< act * G)
+    // rows whose output this pass stores (read after the cluster's verdict)
+    auto act_out = [&]() { return pass == 0 && !same ? 1 : act; };
+    if (tid == 0) stamp_max(p, unit, 1);
+    // bf16 output of packed head `head` (< act_out * G)
     auto out_ptr = [&](int head) {
       const int hrow = head / G, j = head - hrow * G;
       return p.out + (prow + hrow) * p.o_stride_row + (int64_t)(kvh * G + j) * p.o_stride_head;
     };
+    const int kw = warp - kMtpRows;  // K warp index: its O covers dims [64 kw, 64 kw + 64)
     if (p.cluster > 1) {
-      // Every rank publishes its (O, m, l); then every rank merges one slice of the O fragments of all ranks
-      // (fragment f = 4t + n-tile of each warp, slice [12 rank / cluster, 12 (rank + 1) / cluster)) over
-      // distributed shared memory and stores it, with per-head weights 2^(m_rank - M) / sum computed once.
-      float4* pub = reinterpret_cast<float4*>(&sm.rec[0][0]);  // [warp][12][32]
-      if (!aborted) {
+      // Every rank publishes its (O, m, l); then every K warp of every rank merges one slice of its O fragments
+      // over all ranks (fragment f = 8t + n-tile, slice [24 rank / C, 24 (rank + 1) / C)) through distributed
+      // shared memory and stores it, with per-head weights 2^(m_rank - M) / sum.  The sharing verdicts, the
+      // abort flags and the per-head (m, l) of every rank are loaded in one round before the CTA barriers that
+      // agree on the verdict and publish the weights; then the fragments, two at a time from every rank.
+      float4* pub = reinterpret_cast<float4*>(&sm.rec[0][0]);  // [K warp][24][32]
+      if (!aborted && kwarp) {
 #pragma unroll
         for (int t = 0; t < kMtpMTiles; ++t)
 #pragma unroll
-          for (int j = 0; j < kMtpNT; ++j)
-            pub[(warp * kMtpFrags + t * kMtpNT + j) * 32 + lane] =
-                make_float4(oacc[t][j][0], oacc[t][j][1], oacc[t][j][2], oacc[t][j][3]);
+          for (int j = 0; j < 8; ++j)
+            pub[(kw * 24 + t * 8 + j) * 32 + lane] = make_float4(oacc[t][j][0], oacc[t][j][1], oacc[t][j][2], oacc[t][j][3]);
       }
+      if (tid == 0) sm.shared_ok = cta_same ? 1 : 0;
       cluster_sync();
-      const int rank = split % p.cluster;
-      float* wts = reinterpret_cast<float*>(&sm.ph[0][0][0]);  // [cluster][48] merge weights (P space is free)
-      const int bad_rank = tid < p.cluster ? cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)tid)) : 0;
-      if (tid < kMtpHeads && tid < act * G) {
-        float mr[kMtpMaxCluster], lr[kMtpMaxCluster], M = kMaskedScore;
+      const int C = p.cluster;
+      const int rank = split % C;
+      const int f_lo = rank * 24 / C, f_hi = (rank + 1) * 24 / C;
+      float4 v[2][kMtpMaxCluster];
+#define NVQSA_MTP_LOAD_PAIR(F0)                                                                              \
+  _Pragma("unroll") for (int q = 0; q < 2; ++q) {                                                          \
+    const uint32_t off = (uint32_t)((kw * 24 + min((F0) + q, f_hi - 1)) * 32 + lane) * 16u;                \
+    _Pragma("unroll") for (int rk = 0; rk < kMtpMaxCluster; ++rk) v[q][rk] =                               \
+        rk < C ? cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off) : make_float4(0.f, 0.f, 0.f, 0.f); \
+  }
+      const int mine = tid < C ? cluster_ld_s32(cluster_map(smem_u32(&sm.shared_ok), (uint32_t)tid)) : 1;
+      const int bad_rank = tid < C ? cluster_ld_s32(cluster_map(smem_u32(&sm.abort), (uint32_t)tid)) : 0;
+      float mr[kMtpMaxCluster], lr[kMtpMaxCluster];
 #pragma unroll
-        for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
-          mr[rk] = kMaskedScore;
-          lr[rk] = 0.0f;
-          if (rk < p.cluster) {
-            mr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.m_s[tid]), (uint32_t)rk)));
-            lr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.l_s[tid]), (uint32_t)rk)));
-          }
+      for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
+        mr[rk] = kMaskedScore;
+        lr[rk] = 0.0f;
+        if (tid < kMtpHeads && rk < C) {
+          mr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.m_s[tid]), (uint32_t)rk)));
+          lr[rk] = __int_as_float(cluster_ld_s32(cluster_map(smem_u32(&sm.l_s[tid]), (uint32_t)rk)));
         }
+      }
+      if (pass == 0) {  // the cluster's sharing verdict: every rank takes the same passes
+        same = __syncthreads_and(mine) != 0;
+        passes = same ? 1 : nrows;
+      }
+      float* wts = reinterpret_cast<float*>(&sm.ph[0][0][0]);  // [cluster][48] merge weights (P space is free)
+      if (tid < kMtpHeads && tid < act_out() * G) {
+        float M = kMaskedScore;
 #pragma unroll
         for (int rk = 0; rk < kMtpMaxCluster; ++rk) M = fmaxf(M, mr[rk]);
         float L = 0.0f;
@@ -595,74 +646,74 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
         const float inv = L > 0.0f ? p.inv_value_scale / fmaxf(L, 1.0e-20f) : 0.0f;
 #pragma unroll
         for (int rk = 0; rk < kMtpMaxCluster; ++rk)
-          if (rk < p.cluster) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
+          if (rk < C) wts[rk * kMtpHeads + tid] = mr[rk] * inv;
       }
-      if (!__syncthreads_or(bad_rank)) {  // weights in place; no rank gave up
-        const int f_lo = rank * kMtpFrags / p.cluster, f_hi = (rank + 1) * kMtpFrags / p.cluster;
-        for (int f0 = f_lo; f0 < f_hi; f0 += 2) {  // two fragments' loads of every rank in flight at once
-          float4 v[2][kMtpMaxCluster];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint32_t off = (uint32_t)((warp * kMtpFrags + min(f0 + q, f_hi - 1)) * 32 + lane) * 16u;
-#pragma unroll
-            for (int rk = 0; rk < kMtpMaxCluster; ++rk)
-              v[q][rk] = rk < p.cluster ? cluster_ld_f4(cluster_map(smem_u32(pub), (uint32_t)rk) + off)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
+      if (!__syncthreads_or(bad_rank) && kwarp) {  // weights in place; no rank gave up
+        for (int f0 = f_lo; f0 < f_hi; f0 += 2) {
+          NVQSA_MTP_LOAD_PAIR(f0)
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
             const int f = f0 + q;
             if (f >= f_hi) break;
-            const int t = f / kMtpNT, jn = f - t * kMtpNT;
+            const int t = f >> 3, jn = f & 7;
             const int h0 = 16 * t + r, h1 = h0 + 8;
-            const bool l0 = h0 < act * G, l1 = h1 < act * G;
+            const bool l0 = h0 < act_out() * G, l1 = h1 < act_out() * G;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int rk = 0; rk < kMtpMaxCluster; ++rk) {
-              if (rk >= p.cluster) break;
+              if (rk >= C) break;
               const float w0 = l0 ? wts[rk * kMtpHeads + h0] : 0.0f, w1 = l1 ? wts[rk * kMtpHeads + h1] : 0.0f;
               acc.x += w0 * v[q][rk].x; acc.y += w0 * v[q][rk].y; acc.z += w1 * v[q][rk].z; acc.w += w1 * v[q][rk].w;
             }
-            // n-tile jn, columns 2c and 2c+1: dims 32w + 8c + jn and 32w + 8c + 4 + jn
-            const int d = 32 * warp + 8 * c + jn;
+            // n-tile jn, columns 2c and 2c+1: dims 64kw + 16c + jn and 64kw + 16c + 8 + jn
+            const int d = 64 * kw + 16 * c + jn;
             if (l0) {
               __nv_bfloat16* op = out_ptr(h0);
               op[d] = __float2bfloat16_rn(acc.x);
-              op[d + 4] = __float2bfloat16_rn(acc.y);
+              op[d + 8] = __float2bfloat16_rn(acc.y);
             }
             if (l1) {
               __nv_bfloat16* op = out_ptr(h1);
               op[d] = __float2bfloat16_rn(acc.z);
-              op[d + 4] = __float2bfloat16_rn(acc.w);
+              op[d + 8] = __float2bfloat16_rn(acc.w);
             }
           }
         }
       }
+#undef NVQSA_MTP_LOAD_PAIR
       cluster_sync();  // every rank keeps its shared memory until all have read it
-    } else if (!aborted) {
+    } else if (!aborted && kwarp) {
       // one CTA per group: normalise and store every fragment from registers
 #pragma unroll
       for (int t = 0; t < kMtpMTiles; ++t) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int head = 16 * t + r + 8 * hh;
-          if (head >= act * G) continue;
+          if (head >= act_out() * G) continue;
           const float l = sm.l_s[head];
           // kernels.py:333-337: acc / l when l > 0, else 0; then / value_global_scale
           const float inv = l > 0.0f ? p.inv_value_scale / fmaxf(l, 1.0e-20f) : 0.0f;
-          // dims 32w + 8c + j (column 2c of n-tile j) and 32w + 8c + 4 + j (column 2c + 1)
-          __nv_bfloat162 w2[4];
-          w2[0] = __floats2bfloat162_rn(oacc[t][0][2 * hh] * inv, oacc[t][1][2 * hh] * inv);
-          w2[1] = __floats2bfloat162_rn(oacc[t][2][2 * hh] * inv, oacc[t][3][2 * hh] * inv);
-          w2[2] = __floats2bfloat162_rn(oacc[t][0][2 * hh + 1] * inv, oacc[t][1][2 * hh + 1] * inv);
-          w2[3] = __floats2bfloat162_rn(oacc[t][2][2 * hh + 1] * inv, oacc[t][3][2 * hh + 1] * inv);
-          __nv_bfloat16* op = out_ptr(head) + 32 * warp + 8 * c;
-          if (p.vec_o) {
-            *reinterpret_cast<uint4*>(op) = *reinterpret_cast<const uint4*>(w2);
-          } else {
-            const unsigned short* ws = reinterpret_cast<const unsigned short*>(w2);
+          // dims 64kw + 16c + i (n = 2c, n-tile i) and 64kw + 16c + 8 + i (n = 2c + 1)
+          uint32_t wv[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) reinterpret_cast<unsigned short*>(op)[q] = ws[q];
+          for (int i2 = 0; i2 < 4; ++i2) {
+            __nv_bfloat162 lo2 = __floats2bfloat162_rn(oacc[t][2 * i2][2 * hh] * inv, oacc[t][2 * i2 + 1][2 * hh] * inv);
+            __nv_bfloat162 hi2 =
+                __floats2bfloat162_rn(oacc[t][2 * i2][2 * hh + 1] * inv, oacc[t][2 * i2 + 1][2 * hh + 1] * inv);
+            wv[i2] = *reinterpret_cast<uint32_t*>(&lo2);
+            wv[4 + i2] = *reinterpret_cast<uint32_t*>(&hi2);
+          }
+          __nv_bfloat16* op = out_ptr(head) + 64 * kw + 16 * c;
+          if (p.vec_o) {
+            reinterpret_cast<uint4*>(op)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            reinterpret_cast<uint4*>(op)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+          } else {
+            unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+            for (int i2 = 0; i2 < 8; ++i2) {
+              os[2 * i2] = (unsigned short)(wv[i2] & 0xffffu);
+              os[2 * i2 + 1] = (unsigned short)(wv[i2] >> 16);
+            }
           }
         }
       }
