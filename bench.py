@@ -78,11 +78,12 @@ def measured_peaks():
 # summary of that kernel.  Reported as roofline.traffic beside the algorithmic bytes.
 NCU_TRAFFIC = {
     "read": 157334784,         # sparse_attention_kernel<0>, 96 rows x 2 KV heads x top-2048 (one layer)
-    "mtp": 19768576,           # sparse_attention_mtp_kernel, config 4 (12 x 4 rows, top-2048)
+    "mtp": 19777280,           # sparse_attention_mtp_kernel, config 4 (12 x 4 rows, top-2048)
     "fp8": 210388736,          # sparse_attention_kernel<3>, 96 rows x top-2048, FP8 K/V
     "write": 16863744,         # write_cache_group_kernel, 8,192 tokens into 64 x 3,136
     "fused_write": 18579712,   # write_cache_kernel<256,...,FUSE>, 8,192 tokens
     "bf16": 413479424,         # sparse_attention_bf16_kernel, 96 rows x top-2048 (48-row capture x 2)
+    "topk": 50476800,          # topk_indices_kernel, 96 rows x 131,072 scores, k = 2048
 }
 
 
@@ -621,7 +622,8 @@ def bench_topk(device, steps):
     peak, kind = measured_peaks()
     a = res["5a"]
     res["roofline"] = {"bound": "hbm", "achieved": a["gb_per_s"], "peak": peak, "unit": "GB/s",
-                       "frac": a["gb_per_s"] / peak, "peak_kind": kind, "kernel": "topk_indices_kernel (96 rows)"}
+                       "frac": a["gb_per_s"] / peak, "peak_kind": kind, "kernel": "topk_indices_kernel (96 rows)",
+                       "algorithmic_bytes_per_launch": 96 * 131072 * 4 + 96 * 2048 * 4, "traffic": NCU_TRAFFIC["topk"]}
     res["gpu_launches"] = 2 * (max(40, steps) + 8)
     return res
 
