@@ -14,22 +14,23 @@
 // One CTA of 32 warps per row; warp w owns the w-th of 32 consecutive
 // position ranges of the row (a multiple of 32 positions each), so position
 // order is warp order.  On an order-preserving 32-bit key of each score:
-//   1. the CTA histograms the top 11 bits and finds the bin b1 holding the
-//      k-th largest key (shared atomics into 8 sub-histograms, one per four
-//      warps: score distributions put most keys in a few top-bit bins, and
-//      one shared histogram serialises its hot bins);
-//   2. every warp re-reads its range (from L2): it counts the keys above b1
-//      and keeps the keys inside b1 in a per-warp candidate list, while the
-//      CTA histograms their next 11 bits -> bin b2;
-//   3. the candidates inside (b1, b2) histogram their last 10 bits -> the k-th
-//      largest key T exactly, and how many keys equal to T are selected;
-//   4. per-warp counts of keys above T and equal to T, scanned over the
+//   1. the CTA histograms the top 11 bits (shared atomics into 8
+//      sub-histograms, one per four warps) and finds the bin b1 holding the
+//      k-th largest key;
+//   2. every warp re-reads its range (from L2) and keeps every key at or
+//      above b1 with its position in a per-warp list (position order), while
+//      the CTA histograms the next 11 bits of the keys inside b1 -> bin b2;
+//   3. the listed keys inside (b1, b2) histogram their last 10 bits -> the
+//      k-th largest key T exactly, and how many keys equal to T are selected;
+//   4. per-warp counts of listed keys above T and equal to T, scanned over the
 //      warps, give every warp its output offset and its share of the ties
 //      (lowest positions first);
-//   5. every warp re-reads its range in order and writes the selected
-//      positions with warp ballots: the output comes out sorted with no sort.
-// A warp whose candidates overflow its list recomputes steps 3 and 4 from its
-// range in global memory instead (many equal scores); the result is the same.
+//   5. every warp walks its list in order and writes the selected positions
+//      with warp ballots: the output comes out sorted with no sort and no
+//      third read of the scores.
+// A warp whose list overflows (the top keys concentrated in its range, or many
+// equal scores) recomputes steps 3-5 from its range in global memory instead;
+// the result is the same.
 // Every output store is bounds-checked against k.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -42,7 +43,7 @@ namespace {
 constexpr int kTkThreads = 1024;
 constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kTkBins = 2048;          // 11-bit digits (the last digit has 10 bits)
-constexpr int kTkCandPerWarp = 192;    // candidate keys kept per warp
+constexpr int kTkListPerWarp = 256;    // (key, position) pairs at or above the first pass's bin, per warp
 constexpr int kTkUnroll = 8;           // loads in flight per lane
 constexpr int kTkSubHists = 8;         // histogram copies (warp w adds into copy w / 4)
 
@@ -58,7 +59,8 @@ struct TopkParams {
 
 struct TopkSmem {
   int hist[kTkSubHists][kTkBins];
-  uint32_t ckey[kTkWarps][kTkCandPerWarp];
+  uint32_t lkey[kTkWarps][kTkListPerWarp];
+  int32_t lpos[kTkWarps][kTkListPerWarp];
   int warp_sums[kTkWarps];
   int wgt[kTkWarps];   // keys above T, per warp
   int weq[kTkWarps];   // keys equal to T, per warp
@@ -150,21 +152,22 @@ __global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkPara
     return;
   }
 
-  // this warp's positions [lo, hi): the warp-th of 32 ranges of a multiple of 32 positions
-  const int64_t span = (((len + kTkWarps - 1) / kTkWarps) + 31) & ~(int64_t)31;
-  const int64_t lo = min(len, (int64_t)warp * span);
-  const int64_t hi = min(len, lo + span);
+  // this warp's positions [lo, hi): the warp-th of 32 ranges of a multiple of 32 positions (int32: context
+  // < 2^31)
+  const int span = (int)((((len + kTkWarps - 1) / kTkWarps) + 31) & ~(int64_t)31);
+  const int lo = (int)min(len, (int64_t)warp * span);
+  const int hi = (int)min(len, (int64_t)lo + span);
   int* hist = sm.hist[warp / (kTkWarps / kTkSubHists)];
 
   for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
 
   // ---- 1. top 11 bits ----
-  for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+  for (int b = lo; b < hi; b += 32 * kTkUnroll) {
     float v[kTkUnroll];
 #pragma unroll
     for (int u = 0; u < kTkUnroll; ++u) {
-      const int64_t pos = b + u * 32 + lane;
+      const int pos = b + u * 32 + lane;
       v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
     }
 #pragma unroll
@@ -177,52 +180,53 @@ __global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkPara
   for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
 
-  // ---- 2. keys above b1 counted, keys inside b1 kept as candidates; their next 11 bits ----
-  int gt = 0, ncand = 0;
-  for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+  // ---- 2. keys at or above b1 kept in the warp's list, in position order; b1's next 11 bits ----
+  int nlist = 0;  // warp-uniform
+  for (int b = lo; b < hi; b += 32 * kTkUnroll) {
     float v[kTkUnroll];
 #pragma unroll
     for (int u = 0; u < kTkUnroll; ++u) {
-      const int64_t pos = b + u * 32 + lane;
+      const int pos = b + u * 32 + lane;
       v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
     }
 #pragma unroll
     for (int u = 0; u < kTkUnroll; ++u) {
-      const bool valid = b + u * 32 + lane < hi;
+      const int pos = b + u * 32 + lane;
       const uint32_t key = order_key(v[u]);
       const uint32_t d1 = key >> 21;
-      gt += (valid && d1 > b1) ? 1 : 0;
-      const bool in = valid && d1 == b1;
-      const uint32_t m = __ballot_sync(0xffffffffu, in);
-      if (in) {
-        const int idx = ncand + __popc(m & lt_mask);
-        if (idx < kTkCandPerWarp) sm.ckey[warp][idx] = key;
-        atomicAdd(&hist[(key >> 10) & (kTkBins - 1)], 1);
+      const bool keep = pos < hi && d1 >= b1;
+      const uint32_t m = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const int idx = nlist + __popc(m & lt_mask);
+        if (idx < kTkListPerWarp) {
+          sm.lkey[warp][idx] = key;
+          sm.lpos[warp][idx] = pos;
+        }
+        if (d1 == b1) atomicAdd(&hist[(key >> 10) & (kTkBins - 1)], 1);
       }
-      ncand += __popc(m);
+      nlist += __popc(m);
     }
   }
-  gt = warp_sum(gt);
   __syncthreads();
   const uint32_t b2 = select_bin(sm, kTkBins, need1);
   const int need2 = sm.s_need;
   for (int i = tid; i < kTkSubHists * kTkBins; i += kTkThreads) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
   const uint32_t prefix22 = (b1 << 11) | b2;
-  const bool listed = ncand <= kTkCandPerWarp;  // warp-uniform
+  const bool listed = nlist <= kTkListPerWarp;  // warp-uniform
 
-  // ---- 3. last 10 bits of the candidates inside (b1, b2) ----
+  // ---- 3. last 10 bits of the keys inside (b1, b2) ----
   if (listed) {
-    for (int i = lane; i < ncand; i += 32) {
-      const uint32_t key = sm.ckey[warp][i];
+    for (int i = lane; i < nlist; i += 32) {
+      const uint32_t key = sm.lkey[warp][i];
       if ((key >> 10) == prefix22) atomicAdd(&hist[key & 1023u], 1);
     }
   } else {
-    for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+    for (int b = lo; b < hi; b += 32 * kTkUnroll) {
       float v[kTkUnroll];
 #pragma unroll
       for (int u = 0; u < kTkUnroll; ++u) {
-        const int64_t pos = b + u * 32 + lane;
+        const int pos = b + u * 32 + lane;
         v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
       }
 #pragma unroll
@@ -239,18 +243,17 @@ __global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkPara
   // ---- 4. per-warp counts above and at T; offsets over the warps ----
   int wg = 0, we = 0;
   if (listed) {
-    for (int i = lane; i < ncand; i += 32) {
-      const uint32_t key = sm.ckey[warp][i];
+    for (int i = lane; i < nlist; i += 32) {
+      const uint32_t key = sm.lkey[warp][i];
       wg += key > T ? 1 : 0;
       we += key == T ? 1 : 0;
     }
-    wg = gt + warp_sum(wg);
   } else {
-    for (int64_t b = lo; b < hi; b += 32 * kTkUnroll) {
+    for (int b = lo; b < hi; b += 32 * kTkUnroll) {
       float v[kTkUnroll];
 #pragma unroll
       for (int u = 0; u < kTkUnroll; ++u) {
-        const int64_t pos = b + u * 32 + lane;
+        const int pos = b + u * 32 + lane;
         v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
       }
 #pragma unroll
@@ -261,45 +264,53 @@ __global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkPara
         we += (valid && key == T) ? 1 : 0;
       }
     }
-    wg = warp_sum(wg);
   }
+  wg = warp_sum(wg);
   we = warp_sum(we);
   if (lane == 0) {
     sm.wgt[warp] = wg;
     sm.weq[warp] = we;
   }
   __syncthreads();
-  int64_t gt_before = 0, eq_before = 0;
+  int gt_before = 0, eq_before = 0;
   for (int w = 0; w < warp; ++w) {
     gt_before += sm.wgt[w];
     eq_before += sm.weq[w];
   }
-  const int64_t sel_before = gt_before + min((int64_t)ties, eq_before);
-  const int64_t take_ties = max((int64_t)0, min((int64_t)we, (int64_t)ties - eq_before));
-  const int64_t sel = (int64_t)wg + take_ties;
+  const int sel_before = gt_before + min(ties, eq_before);
+  const int sel = wg + max(0, min(we, ties - eq_before));
 
-  // ---- 5. selected positions in order: ballots over 32 consecutive positions ----
-  int64_t written = 0, eq_seen = eq_before;
-  for (int64_t b = lo; b < hi && written < sel; b += 32 * kTkUnroll) {
-    float v[kTkUnroll];
-#pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u) {
-      const int64_t pos = b + u * 32 + lane;
-      v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+  // ---- 5. selected positions in order: ballots over the list (or over 32 consecutive positions) ----
+  int written = 0, eq_seen = eq_before;
+  auto emit = [&](uint32_t key, int pos, bool valid) {
+    const bool g = valid && key > T, e = valid && key == T;
+    const uint32_t em = __ballot_sync(0xffffffffu, e);
+    const bool take = g || (e && eq_seen + __popc(em & lt_mask) < ties);
+    const uint32_t tm = __ballot_sync(0xffffffffu, take);
+    const int oi = sel_before + written + __popc(tm & lt_mask);
+    if (take && oi < k) orow[oi] = pos;
+    written += __popc(tm);
+    eq_seen += __popc(em);
+  };
+  if (listed) {
+    for (int i0 = 0; i0 < nlist && written < sel; i0 += 32) {
+      const int i = i0 + lane;
+      const bool valid = i < nlist;
+      emit(valid ? sm.lkey[warp][i] : 0u, valid ? sm.lpos[warp][i] : 0, valid);
     }
+  } else {
+    for (int b = lo; b < hi && written < sel; b += 32 * kTkUnroll) {
+      float v[kTkUnroll];
 #pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u) {
-      const int64_t pos = b + u * 32 + lane;
-      const uint32_t key = order_key(v[u]);
-      const bool valid = pos < hi;
-      const bool g = valid && key > T, e = valid && key == T;
-      const uint32_t em = __ballot_sync(0xffffffffu, e);
-      const bool take = g || (e && eq_seen + __popc(em & lt_mask) < ties);
-      const uint32_t tm = __ballot_sync(0xffffffffu, take);
-      const int64_t oi = sel_before + written + __popc(tm & lt_mask);
-      if (take && oi < k) orow[oi] = (int32_t)pos;
-      written += __popc(tm);
-      eq_seen += __popc(em);
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const int pos = b + u * 32 + lane;
+        v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const int pos = b + u * 32 + lane;
+        emit(order_key(v[u]), pos, pos < hi);
+      }
     }
   }
 }

@@ -61,6 +61,15 @@ def test_topk_heavy_ties_at_decode_sizes(rows, context, levels):
     assert np.array_equal(got.cpu().numpy(), want)
 
 
+def test_topk_top_keys_concentrated_in_one_range():
+    # increasing / decreasing scores put every selected key in one warp's range: that warp's list overflows
+    base = torch.arange(50000, device="cuda", dtype=torch.float32)
+    s = torch.stack([base, -base, base.flip(0) * 0.5, torch.zeros_like(base)])
+    got = _select(s, 2048)
+    want = oracle.topk_indices(s.cpu().numpy(), 2048)
+    assert np.array_equal(got.cpu().numpy(), want)
+
+
 def test_topk_unaligned_rows_and_padded_output():
     # rows that start off a 16-byte boundary (scalar loads) and an output buffer wider than its rows' k
     g = torch.Generator(device="cuda").manual_seed(11)
