@@ -47,10 +47,6 @@ constexpr int kPhStride = 40;         // halfs per head row of the P tile (32 + 
 constexpr int kMtpRows = 4;           // rows per group (one S warp each)
 constexpr int kMtpMaxCluster = 8;     // splits of a group: one portable cluster
 constexpr int kMtpCompactIters = kMaxRange / kMtpThreads;
-#ifndef NVQSA_MTP_SUNROLL
-#define NVQSA_MTP_SUNROLL 16
-#endif
-constexpr int kMtpSUnroll = NVQSA_MTP_SUNROLL;
 
 struct __align__(128) SmemMtp {
   uint8_t rec[kMtpRing][kStageBytes];     // gather ring; after the last tile it holds the published O
@@ -470,7 +466,7 @@ __global__ void __launch_bounds__(kMtpThreads, 1) sparse_attention_mtp_kernel(co
 #pragma unroll
           for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
           const uint32_t kaddr = smem_u32(&sm.kh[buf][0][0]) + kh_lane;
-#pragma unroll kMtpSUnroll
+#pragma unroll
           for (int s = 0; s < 16; ++s) {
             uint32_t b0, b1, b2, b3, b4, b5, b6, b7;
             ldsm_x4(kaddr + 32u * s, b0, b1, b2, b3);
