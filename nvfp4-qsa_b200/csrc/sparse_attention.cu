@@ -686,9 +686,9 @@ template <int NFRAG, int SLOTS>
 __device__ __noinline__ bool cluster_merge_store(const AttnParams& p, const float4* comb, int64_t row, int kvh,
                                                  int G, int tid, int split, const int* abort_flag) {
   const int C = p.cluster;
-  bool ok = true;
-  for (int rk = 0; rk < C; ++rk) ok &= cluster_ld_s32(cluster_map(smem_u32(abort_flag), (uint32_t)rk)) == 0;
-  if (!ok) return false;  // the same for every thread: every rank published its abort flag before the barrier
+  // every rank published its abort flag before the caller's cluster barrier: thread rk reads rank rk's, all at once
+  const int bad = tid < C ? cluster_ld_s32(cluster_map(smem_u32(abort_flag), (uint32_t)tid)) : 0;
+  if (__syncthreads_or(bad)) return false;  // the same for every thread
   const uint32_t base = smem_u32(comb);
   if (C <= 2) cluster_merge_units<NFRAG, SLOTS, 8>(p, base, row, kvh, G, tid, split);
   else if (C <= 4) cluster_merge_units<NFRAG, SLOTS, 4>(p, base, row, kvh, G, tid, split);
