@@ -246,6 +246,9 @@ __device__ __forceinline__ int cluster_ld_s32(uint32_t addr) {
   asm volatile("ld.shared::cluster.s32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
   return v;
 }
+__device__ __forceinline__ void cluster_st_s32(uint32_t addr, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
 // Every thread of every CTA of the cluster arrives; shared-memory writes before it are visible after it.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
@@ -559,6 +562,113 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
   if (tid == 0) stamp_set(p, unit, 6);
 }
 
+// Split-KV beyond one cluster on one GPU, merged by the last cluster: every cluster's ranks have stored their
+// slices of the cluster's part (its normalised partial and lse); each fences them, rank 0 counts the cluster's
+// arrival at the unit's counter and writes into every rank of its cluster whether it was the last; then each
+// rank of the last cluster merges its slice of the unit's (head, 8 dims) items over all `nparts` parts -- one
+// item per thread, eight parts' loads in flight -- and stores it.  Called by every thread of every rank of a
+// cluster after the cluster merge (in place of its closing cluster barrier); `scratch` holds nparts * 16 + 32
+// floats of shared memory.
+__device__ __noinline__ void cluster_last_merge(const AttnParams& p, float* scratch, int* last, int64_t row, int kvh,
+                                                int G, int tid, int split) {
+  const int C = p.cluster, rank = split % C;
+  const int nparts = p.splits / C;
+  const int64_t unit = row * p.kv_heads + kvh;
+  __threadfence();  // this rank's slice of the part is visible device-wide before the cluster's arrival
+  cluster_sync();   // also: every rank keeps its shared memory until all ranks have read it
+  if (rank == 0) {
+    if (tid == 0) *last = atomicAdd(p.counters + unit, 1u) == (unsigned int)(nparts - 1) ? 1 : 0;
+    __syncthreads();
+    if (tid < C) cluster_st_s32(cluster_map(smem_u32(last), (uint32_t)tid), *last);
+  }
+  cluster_sync();  // every rank holds rank 0's verdict in its own shared memory
+  if (!*last) return;
+  if (rank == 0 && tid == 0) stamp_set(p, unit, 2);
+  __threadfence();  // the other parts, counted before ours, are visible
+  // every part's lse of this unit's heads, then per head its max, the weights 2^(lse - max) and their sum
+  float* wt = scratch;                // [nparts][16]
+  float* head_m = wt + nparts * 16;   // [16]
+  float* head_den = head_m + 16;      // [16]
+  const int64_t items = p.rows * p.query_heads;
+  const int64_t w0 = row * p.query_heads + (int64_t)kvh * G;
+  for (int i = tid; i < nparts * G; i += kThreads) {
+    const int part = i / G, j = i - part * G;
+    wt[part * 16 + j] = __ldcg(p.part_lse + (int64_t)part * items + w0 + j);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int part = 0; part < nparts; ++part) M = fmaxf(M, wt[part * 16 + tid]);
+    float den = 0.0f;
+    for (int part = 0; part < nparts; ++part) {
+      const float l = wt[part * 16 + tid];
+      const float x = (l == -INFINITY) ? 0.0f : exp2f(l - M);
+      wt[part * 16 + tid] = x;
+      den += x;
+    }
+    head_m[tid] = M;
+    head_den[tid] = den;
+  }
+  __syncthreads();
+  const int nitems = G * 32;
+  const int it = rank * nitems / C + tid;
+  if (it < (rank + 1) * nitems / C) {
+    const int j = it >> 5, d8 = it & 31;
+    const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    constexpr int kRound = 8;
+    for (int q0 = 0; q0 < nparts; q0 += kRound) {
+      float4 x[kRound], y[kRound];
+#pragma unroll
+      for (int v = 0; v < kRound; ++v) {
+        const bool in = q0 + v < nparts;
+        const float4* po = reinterpret_cast<const float4*>(base + (int64_t)(in ? q0 + v : 0) * items * kHeadDim);
+        x[v] = in ? __ldcg(po) : make_float4(0.f, 0.f, 0.f, 0.f);
+        y[v] = in ? __ldcg(po + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int v = 0; v < kRound; ++v) {
+        const float cw = q0 + v < nparts ? wt[(q0 + v) * 16 + j] : 0.0f;
+        acc[0] += cw * x[v].x; acc[1] += cw * x[v].y; acc[2] += cw * x[v].z; acc[3] += cw * x[v].w;
+        acc[4] += cw * y[v].x; acc[5] += cw * y[v].y; acc[6] += cw * y[v].z; acc[7] += cw * y[v].w;
+      }
+    }
+    const float den = head_den[j];
+    const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= inv;
+    const int head = kvh * G + j;
+    if (p.final_mode == 0) {
+      __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
+      uint32_t u4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        u4[i] = *reinterpret_cast<uint32_t*>(&b2);
+      }
+      if (p.vec_o) {
+        *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+      } else {
+        unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
+          os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
+        }
+      }
+    } else {
+      float* op = p.final_out + (row * p.query_heads + head) * kHeadDim + d8 * 8;
+      reinterpret_cast<float4*>(op)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(op)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      if (d8 == 0) p.final_lse[row * p.query_heads + head] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+    }
+  }
+  if (tid == 0) {
+    stamp_max(p, unit, 3);
+    stamp_max(p, unit, 6);
+  }
+}
+
 // Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
 // normalised partial and lse to the workspace; the last part to arrive at the unit's
 // counter merges all parts.  Called by every thread of the CTA.
@@ -589,8 +699,9 @@ __device__ __noinline__ void fused_part_merge(const AttnParams& p, float* scratc
 // (i, q) holds, for lane (r, c) = (q & 31) / 4, (q & 31) % 4, dims D = 128 h + 32 c + k and D + 16 of
 // heads r and r + 8, where (h, k) = (i / 16, i % 16) when SLOTS = 32 (full-width reader) and (q / 32, i)
 // when SLOTS = 64 (warp pairs); so the 16 float4 of one (q, h) run cover 16 consecutive dims.  Work units
-// are GE consecutive float4 of a run (GE = 8, 4, 2 for clusters of <= 2, 4, 8): each rank takes every C-th
-// unit, loads the run's (m, l) and its GE float4 from every rank over distributed shared memory (all in
+// are GE consecutive float4 of a run (GE = 8, 4, 2 for clusters of <= 2, 4, 8), numbered run-fastest so that
+// consecutive threads read consecutive slots of a rank; rank r takes the units [128 (r + kC), 128 (r + kC) + 128),
+// k = 0, 1, ...; a unit loads its run's (m, l) and its GE float4 from every rank over distributed shared memory (all in
 // flight together), weights them by 2^(m_rank - max) and stores the merged, normalised dims as vectors
 // (bf16 output, or the fp32 partial and its lse).  Returns false (nothing stored) when a rank aborted.
 template <int NFRAG, int SLOTS, int GE>
@@ -601,7 +712,7 @@ __device__ __forceinline__ void cluster_merge_units(const AttnParams& p, uint32_
   constexpr int kRanks = 16 / GE;       // largest cluster this unit width serves (C <= kRanks)
   constexpr int kUnits = 64 * kGroups;  // (q, h) runs: 32 lanes x 2 halves, or 64 slots
   for (int u = rank * kThreads + tid; u < kUnits; u += C * kThreads) {
-    const int run = u / kGroups, g = u % kGroups;
+    const int run = u % 64, g = u / 64;  // consecutive threads read consecutive slots of a rank
     const int q = SLOTS == 32 ? run >> 1 : run;
     const int h = SLOTS == 32 ? run & 1 : q >> 5;
     const int i0 = (SLOTS == 32 ? 16 * h : 0) + g * GE;
@@ -1244,6 +1355,10 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     }
     cluster_sync();
     const bool ok = cluster_merge_store<32, 32>(p, comb, row, kvh, G, tid, split, &sm.abort);
+    if (p.fuse && p.xworld == 0 && ok) {  // one GPU: the last cluster to arrive merges the parts, a slice per rank
+      cluster_last_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), &sm.last, row, kvh, G, tid, split);
+      return;
+    }
     cluster_sync();  // every rank keeps its shared memory until all ranks have read it; slices are stored
     if (!ok) return;
     if (p.fuse) {
