@@ -55,6 +55,7 @@ struct TopkParams {
   int32_t k;
   int32_t* out;
   int64_t out_stride;      // elements between rows
+  int32_t vec;             // every row starts 16-byte aligned: the first pass loads float4
 };
 
 struct TopkSmem {
@@ -163,16 +164,42 @@ __global__ void __launch_bounds__(kTkThreads) topk_indices_kernel(const TopkPara
   __syncthreads();
 
   // ---- 1. top 11 bits ----
-  for (int b = lo; b < hi; b += 32 * kTkUnroll) {
-    float v[kTkUnroll];
+  if (p.vec) {  // lane -> 4 consecutive positions (lo is a multiple of 32, the row 16-byte aligned)
+    for (int b = lo; b < hi; b += 128 * (kTkUnroll / 2)) {
+      float4 v[kTkUnroll / 2];
 #pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u) {
-      const int pos = b + u * 32 + lane;
-      v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+      for (int u = 0; u < kTkUnroll / 2; ++u) {
+        const int pos = b + u * 128 + lane * 4;
+        if (pos + 3 < hi) {
+          v[u] = __ldg(reinterpret_cast<const float4*>(srow + pos));
+        } else {
+          v[u].x = pos < hi ? __ldg(srow + pos) : 0.0f;
+          v[u].y = pos + 1 < hi ? __ldg(srow + pos + 1) : 0.0f;
+          v[u].z = pos + 2 < hi ? __ldg(srow + pos + 2) : 0.0f;
+          v[u].w = 0.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kTkUnroll / 2; ++u) {
+        const int pos = b + u * 128 + lane * 4;
+        if (pos < hi) atomicAdd(&hist[order_key(v[u].x) >> 21], 1);
+        if (pos + 1 < hi) atomicAdd(&hist[order_key(v[u].y) >> 21], 1);
+        if (pos + 2 < hi) atomicAdd(&hist[order_key(v[u].z) >> 21], 1);
+        if (pos + 3 < hi) atomicAdd(&hist[order_key(v[u].w) >> 21], 1);
+      }
     }
+  } else {
+    for (int b = lo; b < hi; b += 32 * kTkUnroll) {
+      float v[kTkUnroll];
 #pragma unroll
-    for (int u = 0; u < kTkUnroll; ++u)
-      if (b + u * 32 + lane < hi) atomicAdd(&hist[order_key(v[u]) >> 21], 1);
+      for (int u = 0; u < kTkUnroll; ++u) {
+        const int pos = b + u * 32 + lane;
+        v[u] = pos < hi ? __ldg(srow + pos) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kTkUnroll; ++u)
+        if (b + u * 32 + lane < hi) atomicAdd(&hist[order_key(v[u]) >> 21], 1);
+    }
   }
   __syncthreads();
   const uint32_t b1 = select_bin(sm, kTkBins, k);
@@ -336,6 +363,7 @@ extern "C" int nvqsa_topk_indices(const float* scores, int64_t score_stride_row,
   p.k = k;
   p.out = out;
   p.out_stride = out_stride_row;
+  p.vec = ((reinterpret_cast<uintptr_t>(scores) & 15u) == 0 && (score_stride_row & 3) == 0) ? 1 : 0;
   static std::atomic<bool> configured[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NVQSA_ERR_CUDA;
