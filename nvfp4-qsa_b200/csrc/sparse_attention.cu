@@ -562,11 +562,31 @@ __device__ __noinline__ void xrank_exchange(const AttnParams& p, float* scratch,
   if (tid == 0) stamp_set(p, unit, 6);
 }
 
-// Split-KV beyond one cluster on one GPU, merged by the last cluster: every cluster's ranks have stored their
-// slices of the cluster's part (its normalised partial and lse); each fences them, rank 0 counts the cluster's
-// arrival at the unit's counter and writes into every rank of its cluster whether it was the last; then each
-// rank of the last cluster merges its slice of the unit's (head, 8 dims) items over all `nparts` parts -- one
-// item per thread, eight parts' loads in flight -- and stores it.  Called by every thread of every rank of a
+// Eight fp32 -> bf16 (round to nearest even) at op: one 16-byte store, or eight 2-byte stores.
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* op, const float (&v)[8], int vec) {
+  uint32_t u4[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    u4[i] = *reinterpret_cast<uint32_t*>(&b2);
+  }
+  if (vec) {
+    *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+  } else {
+    unsigned short* os = reinterpret_cast<unsigned short*>(op);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
+      os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
+    }
+  }
+}
+
+// Split-KV beyond one cluster, merged by the last cluster: every cluster's ranks have stored their slices of
+// the cluster's part (its normalised partial and lse); each fences them, rank 0 counts the cluster's arrival
+// at the unit's counter and writes into every rank of its cluster whether it was the last; then each rank of
+// the last cluster merges its slice of the unit's (head, 8 dims) items over all `nparts` parts -- one item per
+// thread, eight parts' loads in flight -- and stores it, or, across GPUs, exchanges it and merges the GPUs.  Called by every thread of every rank of a
 // cluster after the cluster merge (in place of its closing cluster barrier); `scratch` holds nparts * 16 + 32
 // floats of shared memory.
 __device__ __noinline__ void cluster_last_merge(const AttnParams& p, float* scratch, int* last, int64_t row, int kvh,
@@ -612,10 +632,13 @@ __device__ __noinline__ void cluster_last_merge(const AttnParams& p, float* scra
   __syncthreads();
   const int nitems = G * 32;
   const int it = rank * nitems / C + tid;
-  if (it < (rank + 1) * nitems / C) {
-    const int j = it >> 5, d8 = it & 31;
+  const bool has_item = it < (rank + 1) * nitems / C;
+  const int j = has_item ? it >> 5 : 0, d8 = it & 31;
+  const int head = kvh * G + j;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float my_lse = -INFINITY;
+  if (has_item) {
     const float* base = p.part_out + (w0 + j) * kHeadDim + d8 * 8;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     constexpr int kRound = 8;
     for (int q0 = 0; q0 < nparts; q0 += kRound) {
       float4 x[kRound], y[kRound];
@@ -637,36 +660,119 @@ __device__ __noinline__ void cluster_last_merge(const AttnParams& p, float* scra
     const float inv = den > 0.0f ? 1.0f / den : 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] *= inv;
-    const int head = kvh * G + j;
-    if (p.final_mode == 0) {
-      __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
-      uint32_t u4[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-        u4[i] = *reinterpret_cast<uint32_t*>(&b2);
-      }
-      if (p.vec_o) {
-        *reinterpret_cast<uint4*>(op) = make_uint4(u4[0], u4[1], u4[2], u4[3]);
+    my_lse = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+  }
+  if (p.xworld == 0) {
+    if (has_item) {
+      if (p.final_mode == 0) {
+        __nv_bfloat16* op = p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8;
+        store_bf16x8(op, acc, p.vec_o);
       } else {
-        unsigned short* os = reinterpret_cast<unsigned short*>(op);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          os[2 * i] = (unsigned short)(u4[i] & 0xffffu);
-          os[2 * i + 1] = (unsigned short)(u4[i] >> 16);
-        }
+        float* op = p.final_out + (row * p.query_heads + head) * kHeadDim + d8 * 8;
+        reinterpret_cast<float4*>(op)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        reinterpret_cast<float4*>(op)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (d8 == 0) p.final_lse[row * p.query_heads + head] = my_lse;
       }
-    } else {
-      float* op = p.final_out + (row * p.query_heads + head) * kHeadDim + d8 * 8;
-      reinterpret_cast<float4*>(op)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      reinterpret_cast<float4*>(op)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      if (d8 == 0) p.final_lse[row * p.query_heads + head] = den > 0.0f ? head_m[j] + log2f(den) : -INFINITY;
+    }
+    if (tid == 0) {
+      stamp_max(p, unit, 3);
+      stamp_max(p, unit, 6);
+    }
+    return;
+  }
+
+  // ---- across GPUs: every rank of the last cluster pushes its slice of this GPU's merged (O, lse) into slot
+  // xrank of every other GPU's exchange buffer; rank 0 publishes a flag per destination (release) and waits
+  // for every other GPU's flag (acquire, bounded by time); then each rank merges its slice over the GPUs.
+  if (tid == 0) stamp_max(p, unit, 3);
+  const int world = p.xworld, me = p.xrank;
+  const int64_t units = p.rows * p.kv_heads;
+  float* mine = p.xpeer[me];
+  auto lse_of = [&](float* b) { return b + (int64_t)world * items * kHeadDim; };
+  auto flag_of = [&](float* b, int src) {
+    return reinterpret_cast<unsigned int*>(lse_of(b) + (int64_t)world * items) +
+           ((int64_t)p.xparity * units + unit) * world + src;
+  };
+  if (has_item) {
+    for (int r = 0; r < world; ++r) {
+      if (r == me) continue;
+      float4* dst = reinterpret_cast<float4*>(p.xpeer[r] + ((int64_t)me * items + w0 + j) * kHeadDim + d8 * 8);
+      dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      if (d8 == 0) lse_of(p.xpeer[r])[(int64_t)me * items + w0 + j] = my_lse;
     }
   }
-  if (tid == 0) {
-    stamp_max(p, unit, 3);
-    stamp_max(p, unit, 6);
+  // Every thread's peer stores precede rank 0's system-scope release of the flags in causality order (the
+  // cluster barrier), so each flag makes them visible to the GPU that acquires it.
+  cluster_sync();
+  if (rank == 0) {
+    if (tid == 0) {
+      for (int r = 0; r < world; ++r) {
+        if (r == me) continue;
+        asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(flag_of(p.xpeer[r], me)), "r"(1u) : "memory");
+      }
+      stamp_set(p, unit, 4);
+      unsigned long long t0;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      int ok = 1;
+      for (int r = 0; r < world && ok; ++r) {
+        if (r == me) continue;
+        unsigned int* f = flag_of(mine, r);
+        while (true) {
+          unsigned int v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(f) : "memory");
+          if (v) break;
+          unsigned long long t;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+          if (t - t0 > kPeerWaitNs) {  // a GPU that never arrives cannot hang this one
+            ok = 0;
+            atomicOr(&g_error_flags, kErrPeerTimeout);
+            break;
+          }
+          __nanosleep(200);
+        }
+      }
+      *last = ok;
+      stamp_set(p, unit, 5);
+      for (int r = 0; r < world; ++r) *flag_of(mine, r) = 0u;  // re-arm this parity for the call after next
+    }
+    __syncthreads();
+    if (tid < C) cluster_st_s32(cluster_map(smem_u32(last), (uint32_t)tid), *last);
   }
+  cluster_sync();  // every rank holds rank 0's result of the wait, which acquired the other GPUs' slots
+  if (!*last) return;
+  if (has_item) {
+    float lr[8];
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      lr[r] = -INFINITY;
+      if (r < world) lr[r] = r == me ? my_lse : __ldcg(lse_of(mine) + (int64_t)r * items + w0 + j);
+      M = fmaxf(M, lr[r]);
+    }
+    float out[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float den = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= world) break;
+      const float w = lr[r] == -INFINITY ? 0.0f : exp2f(lr[r] - M);
+      den += w;
+      if (r == me) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] += w * acc[i];
+      } else {
+        const float4* src = reinterpret_cast<const float4*>(mine + ((int64_t)r * items + w0 + j) * kHeadDim + d8 * 8);
+        const float4 a = __ldcg(src), b = __ldcg(src + 1);
+        out[0] += w * a.x; out[1] += w * a.y; out[2] += w * a.z; out[3] += w * a.w;
+        out[4] += w * b.x; out[5] += w * b.y; out[6] += w * b.z; out[7] += w * b.w;
+      }
+    }
+    const float inv = den > 0.0f ? 1.0f / den : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] *= inv;
+    store_bf16x8(p.out + row * p.o_stride_row + (int64_t)head * p.o_stride_head + d8 * 8, out, p.vec_o);
+  }
+  if (tid == 0) stamp_max(p, unit, 6);
 }
 
 // Split-KV beyond one cluster: every part (one per cluster, its rank 0) has written its
@@ -1355,7 +1461,7 @@ __global__ void __launch_bounds__(kThreads, 3) sparse_attention_kernel(const __g
     }
     cluster_sync();
     const bool ok = cluster_merge_store<32, 32>(p, comb, row, kvh, G, tid, split, &sm.abort);
-    if (p.fuse && p.xworld == 0 && ok) {  // one GPU: the last cluster to arrive merges the parts, a slice per rank
+    if (p.fuse && ok) {  // the last cluster to arrive merges the parts (and exchanges them), a slice per rank
       cluster_last_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), &sm.last, row, kvh, G, tid, split);
       return;
     }

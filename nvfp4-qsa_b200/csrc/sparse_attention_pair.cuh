@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 4) sparse_attention_pair_kernel(cons
     }
     cluster_sync();
     const bool ok = cluster_merge_store<16, 64>(p, comb, row, kvh, G, tid, split, &sm.abort);
-    if (p.fuse && p.xworld == 0 && ok) {  // one GPU: the last cluster to arrive merges the parts, a slice per rank
+    if (p.fuse && ok) {  // the last cluster to arrive merges the parts (and exchanges them), a slice per rank
       cluster_last_merge(p, reinterpret_cast<float*>(&sm.rec[0][0][0]), &sm.last, row, kvh, G, tid, split);
       return;
     }
