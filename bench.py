@@ -57,6 +57,7 @@ def parse_args():
     ap.add_argument("--skip-mtp", action="store_true", help="skip the MTP (config 4) section")
     ap.add_argument("--skip-fp8", action="store_true", help="skip the FP8 sibling-reader section")
     ap.add_argument("--skip-bf16", action="store_true", help="skip the BF16 sibling-reader section")
+    ap.add_argument("--skip-proj", action="store_true", help="skip the fused K/V projection section")
     return ap.parse_args()
 
 
@@ -71,6 +72,16 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense bf16 TFLOP/s: the measured burst figure (a kernel timed in isolation), else the fallback."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each timed kernel, from one ncu
@@ -334,6 +345,95 @@ def bench_fused_write(device, steps):
                      "algorithmic_bytes_per_launch": algo,
                      "traffic": NCU_TRAFFIC["fused_write"]},
         "gpu_launches": launches + launches_ko,
+    }
+
+
+def bench_kv_proj_write(device, steps):
+    """K/V projection GEMM fused with k-norm, RoPE, NVFP4 quantisation and the scatter, against the chain it
+    replaces (cuBLAS projection into bf16 K|V, then the fused norm/RoPE writer), on the prefill configuration.
+
+    8,192 tokens, hidden size 4,096 (the reference's architecture file gives no hidden size; 4,096 is assumed),
+    2 KV heads x 256 for K and for V (1,024 output columns), GemmaRMSNorm and a 64-dim NeoX rotary, into a
+    64 x 3,136 cache.  3 rotating sets of hidden states and weights (216 MB > L2) per CUDA-graph round.
+    """
+    import torch
+    from nvfp4_qsa import kernels
+    from nvfp4_qsa import workloads as W
+
+    tokens, hidden, blocks, page, sets, rot, max_pos = 8192, 4096, 64, 3136, 3, 64, 262144
+    cols = 2 * KV_HEADS * HEAD_DIM
+    gen = torch.Generator(device=device).manual_seed(77)
+    cos_sin = torch.from_numpy(W.rope_cos_sin(max_pos, rot)).to(device=device, dtype=torch.bfloat16)
+    weight = (torch.randn(HEAD_DIM, device=device, generator=gen) * 0.1).to(torch.bfloat16).float()
+    bufs = []
+    for i in range(sets):
+        x = torch.randn(tokens, hidden, device=device, generator=gen).to(torch.bfloat16)
+        wkv = (torch.randn(cols, hidden, device=device, generator=gen) * hidden ** -0.5).to(torch.bfloat16)
+        storage = torch.zeros(blocks, KV_HEADS, page, RECORD, dtype=torch.uint8, device=device)
+        parts = storage.transpose(1, 2).split(HEAD_DIM // 2 + HEAD_DIM // 16, dim=-1)
+        kd, ks = parts[0].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        vd, vs = parts[1].split((HEAD_DIM // 2, HEAD_DIM // 16), dim=-1)
+        slots = torch.randperm(blocks * page, device=device, generator=gen)[:tokens].contiguous()
+        pos = torch.randint(0, max_pos, (tokens,), device=device, generator=gen)
+        kv = torch.empty(tokens, cols, device=device, dtype=torch.bfloat16)
+        bufs.append((x, wkv, (kd, ks, vd, vs), slots, pos, kv))
+
+    def fused_round():
+        for x, wkv, regs, slots, pos, _ in bufs:
+            kernels.qsa_kv_proj_write_cache_nvfp4(x, wkv[:cols // 2], wkv[cols // 2:], *regs, slots, 1.0, 1.0,
+                                                  positions=pos, cos_sin_cache=cos_sin, k_norm_weight=weight,
+                                                  eps=1e-6)
+
+    def chain_round():
+        for x, wkv, regs, slots, pos, kv in bufs:
+            torch.mm(x, wkv.t(), out=kv)
+            k = kv[:, :cols // 2].view(tokens, KV_HEADS, HEAD_DIM)
+            v = kv[:, cols // 2:].view(tokens, KV_HEADS, HEAD_DIM)
+            kernels.qsa_norm_rope_write_cache_nvfp4(k, v, *regs, slots, 1.0, 1.0, positions=pos,
+                                                    cos_sin_cache=cos_sin, k_norm_weight=weight, eps=1e-6)
+
+    def gemm_round():
+        for x, wkv, _, _, _, kv in bufs:
+            torch.mm(x, wkv.t(), out=kv)
+
+    def measure(body):
+        body()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            body()
+        torch.cuda.current_stream(device).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            body()
+        for _ in range(3):
+            graph.replay()
+        rounds = max(10, steps // 4)
+        secs = timed(graph.replay, rounds, device)
+        del graph
+        return secs / (rounds * sets), rounds * sets
+
+    fused, launches = measure(fused_round)
+    chain, _ = measure(chain_round)
+    gemm, _ = measure(gemm_round)
+    flops = 2.0 * tokens * hidden * cols
+    peak, kind = measured_tensor_peak()
+    achieved = flops / fused / 1e12
+    return {
+        "config": {"workload": "prefill: hidden [8192, 4096] bf16 x K|V weight [1024, 4096] bf16 (2 KV heads x 256 "
+                               "each), GemmaRMSNorm + NeoX rotary 64 of 256 on K, NVFP4 into a 64 x 3136 cache at "
+                               "random free slots; 3 rotating sets of hidden states and weights (inputs > L2)",
+                   "hidden_size_assumed": hidden, "launches": launches},
+        "us_per_launch": fused * 1e6,
+        "tflops": achieved,
+        "unfused_us": chain * 1e6,
+        "unfused": "torch.mm (cuBLAS) into bf16 K|V [8192, 1024], then nvqsa_norm_rope_write_cache",
+        "cublas_gemm_only_us": gemm * 1e6,
+        "speedup_vs_unfused": chain / fused,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_kind": kind, "kernel": "kv_proj_write_kernel",
+                     "algorithmic_flops_per_launch": flops, "traffic": None},
+        "gpu_launches": launches,
     }
 
 
@@ -1039,6 +1139,7 @@ def main_ours(args):
     split = None if args.skip_split else bench_split_kv(args, device, world, rank, args.steps)
     write = bench_write(device, args.steps) if rank == 0 else None
     fused_write = bench_fused_write(device, args.steps) if rank == 0 else None
+    kv_proj = bench_kv_proj_write(device, args.steps) if rank == 0 and not args.skip_proj else None
     # config 4 and the FP8 sibling reader are single-GPU side measurements: one GPU runs only
     mtp = bench_mtp(args, device, args.steps) if world == 1 and not args.skip_mtp else None
     fp8 = bench_fp8(args, device, args.steps) if world == 1 and not args.skip_fp8 else None
@@ -1083,6 +1184,7 @@ def main_ours(args):
             "gpu_launches": args.steps * args.layers * launches_per_layer,
             "write": write,
             "fused_write": fused_write,
+            "kv_proj_write": kv_proj,
         }
         if split is not None:
             result["split_kv"] = split

@@ -139,6 +139,55 @@ int nvqsa_norm_rope_write_cache(
     void* key_out, int64_t key_out_stride_token, int64_t key_out_stride_head, void* stream);
 
 /*
+ * The K and V columns of the attention layer's QKV projection, computed and
+ * written to the NVFP4 cache in ONE launch (tensor-core GEMM whose epilogue is
+ * nvqsa_norm_rope_write_cache): the bf16 K and V never go through HBM.
+ *
+ * Replaces, at the reference's call site (integration/snapshot/qsa.py:658-667
+ * -> :618-640: qkv_proj -> split -> k_norm -> rotary_emb ->
+ * qsa_write_cache_nvfp4), the K/V part of the projection plus the norm,
+ * rotation and writer.  For token t and kv head h:
+ *   K[t, h, :] = bf16_rn(sum_c hidden[t, c] * key_weight[h*256 + d, c]),
+ *   V likewise with value_weight (fp32 accumulation; the order of the sum is
+ *   the tensor cores', so a value can differ by one bf16 ulp from another
+ *   GEMM's), then K goes through the norm and rotation and both are encoded
+ *   and scattered exactly as nvqsa_norm_rope_write_cache does with these K and
+ *   V (same skip rules for positions and slots, same bytes).
+ * hidden    : bf16 [num_tokens, hidden_size], row stride hidden_stride_token
+ *             elements; key_weight / value_weight: bf16 [kv_heads*256,
+ *             hidden_size] (the K and V row blocks of the QKV weight), row
+ *             stride weight_stride_row.  Bases 16-byte aligned, row strides
+ *             multiples of 8 elements (NVQSA_ERR_MISALIGNED).
+ * head_dim  : 256 only (NVQSA_ERR_HEAD_DIM).
+ * cache     : the four regions must be views of one [blocks, kv_heads, page,
+ *             288]-style record storage with shared strides (the reference's
+ *             and vLLM's layout) and 8-byte aligned strides and bases, else
+ *             NVQSA_ERR_MISALIGNED.
+ * rotation  : rotary_dim a multiple of 32 (NeoX) or 16 (GPT-J), at most 256;
+ *             the cos/sin table's base and row stride 16-byte aligned.
+ * norm_weight (fp32 [256], 16-byte aligned) or NULL; eps as the fused writer.
+ * key_out   : optional bf16 [num_tokens, kv_heads, 256] rotated K (rows of
+ *             tokens with a valid position), value_out: optional bf16 V
+ *             projection (every token); bases and strides 16-byte aligned.
+ * A wait of the kernel that runs out sets bit 2 of nvqsa_read_error_flags.
+ * No counterpart entry in the reference (its projection is vLLM's GEMM).
+ */
+int nvqsa_kv_proj_write_cache(
+    const void* hidden, int64_t hidden_stride_token, int64_t num_tokens, int32_t hidden_size,
+    const void* key_weight, const void* value_weight, int64_t weight_stride_row,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size, float key_global_scale, float value_global_scale,
+    const float* norm_weight, float norm_weight_offset, float eps,
+    const int64_t* positions, const void* cos_sin_cache, int64_t cos_sin_stride, int64_t max_position,
+    int32_t rotary_dim, int32_t is_neox_style,
+    void* key_out, int64_t key_out_stride_token, int64_t key_out_stride_head,
+    void* value_out, int64_t value_out_stride_token, int64_t value_out_stride_head, void* stream);
+
+/*
  * Bytes of workspace nvqsa_sparse_attention needs for this problem on the
  * current device (0 when the problem runs without a split-KV merge).
  */

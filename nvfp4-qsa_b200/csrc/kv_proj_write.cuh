@@ -1,0 +1,352 @@
+// K/V projection GEMM with the NVFP4 cache writer as its epilogue, on the
+// 5th-generation tensor cores.  Included by write_cache.cu inside namespace
+// nvqsa::{anonymous}; uses its parameter block, scale table, encoder and slot
+// helpers, so the bytes it writes are those of nvqsa_norm_rope_write_cache.
+//
+// The reference's attention layer computes qkv = hidden @ W_qkv^T (vLLM's
+// QKVParallelLinear, bf16 output), splits K and V off it, runs k_norm and the
+// rotary embedding on K and only then calls the writer
+// (integration/snapshot/qsa.py:658-667 -> :618-640).  Here the K and V
+// columns of that GEMM are computed and encoded in one launch, so the bf16 K
+// and V never reach HBM unless key_out / value_out ask for them.
+//
+// One CTA = 128 tokens x one head (256 columns) of K or of V.  Warp 4 streams
+// 64-wide k-slices of the hidden rows (16 KB) and of the head's weight rows
+// (32 KB) through a 4-stage ring with TMA (128-byte swizzle); one thread of
+// warp 5 issues the tcgen05.mma (M 128, N 256, K 16, bf16 -> fp32) into a
+// 128 x 256 fp32 accumulator in tensor memory and releases each stage with
+// tcgen05.commit.  Warps 0-3 (one per tensor-memory lane quarter: thread =
+// token row) then read the row back, round it to bf16 as the GEMM output
+// would be, and run the writer's arithmetic on whole 16-element groups: for
+// K the RMS norm (the writer's summation order, emulated in one thread),
+// the rotation (bf16 arithmetic, NeoX halves or GPT-J pairs), then the
+// group scale and E2M1 codes; for V the codes alone.
+constexpr int kPwBM = 128;        // tokens per CTA (tensor-memory lanes)
+constexpr int kPwBN = 256;        // columns per CTA: one head
+constexpr int kPwBK = 64;         // k-slice per stage: 128 bytes of bf16 (one swizzle atom row)
+constexpr int kPwStages = 4;
+constexpr int kPwThreads = 192;   // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
+constexpr uint32_t kPwStageA = kPwBM * kPwBK * 2;  // 16 KB
+constexpr uint32_t kPwStageB = kPwBN * kPwBK * 2;  // 32 KB
+constexpr uint32_t kPwSpinLimit = 1u << 24;        // bounded mbarrier waits (the mainloop is tens of us)
+constexpr unsigned int kErrProjWait = 4u;          // bit 2 of the error flags: a projection-writer wait ran out
+
+__device__ unsigned int g_write_error_flags;
+
+struct __align__(1024) SmemPw {
+  uint8_t a[kPwStages][kPwStageA];  // hidden rows, swizzled 128-byte rows (1024-byte aligned atoms)
+  uint8_t b[kPwStages][kPwStageB];  // weight rows
+  unsigned long long full[kPwStages];
+  unsigned long long empty[kPwStages];
+  unsigned long long accum;
+  uint32_t tmem;
+  float lut[2][256];
+  float quot[2][16];
+};
+
+struct ProjParams {
+  CUtensorMap map_x;      // hidden [tokens, hidden] bf16, box 64 x 128
+  CUtensorMap map_w[2];   // K / V weight rows [kv_heads * 256, hidden] bf16, box 64 x 256
+  WriteParams w;          // cache regions, slots, scales, norm and rotation (head_dim 256, record layout)
+  int32_t kblocks;        // hidden / 64, rounded up (the tail is zero-filled by TMA)
+  __nv_bfloat16* value_out;  // optional bf16 V projection [tokens, kv_heads, 256]
+  int64_t value_out_stride_token, value_out_stride_head;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void pw_mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool pw_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool pw_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kPwSpinLimit; ++i)
+    if (pw_try_wait(bar, parity)) return true;
+  atomicOr(&g_write_error_flags, kErrProjWait);
+  return false;
+}
+__device__ __forceinline__ void pw_tma_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
+      ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// Shared-memory matrix descriptor: K-major operand in 128-byte swizzled rows, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t pw_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3fffu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: D f32, A and B bf16, both K-major, N = 256, M = 128.
+constexpr uint32_t kPwIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPwBN >> 3) << 17) |
+                              ((uint32_t)(kPwBM >> 4) << 24);
+
+__device__ __forceinline__ void pw_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void pw_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's tensor-memory lane, rounded to bf16 pairs (the GEMM's output).
+__device__ __forceinline__ void pw_load_bf16(uint32_t taddr, uint32_t (&w)[8]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+}
+
+__global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __grid_constant__ ProjParams p) {
+  extern __shared__ __align__(1024) uint8_t pw_smem_raw[];
+  SmemPw& sm = *reinterpret_cast<SmemPw*>(pw_smem_raw + ((1024u - (smem_u32(pw_smem_raw) & 1023u)) & 1023u));
+  const WriteParams& wp = p.w;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kvh = wp.kv_heads;
+  const int nt = blockIdx.x;  // 0 .. kvh-1: K head nt; kvh .. 2 kvh-1: V head nt - kvh
+  const int r = nt < kvh ? 0 : 1;
+  const int head = nt - r * kvh;
+  const int64_t m0 = (int64_t)blockIdx.y * kPwBM;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kPwStages; ++s) {
+      pw_mbar_init(smem_u32(&sm.full[s]), 1);
+      pw_mbar_init(smem_u32(&sm.empty[s]), 1);
+    }
+    pw_mbar_init(smem_u32(&sm.accum), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&sm.tmem)),
+                 "r"(kPwBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  build_out_scale_lut(wp, sm.lut, sm.quot);
+  pw_fence_before();
+  __syncthreads();
+  pw_fence_after();
+  const uint32_t tmem = sm.tmem;
+  const int kb = p.kblocks;
+
+  if (warp == 4) {
+    // ---------------- producer: TMA into the stage ring ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < kb; ++i) {
+        const int s = i % kPwStages;
+        if (i >= kPwStages && !pw_wait(smem_u32(&sm.empty[s]), (uint32_t)(((i / kPwStages) & 1) ^ 1))) break;
+        const uint32_t full = smem_u32(&sm.full[s]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(full),
+                     "r"(kPwStageA + kPwStageB)
+                     : "memory");
+        pw_tma_2d(smem_u32(sm.a[s]), &p.map_x, i * kPwBK, (int32_t)m0, full);
+        pw_tma_2d(smem_u32(sm.b[s]), &p.map_w[r], i * kPwBK, head * kPwBN, full);
+        issued = i + 1;
+      }
+      // copies still in flight land before the CTA can leave (only a timed-out consumer leaves them)
+      for (int j = issued > kPwStages ? issued - kPwStages : 0; j < issued; ++j)
+        pw_wait(smem_u32(&sm.full[j % kPwStages]), (uint32_t)((j / kPwStages) & 1));
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issue: one thread ----------------
+    if (lane == 0) {
+      for (int i = 0; i < kb; ++i) {
+        const int s = i % kPwStages;
+        if (!pw_wait(smem_u32(&sm.full[s]), (uint32_t)((i / kPwStages) & 1))) break;
+        pw_fence_after();
+        const uint64_t da = pw_desc(smem_u32(sm.a[s])), db = pw_desc(smem_u32(sm.b[s]));
+#pragma unroll
+        for (int k = 0; k < kPwBK / 16; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          // advancing the start address by 32 bytes steps 16 elements along K inside the swizzled row
+          asm volatile(
+              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+              "l"(da + (uint64_t)(2 * k)), "l"(db + (uint64_t)(2 * k)), "r"(kPwIdesc), "r"(acc)
+              : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                         smem_u32(&sm.empty[s]))
+                     : "memory");
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                       smem_u32(&sm.accum))
+                   : "memory");
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: thread = token row ----------------
+    const int64_t row = m0 + 32 * warp + lane;
+    const bool live = row < wp.num_tokens;
+    const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
+    pw_fence_after();
+    int64_t pos = 0;
+    bool pos_ok = live;
+    if (live && wp.rot_dim > 0) {
+      pos = __ldg(wp.positions + row);
+      pos_ok = pos >= 0 && pos < wp.max_position;
+      if (!pos_ok) pos = 0;
+    }
+    int64_t block = 0, offset = 0;
+    const bool slot_ok = ready && pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
+    uint8_t* rec = wp.data[0] + ((int64_t)(int32_t)block * wp.rec_block32 +
+                                 (int32_t)((int32_t)offset * wp.rec_token32 + head * wp.rec_head32));
+    uint8_t* drow = rec + (r == 0 ? 0 : wp.off_vd);
+    uint8_t* srow = rec + (r == 0 ? wp.off_ks : wp.off_vs);
+    const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
+    const float gs = wp.global_scale[r];
+
+    // encode one finished 16-element group (bf16 pairs) and store its 8 code bytes and scale byte
+    auto put_group = [&](int g, const uint32_t (&x)[8]) {
+      bool exact;
+      const uint32_t amax = group_amax_bits<16>(x);
+      const float ga = __fmul_rn(gs, __uint_as_float(amax));
+      uint32_t sb = cvt_e4m3(div6_fast(ga, exact));
+      const bool slow = __any_sync(0xffffffffu, !wp.plain || !exact);
+      uint32_t packed[2];
+      if (slow) {
+        sb = cvt_e4m3(__fdiv_rn(ga, 6.0f));
+        encode_row<16, true>(x, sm.lut[r][sb], wp.zero, packed);
+      } else {
+        encode_row<16, false>(x, sm.lut[r][sb], wp.zero, packed);
+      }
+      if (slot_ok) {
+        *reinterpret_cast<uint2*>(drow + 8 * g) = make_uint2(packed[0], packed[1]);
+        srow[g] = (uint8_t)sb;
+      }
+    };
+    auto put_bf16 = [&](__nv_bfloat16* out, int g, const uint32_t (&x)[8]) {
+      uint4* o = reinterpret_cast<uint4*>(out + 16 * g);
+      o[0] = make_uint4(x[0], x[1], x[2], x[3]);
+      o[1] = make_uint4(x[4], x[5], x[6], x[7]);
+    };
+
+    if (r == 1) {
+      __nv_bfloat16* vo = (p.value_out && live && ready)
+                              ? p.value_out + row * p.value_out_stride_token + head * p.value_out_stride_head
+                              : nullptr;
+#pragma unroll 1
+      for (int g = 0; g < 16; ++g) {
+        uint32_t x[8];
+        pw_load_bf16(taddr + 16 * g, x);
+        if (vo) put_bf16(vo, g, x);
+        put_group(g, x);
+      }
+    } else {
+      __nv_bfloat16* ko = (wp.key_out && pos_ok && ready)
+                              ? wp.key_out + row * wp.key_out_stride_token + head * wp.key_out_stride_head
+                              : nullptr;
+      const bool norm = wp.norm_weight != nullptr;
+      float rr = 1.0f;
+      if (norm) {
+        // the writer's order: partial l = (even squares of [8l, 8l+8)) + (odd squares), then pairwise at
+        // distances 16, 8, 4, 2, 1
+        float part[32];
+#pragma unroll
+        for (int g = 0; g < 16; ++g) {
+          uint32_t x[8];
+          pw_load_bf16(taddr + 16 * g, x);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float2 a = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = make_float2(bf_lo(x[4 * h + i]), bf_hi(x[4 * h + i]));
+              a = __ffma2_rn(f, f, a);
+            }
+            part[2 * g + h] = __fadd_rn(a.x, a.y);
+          }
+        }
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+          for (int l = 0; l < m; ++l) part[l] = __fadd_rn(part[l], part[l + m]);
+        rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(part[0], wp.inv_head_dim), wp.norm_eps)));
+      }
+      const float2 rr2 = make_float2(rr, rr);
+      // group g read back, rounded, normed: y = bf16((x * r) * (w + offset))
+      auto load_normed = [&](int g, uint32_t (&x)[8]) {
+        pw_load_bf16(taddr + 16 * g, x);
+        if (norm) {
+          const float4* wv = reinterpret_cast<const float4*>(wp.norm_weight + 16 * g);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 w4 = __ldg(wv + q);
+            const float2 wa = make_float2(__fadd_rn(w4.x, wp.norm_offset), __fadd_rn(w4.y, wp.norm_offset));
+            const float2 wb = make_float2(__fadd_rn(w4.z, wp.norm_offset), __fadd_rn(w4.w, wp.norm_offset));
+            const float2 ya = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(x[2 * q]), bf_hi(x[2 * q])), rr2), wa);
+            const float2 yb =
+                __fmul2_rn(__fmul2_rn(make_float2(bf_lo(x[2 * q + 1]), bf_hi(x[2 * q + 1])), rr2), wb);
+            x[2 * q] = pack_bf16x2(ya.x, ya.y);
+            x[2 * q + 1] = pack_bf16x2(yb.x, yb.y);
+          }
+        }
+      };
+      auto finish = [&](int g, const uint32_t (&x)[8]) {
+        if (ko) put_bf16(ko, g, x);
+        put_group(g, x);
+      };
+      const int rot_groups = wp.rot_dim >> 4;  // groups of 16 inside the rotated dims
+      const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
+      const int half = wp.rot_dim >> 1;
+      if (wp.rot_dim > 0 && wp.neox) {
+        // group ga of the first half pairs with group ga + half/16 (half is a multiple of 16)
+#pragma unroll 1
+        for (int ga = 0; ga < (half >> 4); ++ga) {
+          uint32_t x1[8], x2[8], cw[8], sw[8];
+          load_normed(ga, x1);
+          load_normed(ga + (half >> 4), x2);
+          load_bf16_run<16>(cs + 16 * ga, cw);
+          load_bf16_run<16>(cs + half + 16 * ga, sw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t a = x1[i], b = x2[i];
+            x1[i] = bf16x2_add(bf16x2_mul(a, cw[i]), bf16x2_mul(b, sw[i]) ^ 0x80008000u);
+            x2[i] = bf16x2_add(bf16x2_mul(b, cw[i]), bf16x2_mul(a, sw[i]));
+          }
+          finish(ga, x1);
+          finish(ga + (half >> 4), x2);
+        }
+      } else if (wp.rot_dim > 0) {
+        // GPT-J: word i of group g = elements (16g + 2i, 16g + 2i + 1), cos/sin index 8g + i
+#pragma unroll 1
+        for (int g = 0; g < rot_groups; ++g) {
+          uint32_t x[8], cw[4], sw[4];
+          load_normed(g, x);
+          load_bf16_run<8>(cs + 8 * g, cw);
+          load_bf16_run<8>(cs + half + 8 * g, sw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t sel = (i & 1) ? 0x3232u : 0x1010u;
+            const uint32_t cc = __byte_perm(cw[i >> 1], 0u, sel), ss = __byte_perm(sw[i >> 1], 0u, sel);
+            x[i] = bf16x2_add(bf16x2_mul(x[i], cc), bf16x2_mul(__byte_perm(x[i], 0u, 0x1032u), ss) ^ 0x00008000u);
+          }
+          finish(g, x);
+        }
+      }
+#pragma unroll 1
+      for (int g = (wp.rot_dim > 0 ? rot_groups : 0); g < 16; ++g) {  // dims past the rotation pass through
+        uint32_t x[8];
+        load_normed(g, x);
+        finish(g, x);
+      }
+    }
+  }
+
+  pw_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    pw_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kPwBN));
+  }
+}

@@ -2063,11 +2063,17 @@ int run_attention(const void* query, int64_t q_stride_row, int64_t q_stride_head
 
 using namespace nvqsa;
 
+namespace nvqsa {
+int write_error_flags(unsigned int* v, bool clear);  // write_cache.cu: the projection writer's flags
+}
+
 extern "C" int nvqsa_read_error_flags(uint32_t* flags, int clear) {
   if (!flags) return NVQSA_ERR_NULL_POINTER;
-  unsigned int v = 0;
+  unsigned int v = 0, wv = 0;
   if (cudaMemcpyFromSymbol(&v, g_error_flags, sizeof(v)) != cudaSuccess) return NVQSA_ERR_CUDA;
-  *flags = v;
+  const int ws = nvqsa::write_error_flags(&wv, clear != 0);
+  if (ws != NVQSA_OK) return ws;
+  *flags = v | wv;
   if (clear && v) {
     const unsigned int zero = 0;
     if (cudaMemcpyToSymbol(g_error_flags, &zero, sizeof(zero)) != cudaSuccess) return NVQSA_ERR_CUDA;

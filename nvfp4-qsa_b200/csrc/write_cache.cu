@@ -19,6 +19,8 @@
 // The reference Triton kernel (kernels.py:94-96) instead substitutes 1e30 for
 // a zero scale, so it writes code 0 where the oracle saturates to +-6 for
 // groups whose scale rounds to zero; this kernel follows the oracle.
+#include <cuda.h>
+
 #include <cmath>
 #include <type_traits>
 
@@ -753,7 +755,20 @@ cudaError_t launch_write_any(const WriteParams& p, int head_dim, cudaStream_t s)
   }
 }
 
+#include "kv_proj_write.cuh"
+
 }  // namespace
+
+// Error flags of this file's kernels (bit 2: a projection-writer wait ran out), for nvqsa_read_error_flags.
+int write_error_flags(unsigned int* v, bool clear) {
+  if (cudaMemcpyFromSymbol(v, g_write_error_flags, sizeof(*v)) != cudaSuccess) return NVQSA_ERR_CUDA;
+  if (clear && *v) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_write_error_flags, &zero, sizeof(zero)) != cudaSuccess) return NVQSA_ERR_CUDA;
+  }
+  return NVQSA_OK;
+}
+
 }  // namespace nvqsa
 
 using namespace nvqsa;
@@ -961,4 +976,131 @@ extern "C" int nvqsa_norm_rope_write_cache(
     return NVQSA_ERR_MISALIGNED;
   const cudaError_t err = launch_write_any<true>(p, head_dim, as_stream(stream));
   return err == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
+}
+
+// ---------------- K/V projection fused with the writer ----------------
+namespace {
+
+using PwEncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// bf16 matrix [rows, cols] with a row stride in elements, read in boxes of 64 columns x box_rows rows
+// swizzled in 128-byte rows; rows and columns past the end read as zero.
+bool pw_encode(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, int64_t row_stride,
+               uint32_t box_rows) {
+  static std::atomic<PwEncodeTiledFn> encode{nullptr};
+  PwEncodeTiledFn fn = encode.load(std::memory_order_acquire);
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !f)
+      return false;
+    fn = reinterpret_cast<PwEncodeTiledFn>(f);
+    encode.store(fn, std::memory_order_release);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kPwBK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kPwMaxDevices = 64;
+std::atomic<int> g_pw_smem_set[kPwMaxDevices];
+
+}  // namespace
+
+extern "C" int nvqsa_kv_proj_write_cache(
+    const void* hidden, int64_t hidden_stride_token, int64_t num_tokens, int32_t hidden_size,
+    const void* key_weight, const void* value_weight, int64_t weight_stride_row,
+    void* key_data, int64_t kd_stride_block, int64_t kd_stride_token, int64_t kd_stride_head,
+    void* key_scale, int64_t ks_stride_block, int64_t ks_stride_token, int64_t ks_stride_head,
+    void* value_data, int64_t vd_stride_block, int64_t vd_stride_token, int64_t vd_stride_head,
+    void* value_scale, int64_t vs_stride_block, int64_t vs_stride_token, int64_t vs_stride_head,
+    const int64_t* slot_mapping, int32_t kv_heads, int32_t head_dim,
+    int64_t num_blocks, int64_t page_size, float key_global_scale, float value_global_scale,
+    const float* norm_weight, float norm_weight_offset, float eps,
+    const int64_t* positions, const void* cos_sin_cache, int64_t cos_sin_stride, int64_t max_position,
+    int32_t rotary_dim, int32_t is_neox_style,
+    void* key_out, int64_t key_out_stride_token, int64_t key_out_stride_head,
+    void* value_out, int64_t value_out_stride_token, int64_t value_out_stride_head, void* stream) {
+  if (head_dim != kPwBN) return NVQSA_ERR_HEAD_DIM;
+  if (num_tokens < 0 || kv_heads < 1 || hidden_size < 1 || num_blocks < 0 || page_size < 1)
+    return NVQSA_ERR_BAD_SHAPE;
+  if (hidden_stride_token < hidden_size || weight_stride_row < hidden_size) return NVQSA_ERR_BAD_SHAPE;
+  if ((num_tokens + kPwBM - 1) / kPwBM > 65535 || kv_heads > 32767) return NVQSA_ERR_BAD_SHAPE;
+  const bool neox = is_neox_style != 0;
+  if (rotary_dim < 0 || rotary_dim > head_dim || rotary_dim % (neox ? 32 : 16) != 0) return NVQSA_ERR_BAD_SHAPE;
+  if (rotary_dim > 0) {
+    if (!positions || !cos_sin_cache) return NVQSA_ERR_NULL_POINTER;
+    if (max_position < 1 || cos_sin_stride < rotary_dim) return NVQSA_ERR_BAD_SHAPE;
+    if (!aligned_to(cos_sin_cache, 16) || (cos_sin_stride * 2) % 16 != 0) return NVQSA_ERR_MISALIGNED;
+  }
+  if (!(eps >= 0.0f) || !std::isfinite(eps) || !std::isfinite(norm_weight_offset)) return NVQSA_ERR_BAD_SHAPE;
+  if (norm_weight && !aligned_to(norm_weight, 16)) return NVQSA_ERR_MISALIGNED;
+  if (!hidden || !key_weight || !value_weight) return NVQSA_ERR_NULL_POINTER;
+  if (!aligned_to(hidden, 16) || !aligned_to(key_weight, 16) || !aligned_to(value_weight, 16) ||
+      (hidden_stride_token * 2) % 16 != 0 || (weight_stride_row * 2) % 16 != 0)
+    return NVQSA_ERR_MISALIGNED;
+  auto out_ok = [](const void* o, int64_t st, int64_t sh) {
+    return !o || (aligned_to(o, 16) && (st * 2) % 16 == 0 && (sh * 2) % 16 == 0);
+  };
+  if (!out_ok(key_out, key_out_stride_token, key_out_stride_head) ||
+      !out_ok(value_out, value_out_stride_token, value_out_stride_head))
+    return NVQSA_ERR_MISALIGNED;
+
+  WriteParams w;
+  bool go = false;
+  const int st = prepare_write(w, go, hidden, 0, 0, hidden, 0, 0, key_data, kd_stride_block, kd_stride_token,
+                               kd_stride_head, key_scale, ks_stride_block, ks_stride_token, ks_stride_head, value_data,
+                               vd_stride_block, vd_stride_token, vd_stride_head, value_scale, vs_stride_block,
+                               vs_stride_token, vs_stride_head, slot_mapping, num_tokens, kv_heads, head_dim,
+                               num_blocks, page_size, key_global_scale, value_global_scale);
+  if (st != NVQSA_OK || !go) return st;
+  // the epilogue addresses a token's four regions from one record base and stores 8-byte code runs
+  if (!w.record || !aligned_to(w.data[0], 8) || w.off_ks % 8 != 0 || w.off_vd % 8 != 0 || w.rec_block32 % 8 != 0 ||
+      w.rec_token32 % 8 != 0 || w.rec_head32 % 8 != 0)
+    return NVQSA_ERR_MISALIGNED;
+  w.norm_weight = norm_weight;
+  w.norm_offset = norm_weight_offset;
+  w.norm_eps = eps;
+  w.inv_head_dim = 1.0f / (float)head_dim;
+  w.rot_dim = rotary_dim;
+  w.neox = neox ? 1 : 0;
+  w.positions = positions;
+  w.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin_cache);
+  w.cos_sin_stride = cos_sin_stride;
+  w.max_position = max_position;
+  w.key_out = static_cast<__nv_bfloat16*>(key_out);
+  w.key_out_stride_token = key_out_stride_token;
+  w.key_out_stride_head = key_out_stride_head;
+
+  ProjParams pp;
+  pp.w = w;
+  pp.kblocks = (hidden_size + kPwBK - 1) / kPwBK;
+  pp.value_out = static_cast<__nv_bfloat16*>(value_out);
+  pp.value_out_stride_token = value_out_stride_token;
+  pp.value_out_stride_head = value_out_stride_head;
+  const int64_t wrows = (int64_t)kv_heads * head_dim;
+  if (!pw_encode(&pp.map_x, hidden, hidden_size, num_tokens, hidden_stride_token, kPwBM) ||
+      !pw_encode(&pp.map_w[0], key_weight, hidden_size, wrows, weight_stride_row, kPwBN) ||
+      !pw_encode(&pp.map_w[1], value_weight, hidden_size, wrows, weight_stride_row, kPwBN))
+    return NVQSA_ERR_CUDA;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kPwMaxDevices) return NVQSA_ERR_CUDA;
+  const size_t smem = sizeof(SmemPw) + 1024;
+  if (!g_pw_smem_set[dev].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(kv_proj_write_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return NVQSA_ERR_CUDA;
+    g_pw_smem_set[dev].store(1, std::memory_order_release);
+  }
+  const dim3 grid((unsigned)(2 * kv_heads), (unsigned)((num_tokens + kPwBM - 1) / kPwBM));
+  kv_proj_write_kernel<<<grid, kPwThreads, smem, as_stream(stream)>>>(pp);
+  return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }

@@ -60,6 +60,20 @@ _SIGNATURES = {
         _P, _P, _I64, _I64,
         _I32, _I32,
         _P, _I64, _I64, _P]),
+    "nvqsa_kv_proj_write_cache": (c_int, [
+        _P, _I64, _I64, _I32,
+        _P, _P, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I64, _I64, _I64,
+        _P, _I32, _I32,
+        _I64, _I64, _F, _F,
+        _P, _F, _F,
+        _P, _P, _I64, _I64,
+        _I32, _I32,
+        _P, _I64, _I64,
+        _P, _I64, _I64, _P]),
     "nvqsa_sparse_attention_workspace_size": (c_int, [_I64, _I32, _I32, _I32, _I64, POINTER(c_size_t)]),
     "nvqsa_sparse_attention": (c_int, [
         _P, _I64, _I64,

@@ -26,6 +26,7 @@ __all__ = [
     "qsa_sparse_paged_attention_nvfp4",
     "qsa_write_cache_nvfp4",
     "qsa_norm_rope_write_cache_nvfp4",
+    "qsa_kv_proj_write_cache_nvfp4",
     "qsa_sparse_paged_attention_nvfp4_partial",
     "qsa_sparse_paged_attention_fp8",
     "qsa_sparse_paged_attention",
@@ -231,6 +232,141 @@ def qsa_norm_rope_write_cache_nvfp4(
             ko_dst.copy_(key_out)
         return ko_dst
     return key_out
+
+
+def _aligned16(t):
+    """t itself when its base and row strides are 16-byte aligned, else a copy with fresh storage."""
+    if t.data_ptr() % 16 == 0 and all((st * t.element_size()) % 16 == 0 for st in t.stride()[:-1]):
+        return t
+    return t.clone() if t.is_contiguous() else t.contiguous()
+
+
+def qsa_kv_proj_write_cache_nvfp4(
+    hidden,
+    key_weight,
+    value_weight,
+    key_data,
+    key_scale,
+    value_data,
+    value_scale,
+    slot_mapping,
+    key_global_scale,
+    value_global_scale,
+    positions=None,
+    cos_sin_cache=None,
+    k_norm_weight=None,
+    eps=1e-6,
+    is_neox_style=True,
+    norm_weight_offset=1.0,
+    key_out=None,
+    value_out=None,
+):
+    """K/V projection + k-norm + RoPE + NVFP4 quantize + scatter in one launch.
+
+    The reference's layer (integration/snapshot/qsa.py:658-667 -> :618-640)
+    computes ``qkv = hidden @ W_qkv^T`` in bf16, then k_norm and the rotary
+    embedding on K, then ``qsa_write_cache_nvfp4``.  This computes the K and V
+    columns of that projection on the tensor cores and encodes them straight
+    from the accumulators.  ``hidden`` is bf16 ``[tokens, hidden_size]``;
+    ``key_weight`` / ``value_weight`` are the bf16 ``[kv_heads * 256,
+    hidden_size]`` K and V row blocks of the QKV weight (views are fine).  The
+    other arguments mean what they mean for ``qsa_norm_rope_write_cache_nvfp4``;
+    ``key_out`` receives the rotated K and ``value_out`` the V projection (bf16
+    ``[tokens, kv_heads, 256]``, 16-byte aligned rows).  Each K and V value is
+    the fp32 tensor-core sum rounded to bf16, which can differ by one bf16 ulp
+    from another GEMM's; the cache bytes are those of the fused writer on
+    exactly these K and V.  Returns ``(key_out, value_out)``.
+    """
+    if hidden.dim() != 2 or key_weight.dim() != 2 or value_weight.dim() != 2:
+        raise ValueError("hidden must be [tokens, hidden_size] and the weights [kv_heads * 256, hidden_size]")
+    for t in (hidden, key_weight, value_weight):
+        if t.dtype != torch.bfloat16:
+            raise TypeError("the K/V projection takes bf16 hidden states and weights")
+        if t.stride(-1) != 1:
+            raise ValueError("hidden states and weights need a contiguous last dimension")
+    num_tokens, hidden_size = hidden.shape
+    if key_weight.shape != value_weight.shape or key_weight.shape[1] != hidden_size:
+        raise ValueError("key_weight and value_weight must both be [kv_heads * 256, hidden_size]")
+    head_dim = 256
+    if key_weight.shape[0] % head_dim:
+        raise ValueError("the fused K/V projection supports head_dim 256")
+    kv_heads = key_weight.shape[0] // head_dim
+    for data, scale in ((key_data, key_scale), (value_data, value_scale)):  # the writer's checks (kernels.py:118-129)
+        if data.dtype != torch.uint8 or scale.dtype != torch.uint8:
+            raise TypeError("NVFP4 QSA data and scale caches must use uint8 storage")
+        if data.dim() != 4 or scale.dim() != 4:
+            raise ValueError("NVFP4 QSA cache regions must be [blocks, page, kv_heads, bytes]")
+        if data.shape[-1] != head_dim // 2:
+            raise ValueError("invalid NVFP4 QSA packed-data shape")
+        if scale.shape[-1] != head_dim // 16:
+            raise ValueError("invalid NVFP4 QSA group-scale shape")
+        if data.stride(-1) != 1 or scale.stride(-1) != 1:
+            raise ValueError("NVFP4 QSA tensors need a contiguous last dimension")
+    if slot_mapping.dtype != torch.int64:
+        raise TypeError("NVFP4 QSA slot_mapping must be int64")
+    if slot_mapping.dim() != 1 or slot_mapping.shape[0] != num_tokens or slot_mapping.stride(0) != 1:
+        raise ValueError("NVFP4 QSA slot_mapping must be a contiguous [tokens] vector")
+    if key_data.shape[:3] != value_data.shape[:3] or key_data.shape[2] != kv_heads:
+        raise ValueError("NVFP4 QSA K and V caches must share [blocks, page, kv_heads] with the weights' kv_heads")
+    hidden = _aligned16(hidden)
+    key_weight, value_weight = _aligned16(key_weight), _aligned16(value_weight)
+    if key_weight.stride(0) != value_weight.stride(0):
+        key_weight, value_weight = key_weight.contiguous(), value_weight.contiguous()
+    device = hidden.device
+    rotary_dim, max_position, cs_ptr, cs_stride, pos_ptr = 0, 0, 0, 0, 0
+    if cos_sin_cache is not None:
+        if positions is None:
+            raise ValueError("a rotary embedding needs positions")
+        if cos_sin_cache.dim() != 2 or cos_sin_cache.shape[1] % 2:
+            raise ValueError("cos_sin_cache must be [max_position, rotary_dim]")
+        if positions.dtype != torch.int64 or positions.dim() != 1 or positions.shape[0] != num_tokens:
+            raise ValueError("positions must be an int64 [tokens] vector")
+        cos_sin_cache = _aligned16(cos_sin_cache.to(torch.bfloat16))
+        if cos_sin_cache.stride(-1) != 1:
+            cos_sin_cache = cos_sin_cache.contiguous()
+        positions = positions.contiguous()
+        rotary_dim, max_position = cos_sin_cache.shape[1], cos_sin_cache.shape[0]
+        cs_ptr, cs_stride, pos_ptr = cos_sin_cache.data_ptr(), cos_sin_cache.stride(0), positions.data_ptr()
+        if rotary_dim > head_dim or rotary_dim % (32 if is_neox_style else 16):
+            raise ValueError(f"rotary_dim {rotary_dim} must be a multiple of {32 if is_neox_style else 16} "
+                             "and at most 256 for the fused K/V projection")
+    w_ptr = 0
+    if k_norm_weight is not None:
+        if k_norm_weight.numel() != head_dim:
+            raise ValueError("k_norm_weight must have head_dim elements")
+        k_norm_weight = _aligned16(k_norm_weight.reshape(head_dim).to(torch.float32).contiguous())
+        w_ptr = k_norm_weight.data_ptr()
+    outs = []
+    for o, name in ((key_out, "key_out"), (value_out, "value_out")):
+        if o is None:
+            outs.append((0, 0, 0))
+            continue
+        if o.shape != (num_tokens, kv_heads, head_dim) or o.dtype != torch.bfloat16 or o.stride(-1) != 1:
+            raise ValueError(f"{name} must be bf16 [tokens, kv_heads, 256] with a contiguous last dimension")
+        if o.data_ptr() % 16 or (o.stride(0) * 2) % 16 or (o.stride(1) * 2) % 16:
+            raise ValueError(f"{name} needs 16-byte aligned rows")
+        outs.append((o.data_ptr(), o.stride(0), o.stride(1)))
+    extra = [t for t in (positions, cos_sin_cache, k_norm_weight, key_out, value_out) if t is not None]
+    _check_same_device((key_weight, value_weight, key_data, key_scale, value_data, value_scale, slot_mapping,
+                        *extra), device)
+    if num_tokens == 0:
+        return key_out, value_out
+    lib = _native.load()
+    with _device_ctx(device):
+        status = lib.nvqsa_kv_proj_write_cache(
+            hidden.data_ptr(), hidden.stride(0), num_tokens, hidden_size,
+            key_weight.data_ptr(), value_weight.data_ptr(), key_weight.stride(0),
+            key_data.data_ptr(), key_data.stride(0), key_data.stride(1), key_data.stride(2),
+            key_scale.data_ptr(), key_scale.stride(0), key_scale.stride(1), key_scale.stride(2),
+            value_data.data_ptr(), value_data.stride(0), value_data.stride(1), value_data.stride(2),
+            value_scale.data_ptr(), value_scale.stride(0), value_scale.stride(1), value_scale.stride(2),
+            slot_mapping.data_ptr(), kv_heads, head_dim,
+            key_data.shape[0], key_data.shape[1], float(key_global_scale), float(value_global_scale),
+            w_ptr, float(norm_weight_offset), float(eps),
+            pos_ptr, cs_ptr, cs_stride, max_position, rotary_dim, 1 if is_neox_style else 0,
+            *outs[0], *outs[1], _stream_ptr(device))
+    _native.check(status, "qsa_kv_proj_write_cache_nvfp4")
+    return key_out, value_out
 
 
 @lru_cache(maxsize=256)
