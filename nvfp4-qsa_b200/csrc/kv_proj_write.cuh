@@ -10,34 +10,44 @@
 // columns of that GEMM are computed and encoded in one launch, so the bf16 K
 // and V never reach HBM unless key_out / value_out ask for them.
 //
-// One CTA = 128 tokens x one head (256 columns) of K or of V.  Warp 4 streams
-// 64-wide k-slices of the hidden rows (16 KB) and of the head's weight rows
-// (32 KB) through a 4-stage ring with TMA (128-byte swizzle); one thread of
-// warp 5 issues the tcgen05.mma (M 128, N 256, K 16, bf16 -> fp32) into a
-// 128 x 256 fp32 accumulator in tensor memory and releases each stage with
-// tcgen05.commit.  Warps 0-3 (one per tensor-memory lane quarter: thread =
-// token row) then read the row back, round it to bf16 as the GEMM output
+// One CTA = 128 MH tokens (MH = 1 or 2) x one head (256 columns) of K or of
+// V.  The TMA warp streams 64-wide k-slices of the hidden rows (16 KB per 128
+// tokens) and of the head's weight rows (32 KB) through a ring of stages with
+// TMA (128-byte swizzle); one thread of the MMA warp issues, per 16-wide
+// k-step and per 128-token half, a tcgen05.mma (M 128, N 256, K 16, bf16 ->
+// fp32) into that half's 128 x 256 fp32 accumulator in tensor memory, and
+// releases each stage with tcgen05.commit.  The 4 MH epilogue warps (warp w:
+// lane quarter w % 4 of half w / 4, thread = token row) then read the row
+// back, round it to bf16 as the GEMM output
 // would be, and run the writer's arithmetic on whole 16-element groups: for
 // K the RMS norm (the writer's summation order, emulated in one thread),
 // the rotation (bf16 arithmetic, NeoX halves or GPT-J pairs), then the
 // group scale and E2M1 codes; for V the codes alone.
-constexpr int kPwBM = 128;        // tokens per CTA (tensor-memory lanes)
 constexpr int kPwBN = 256;        // columns per CTA: one head
 constexpr int kPwBK = 64;         // k-slice per stage: 128 bytes of bf16 (one swizzle atom row)
-constexpr int kPwStages = 4;
-constexpr int kPwThreads = 192;   // warps 0-3 epilogue, warp 4 TMA, warp 5 MMA
-constexpr uint32_t kPwStageA = kPwBM * kPwBK * 2;  // 16 KB
 constexpr uint32_t kPwStageB = kPwBN * kPwBK * 2;  // 32 KB
+// MH halves of 128 tokens per CTA, each its own M = 128 accumulator (256 tensor-memory columns) fed by the
+// same weight tile: MH = 2 halves the weight traffic per token; 4 MH epilogue warps, then the TMA and MMA warps.
+template <int MH>
+struct PwShape {
+  static constexpr int kBM = 128 * MH;
+  static constexpr int kStages = MH == 1 ? 4 : 3;
+  static constexpr int kThreads = 32 * (4 * MH + 2);
+  static constexpr int kTmaWarp = 4 * MH, kMmaWarp = 4 * MH + 1;
+  static constexpr uint32_t kStageA = (uint32_t)kBM * kPwBK * 2;
+  static constexpr uint32_t kTmemCols = 256u * MH;
+};
 constexpr uint32_t kPwSpinLimit = 1u << 24;        // bounded mbarrier waits (the mainloop is tens of us)
 constexpr unsigned int kErrProjWait = 4u;          // bit 2 of the error flags: a projection-writer wait ran out
 
 __device__ unsigned int g_write_error_flags;
 
+template <int MH>
 struct __align__(1024) SmemPw {
-  uint8_t a[kPwStages][kPwStageA];  // hidden rows, swizzled 128-byte rows (1024-byte aligned atoms)
-  uint8_t b[kPwStages][kPwStageB];  // weight rows
-  unsigned long long full[kPwStages];
-  unsigned long long empty[kPwStages];
+  uint8_t a[PwShape<MH>::kStages][PwShape<MH>::kStageA];  // hidden rows, swizzled 128-byte rows (1024-byte atoms)
+  uint8_t b[PwShape<MH>::kStages][kPwStageB];             // weight rows
+  unsigned long long full[PwShape<MH>::kStages];
+  unsigned long long empty[PwShape<MH>::kStages];
   unsigned long long accum;
   uint32_t tmem;
   float lut[2][256];
@@ -45,7 +55,7 @@ struct __align__(1024) SmemPw {
 };
 
 struct ProjParams {
-  CUtensorMap map_x;      // hidden [tokens, hidden] bf16, box 64 x 128
+  CUtensorMap map_x;      // hidden [tokens, hidden] bf16, box 64 x (128 MH)
   CUtensorMap map_w[2];   // K / V weight rows [kv_heads * 256, hidden] bf16, box 64 x 256
   WriteParams w;          // cache regions, slots, scales, norm and rotation (head_dim 256, record layout)
   int32_t kblocks;        // hidden / 64, rounded up (the tail is zero-filled by TMA)
@@ -87,7 +97,7 @@ __device__ __forceinline__ uint64_t pw_desc(uint32_t addr) {
 }
 // Instruction descriptor: D f32, A and B bf16, both K-major, N = 256, M = 128.
 constexpr uint32_t kPwIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPwBN >> 3) << 17) |
-                              ((uint32_t)(kPwBM >> 4) << 24);
+                              ((uint32_t)(128 >> 4) << 24);
 
 __device__ __forceinline__ void pw_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void pw_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
@@ -105,29 +115,33 @@ __device__ __forceinline__ void pw_load_bf16(uint32_t taddr, uint32_t (&w)[8]) {
   for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
 }
 
-__global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __grid_constant__ ProjParams p) {
+template <int MH>
+__global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel(const __grid_constant__ ProjParams p) {
+  using S = PwShape<MH>;
+  constexpr int kStages = S::kStages;
   extern __shared__ __align__(1024) uint8_t pw_smem_raw[];
-  SmemPw& sm = *reinterpret_cast<SmemPw*>(pw_smem_raw + ((1024u - (smem_u32(pw_smem_raw) & 1023u)) & 1023u));
+  SmemPw<MH>& sm =
+      *reinterpret_cast<SmemPw<MH>*>(pw_smem_raw + ((1024u - (smem_u32(pw_smem_raw) & 1023u)) & 1023u));
   const WriteParams& wp = p.w;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = wp.kv_heads;
   const int nt = blockIdx.x;  // 0 .. kvh-1: K head nt; kvh .. 2 kvh-1: V head nt - kvh
   const int r = nt < kvh ? 0 : 1;
   const int head = nt - r * kvh;
-  const int64_t m0 = (int64_t)blockIdx.y * kPwBM;
+  const int64_t m0 = (int64_t)blockIdx.y * S::kBM;
 
   if (tid == 0) {
 #pragma unroll
-    for (int s = 0; s < kPwStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       pw_mbar_init(smem_u32(&sm.full[s]), 1);
       pw_mbar_init(smem_u32(&sm.empty[s]), 1);
     }
     pw_mbar_init(smem_u32(&sm.accum), 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 5) {
+  if (warp == S::kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&sm.tmem)),
-                 "r"(kPwBN));
+                 "r"(S::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
   build_out_scale_lut(wp, sm.lut, sm.quot);
@@ -137,42 +151,47 @@ __global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __gr
   const uint32_t tmem = sm.tmem;
   const int kb = p.kblocks;
 
-  if (warp == 4) {
+  if (warp == S::kTmaWarp) {
     // ---------------- producer: TMA into the stage ring ----------------
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < kb; ++i) {
-        const int s = i % kPwStages;
-        if (i >= kPwStages && !pw_wait(smem_u32(&sm.empty[s]), (uint32_t)(((i / kPwStages) & 1) ^ 1))) break;
+        const int s = i % kStages;
+        if (i >= kStages && !pw_wait(smem_u32(&sm.empty[s]), (uint32_t)(((i / kStages) & 1) ^ 1))) break;
         const uint32_t full = smem_u32(&sm.full[s]);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(full),
-                     "r"(kPwStageA + kPwStageB)
+                     "r"(S::kStageA + kPwStageB)
                      : "memory");
         pw_tma_2d(smem_u32(sm.a[s]), &p.map_x, i * kPwBK, (int32_t)m0, full);
         pw_tma_2d(smem_u32(sm.b[s]), &p.map_w[r], i * kPwBK, head * kPwBN, full);
         issued = i + 1;
       }
       // copies still in flight land before the CTA can leave (only a timed-out consumer leaves them)
-      for (int j = issued > kPwStages ? issued - kPwStages : 0; j < issued; ++j)
-        pw_wait(smem_u32(&sm.full[j % kPwStages]), (uint32_t)((j / kPwStages) & 1));
+      for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+        pw_wait(smem_u32(&sm.full[j % kStages]), (uint32_t)((j / kStages) & 1));
     }
-  } else if (warp == 5) {
+  } else if (warp == S::kMmaWarp) {
     // ---------------- MMA issue: one thread ----------------
     if (lane == 0) {
       for (int i = 0; i < kb; ++i) {
-        const int s = i % kPwStages;
-        if (!pw_wait(smem_u32(&sm.full[s]), (uint32_t)((i / kPwStages) & 1))) break;
+        const int s = i % kStages;
+        if (!pw_wait(smem_u32(&sm.full[s]), (uint32_t)((i / kStages) & 1))) break;
         pw_fence_after();
-        const uint64_t da = pw_desc(smem_u32(sm.a[s])), db = pw_desc(smem_u32(sm.b[s]));
+        const uint64_t db = pw_desc(smem_u32(sm.b[s]));
 #pragma unroll
         for (int k = 0; k < kPwBK / 16; ++k) {
           const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          // advancing the start address by 32 bytes steps 16 elements along K inside the swizzled row
-          asm volatile(
-              "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
-              "l"(da + (uint64_t)(2 * k)), "l"(db + (uint64_t)(2 * k)), "r"(kPwIdesc), "r"(acc)
-              : "memory");
+#pragma unroll
+          for (int h = 0; h < MH; ++h) {
+            // half h: A rows [128 h, 128 h + 128) (16 KB further), accumulator columns [256 h, 256 h + 256);
+            // advancing the start address by 32 bytes steps 16 elements along K inside the swizzled row
+            const uint64_t da = pw_desc(smem_u32(sm.a[s]) + 16384u * h);
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem + 256u * h),
+                "l"(da + (uint64_t)(2 * k)), "l"(db + (uint64_t)(2 * k)), "r"(kPwIdesc), "r"(acc)
+                : "memory");
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
                          smem_u32(&sm.empty[s]))
@@ -185,7 +204,8 @@ __global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __gr
     __syncwarp();
   } else {
     // ---------------- epilogue: thread = token row ----------------
-    const int64_t row = m0 + 32 * warp + lane;
+    const int q = warp & 3, half_m = warp >> 2;  // lane quarter q of accumulator half_m
+    const int64_t row = m0 + 128 * half_m + 32 * q + lane;
     const bool live = row < wp.num_tokens;
     const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
     pw_fence_after();
@@ -202,7 +222,7 @@ __global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __gr
                                  (int32_t)((int32_t)offset * wp.rec_token32 + head * wp.rec_head32));
     uint8_t* drow = rec + (r == 0 ? 0 : wp.off_vd);
     uint8_t* srow = rec + (r == 0 ? wp.off_ks : wp.off_vs);
-    const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t taddr = tmem + 256u * half_m + ((uint32_t)(32 * q) << 16);
     const float gs = wp.global_scale[r];
 
     // encode one finished 16-element group (bf16 pairs) and store its 8 code bytes and scale byte
@@ -344,9 +364,9 @@ __global__ void __launch_bounds__(kPwThreads, 1) kv_proj_write_kernel(const __gr
 
   pw_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == S::kMmaWarp) {
     __syncwarp();
     pw_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kPwBN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(S::kTmemCols));
   }
 }

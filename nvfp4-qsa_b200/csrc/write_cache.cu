@@ -1010,7 +1010,7 @@ bool pw_encode(CUtensorMap* map, const void* base, int64_t cols, int64_t rows, i
 }
 
 constexpr int kPwMaxDevices = 64;
-std::atomic<int> g_pw_smem_set[kPwMaxDevices];
+std::atomic<int> g_pw_smem_set[kPwMaxDevices][2];
 
 }  // namespace
 
@@ -1032,7 +1032,7 @@ extern "C" int nvqsa_kv_proj_write_cache(
   if (num_tokens < 0 || kv_heads < 1 || hidden_size < 1 || num_blocks < 0 || page_size < 1)
     return NVQSA_ERR_BAD_SHAPE;
   if (hidden_stride_token < hidden_size || weight_stride_row < hidden_size) return NVQSA_ERR_BAD_SHAPE;
-  if ((num_tokens + kPwBM - 1) / kPwBM > 65535 || kv_heads > 32767) return NVQSA_ERR_BAD_SHAPE;
+  if ((num_tokens + 127) / 128 > 65535 || kv_heads > 32767) return NVQSA_ERR_BAD_SHAPE;
   const bool neox = is_neox_style != 0;
   if (rotary_dim < 0 || rotary_dim > head_dim || rotary_dim % (neox ? 32 : 16) != 0) return NVQSA_ERR_BAD_SHAPE;
   if (rotary_dim > 0) {
@@ -1086,21 +1086,31 @@ extern "C" int nvqsa_kv_proj_write_cache(
   pp.value_out_stride_token = value_out_stride_token;
   pp.value_out_stride_head = value_out_stride_head;
   const int64_t wrows = (int64_t)kv_heads * head_dim;
-  if (!pw_encode(&pp.map_x, hidden, hidden_size, num_tokens, hidden_stride_token, kPwBM) ||
+  // 256-token CTAs (two accumulators sharing each weight tile) once 128-token CTAs would take more than one
+  // wave: half the weight traffic per token and one epilogue per 256 tokens
+  const int sms = device_sm_count();
+  const int64_t ctas128 = (num_tokens + 127) / 128 * 2 * kv_heads;
+  const int mh = ctas128 > (sms > 0 ? sms : 148) ? 2 : 1;
+  const int bm = 128 * mh;
+  if (!pw_encode(&pp.map_x, hidden, hidden_size, num_tokens, hidden_stride_token, (uint32_t)bm) ||
       !pw_encode(&pp.map_w[0], key_weight, hidden_size, wrows, weight_stride_row, kPwBN) ||
       !pw_encode(&pp.map_w[1], value_weight, hidden_size, wrows, weight_stride_row, kPwBN))
     return NVQSA_ERR_CUDA;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kPwMaxDevices) return NVQSA_ERR_CUDA;
-  const size_t smem = sizeof(SmemPw) + 1024;
-  if (!g_pw_smem_set[dev].load(std::memory_order_acquire)) {
-    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(kv_proj_write_kernel),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  const void* fn = mh == 2 ? reinterpret_cast<const void*>(kv_proj_write_kernel<2>)
+                           : reinterpret_cast<const void*>(kv_proj_write_kernel<1>);
+  const size_t smem = (mh == 2 ? sizeof(SmemPw<2>) : sizeof(SmemPw<1>)) + 1024;
+  if (!g_pw_smem_set[dev][mh - 1].load(std::memory_order_acquire)) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return NVQSA_ERR_CUDA;
-    g_pw_smem_set[dev].store(1, std::memory_order_release);
+    g_pw_smem_set[dev][mh - 1].store(1, std::memory_order_release);
   }
-  const dim3 grid((unsigned)(2 * kv_heads), (unsigned)((num_tokens + kPwBM - 1) / kPwBM));
-  kv_proj_write_kernel<<<grid, kPwThreads, smem, as_stream(stream)>>>(pp);
+  const dim3 grid((unsigned)(2 * kv_heads), (unsigned)((num_tokens + bm - 1) / bm));
+  if (mh == 2)
+    kv_proj_write_kernel<2><<<grid, PwShape<2>::kThreads, smem, as_stream(stream)>>>(pp);
+  else
+    kv_proj_write_kernel<1><<<grid, PwShape<1>::kThreads, smem, as_stream(stream)>>>(pp);
   return cudaGetLastError() == cudaSuccess ? NVQSA_OK : NVQSA_ERR_LAUNCH;
 }

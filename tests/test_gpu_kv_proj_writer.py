@@ -67,6 +67,7 @@ def _slots_positions(rng, tokens, blocks, page, max_pos, holes=True):
     (128, 512, 1, 64, True, True),       # partial NeoX rotation (Qwen3-Next style), one head
     (77, 1000, 4, 64, False, True),      # GPT-J pairs, hidden not a multiple of 64 (zero-filled tail)
     (200, 768, 2, 0, True, False),       # no rotation, no norm: the plain writer on the projection
+    (2400, 512, 4, 256, True, True),     # more 128-token CTAs than SMs: 256-token CTAs, ragged last one
 ])
 def test_exact_projection_matches_oracle_chain(tokens, hidden_size, kvh, rot, neox, norm):
     rng = np.random.default_rng(tokens + hidden_size + kvh)
@@ -90,8 +91,9 @@ def test_exact_projection_matches_oracle_chain(tokens, hidden_size, kvh, rot, ne
     assert np.array_equal(cuda_to_bits(ko)[valid.astype(bool)], kr[valid.astype(bool)])
 
 
-def test_random_projection_within_one_rounding_and_epilogue_bit_exact():
-    tokens, hidden_size, kvh = 1000, 4096, 2
+@pytest.mark.parametrize("tokens", [1000, 5000])  # 128-token CTAs; 256-token CTAs (more than one wave of 128)
+def test_random_projection_within_one_rounding_and_epilogue_bit_exact(tokens):
+    hidden_size, kvh = 4096, 2
     rng = np.random.default_rng(17)
     g = torch.Generator(device="cuda").manual_seed(17)
     hidden = torch.randn(tokens, hidden_size, device="cuda", generator=g).to(torch.bfloat16)
