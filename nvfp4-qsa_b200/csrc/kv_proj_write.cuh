@@ -16,24 +16,29 @@
 // TMA (128-byte swizzle); one thread of the MMA warp issues, per 16-wide
 // k-step and per 128-token half, a tcgen05.mma (M 128, N 256, K 16, bf16 ->
 // fp32) into that half's 128 x 256 fp32 accumulator in tensor memory, and
-// releases each stage with tcgen05.commit.  The 4 MH epilogue warps (warp w:
-// lane quarter w % 4 of half w / 4, thread = token row) then read the row
-// back, round it to bf16 as the GEMM output
-// would be, and run the writer's arithmetic on whole 16-element groups: for
-// K the RMS norm (the writer's summation order, emulated in one thread),
-// the rotation (bf16 arithmetic, NeoX halves or GPT-J pairs), then the
-// group scale and E2M1 codes; for V the codes alone.
+// releases each stage with tcgen05.commit.  The 8 MH epilogue warps load
+// each token's position, slot and cos/sin row during the mainloop; once the
+// accumulators are complete two threads per token row (one lane of each of
+// two warps on the row's tensor-memory lane) read the row back, round it to
+// bf16 as the GEMM output would be, and run the writer's arithmetic on whole
+// 16-element groups, 8 groups each: for K the RMS norm (the writer's
+// summation order: each thread's partial sums go through shared memory and
+// both add all 32 in that order), the rotation (bf16 arithmetic, NeoX halves
+// or GPT-J pairs; a NeoX pair of groups stays in one thread), then the group
+// scale and E2M1 codes; for V the codes alone.
 constexpr int kPwBN = 256;        // columns per CTA: one head
 constexpr int kPwBK = 64;         // k-slice per stage: 128 bytes of bf16 (one swizzle atom row)
 constexpr uint32_t kPwStageB = kPwBN * kPwBK * 2;  // 32 KB
 // MH halves of 128 tokens per CTA, each its own M = 128 accumulator (256 tensor-memory columns) fed by the
-// same weight tile: MH = 2 halves the weight traffic per token; 4 MH epilogue warps, then the TMA and MMA warps.
+// same weight tile: MH = 2 halves the weight traffic per token.  8 MH epilogue warps (two threads per token
+// row, each finishing 8 of its 16 groups), then the TMA and MMA warps.
 template <int MH>
 struct PwShape {
   static constexpr int kBM = 128 * MH;
   static constexpr int kStages = MH == 1 ? 4 : 3;
-  static constexpr int kThreads = 32 * (4 * MH + 2);
-  static constexpr int kTmaWarp = 4 * MH, kMmaWarp = 4 * MH + 1;
+  static constexpr int kEpiWarps = 8 * MH;
+  static constexpr int kThreads = 32 * (kEpiWarps + 2);
+  static constexpr int kTmaWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
   static constexpr uint32_t kStageA = (uint32_t)kBM * kPwBK * 2;
   static constexpr uint32_t kTmemCols = 256u * MH;
 };
@@ -46,6 +51,7 @@ template <int MH>
 struct __align__(1024) SmemPw {
   uint8_t a[PwShape<MH>::kStages][PwShape<MH>::kStageA];  // hidden rows, swizzled 128-byte rows (1024-byte atoms)
   uint8_t b[PwShape<MH>::kStages][kPwStageB];             // weight rows
+  float nw[kPwBN];  // norm weight + offset (fp32); at a multiple of 1024 bytes, read as float2
   unsigned long long full[PwShape<MH>::kStages];
   unsigned long long empty[PwShape<MH>::kStages];
   unsigned long long accum;
@@ -53,6 +59,7 @@ struct __align__(1024) SmemPw {
   float lut[2][256];
   float quot[2][16];
 };
+constexpr int kPwRedStride = 33;  // floats per token row of the norm partials (conflict-free), in the free stages
 
 struct ProjParams {
   CUtensorMap map_x;      // hidden [tokens, hidden] bf16, box 64 x (128 MH)
@@ -145,6 +152,8 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
   build_out_scale_lut(wp, sm.lut, sm.quot);
+  if (wp.norm_weight != nullptr)
+    for (int j = tid; j < kPwBN; j += S::kThreads) sm.nw[j] = __fadd_rn(__ldg(wp.norm_weight + j), wp.norm_offset);
   pw_fence_before();
   __syncthreads();
   pw_fence_after();
@@ -203,12 +212,18 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue: thread = token row ----------------
-    const int q = warp & 3, half_m = warp >> 2;  // lane quarter q of accumulator half_m
-    const int64_t row = m0 + 128 * half_m + 32 * q + lane;
+    // ---------------- epilogue: two threads per token row ----------------
+    // warp w: lane quarter w % 4 of accumulator half (w / 4) % MH, column split c = w / (4 MH); split c
+    // finishes the groups g with own(g) == c, keeping each NeoX pair (g, g + half/16) in one thread
+    const int q = warp & 3, half_m = (warp >> 2) % MH, c = warp / (4 * MH);
+    const int trow = 128 * half_m + 32 * q + lane;  // row inside the tile
+    const int64_t row = m0 + trow;
     const bool live = row < wp.num_tokens;
-    const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
-    pw_fence_after();
+    const int half = wp.rot_dim >> 1;
+    const int P = wp.neox ? (half >> 4) : 0;  // NeoX: groups [0, P) pair with [P, 2P)
+    auto own = [&](int g) -> int { return (g < 2 * P) ? (P == 1 ? 0 : (g % P) & 1) : (g & 1); };
+
+    // per-row loads before the accumulator is ready: position, slot, and the cos/sin row into L2
     int64_t pos = 0;
     bool pos_ok = live;
     if (live && wp.rot_dim > 0) {
@@ -217,7 +232,14 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
       if (!pos_ok) pos = 0;
     }
     int64_t block = 0, offset = 0;
-    const bool slot_ok = ready && pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
+    bool slot_ok = pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
+    const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
+    if (r == 0 && wp.rot_dim > 0 && c == 0)
+      for (int b = 0; b < wp.rot_dim * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + b / 2));
+
+    const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
+    pw_fence_after();
+    slot_ok = slot_ok && ready;
     uint8_t* rec = wp.data[0] + ((int64_t)(int32_t)block * wp.rec_block32 +
                                  (int32_t)((int32_t)offset * wp.rec_token32 + head * wp.rec_head32));
     uint8_t* drow = rec + (r == 0 ? 0 : wp.off_vd);
@@ -255,7 +277,7 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
                               ? p.value_out + row * p.value_out_stride_token + head * p.value_out_stride_head
                               : nullptr;
 #pragma unroll 1
-      for (int g = 0; g < 16; ++g) {
+      for (int g = c; g < 16; g += 2) {
         uint32_t x[8];
         pw_load_bf16(taddr + 16 * g, x);
         if (vo) put_bf16(vo, g, x);
@@ -269,10 +291,11 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
       float rr = 1.0f;
       if (norm) {
         // the writer's order: partial l = (even squares of [8l, 8l+8)) + (odd squares), then pairwise at
-        // distances 16, 8, 4, 2, 1
-        float part[32];
-#pragma unroll
+        // distances 16, 8, 4, 2, 1; each thread computes its groups' partials, both read all 32
+        float* red = reinterpret_cast<float*>(&sm.b[0][0]) + trow * kPwRedStride;  // stages are free now
+#pragma unroll 1
         for (int g = 0; g < 16; ++g) {
+          if (own(g) != c) continue;
           uint32_t x[8];
           pw_load_bf16(taddr + 16 * g, x);
 #pragma unroll
@@ -283,9 +306,13 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
               const float2 f = make_float2(bf_lo(x[4 * h + i]), bf_hi(x[4 * h + i]));
               a = __ffma2_rn(f, f, a);
             }
-            part[2 * g + h] = __fadd_rn(a.x, a.y);
+            red[2 * g + h] = __fadd_rn(a.x, a.y);
           }
         }
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * S::kEpiWarps) : "memory");  // epilogue warps only
+        float part[32];
+#pragma unroll
+        for (int l = 0; l < 32; ++l) part[l] = red[l];
 #pragma unroll
         for (int m = 16; m >= 1; m >>= 1)
 #pragma unroll
@@ -297,17 +324,11 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
       auto load_normed = [&](int g, uint32_t (&x)[8]) {
         pw_load_bf16(taddr + 16 * g, x);
         if (norm) {
-          const float4* wv = reinterpret_cast<const float4*>(wp.norm_weight + 16 * g);
+          const float2* wv = reinterpret_cast<const float2*>(sm.nw + 16 * g);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 w4 = __ldg(wv + q);
-            const float2 wa = make_float2(__fadd_rn(w4.x, wp.norm_offset), __fadd_rn(w4.y, wp.norm_offset));
-            const float2 wb = make_float2(__fadd_rn(w4.z, wp.norm_offset), __fadd_rn(w4.w, wp.norm_offset));
-            const float2 ya = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(x[2 * q]), bf_hi(x[2 * q])), rr2), wa);
-            const float2 yb =
-                __fmul2_rn(__fmul2_rn(make_float2(bf_lo(x[2 * q + 1]), bf_hi(x[2 * q + 1])), rr2), wb);
-            x[2 * q] = pack_bf16x2(ya.x, ya.y);
-            x[2 * q + 1] = pack_bf16x2(yb.x, yb.y);
+          for (int i = 0; i < 8; ++i) {
+            const float2 y = __fmul2_rn(__fmul2_rn(make_float2(bf_lo(x[i]), bf_hi(x[i])), rr2), wv[i]);
+            x[i] = pack_bf16x2(y.x, y.y);
           }
         }
       };
@@ -316,17 +337,15 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
         put_group(g, x);
       };
       const int rot_groups = wp.rot_dim >> 4;  // groups of 16 inside the rotated dims
-      const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
-      const int half = wp.rot_dim >> 1;
       if (wp.rot_dim > 0 && wp.neox) {
-        // group ga of the first half pairs with group ga + half/16 (half is a multiple of 16)
 #pragma unroll 1
-        for (int ga = 0; ga < (half >> 4); ++ga) {
+        for (int ga = 0; ga < P; ++ga) {
+          if (own(ga) != c) continue;
           uint32_t x1[8], x2[8], cw[8], sw[8];
-          load_normed(ga, x1);
-          load_normed(ga + (half >> 4), x2);
           load_bf16_run<16>(cs + 16 * ga, cw);
           load_bf16_run<16>(cs + half + 16 * ga, sw);
+          load_normed(ga, x1);
+          load_normed(ga + P, x2);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t a = x1[i], b = x2[i];
@@ -334,16 +353,16 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
             x2[i] = bf16x2_add(bf16x2_mul(b, cw[i]), bf16x2_mul(a, sw[i]));
           }
           finish(ga, x1);
-          finish(ga + (half >> 4), x2);
+          finish(ga + P, x2);
         }
       } else if (wp.rot_dim > 0) {
         // GPT-J: word i of group g = elements (16g + 2i, 16g + 2i + 1), cos/sin index 8g + i
 #pragma unroll 1
-        for (int g = 0; g < rot_groups; ++g) {
+        for (int g = c; g < rot_groups; g += 2) {
           uint32_t x[8], cw[4], sw[4];
-          load_normed(g, x);
           load_bf16_run<8>(cs + 8 * g, cw);
           load_bf16_run<8>(cs + half + 8 * g, sw);
+          load_normed(g, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t sel = (i & 1) ? 0x3232u : 0x1010u;
@@ -353,8 +372,10 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
           finish(g, x);
         }
       }
+      const int first_plain = wp.rot_dim > 0 ? rot_groups : 0;  // dims past the rotation pass through
 #pragma unroll 1
-      for (int g = (wp.rot_dim > 0 ? rot_groups : 0); g < 16; ++g) {  // dims past the rotation pass through
+      for (int g = first_plain; g < 16; ++g) {
+        if (own(g) != c) continue;
         uint32_t x[8];
         load_normed(g, x);
         finish(g, x);
