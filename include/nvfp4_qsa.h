@@ -161,8 +161,8 @@ int nvqsa_norm_rope_write_cache(
  * head_dim  : 256 only (NVQSA_ERR_HEAD_DIM).
  * cache     : the four regions must be views of one [blocks, kv_heads, page,
  *             288]-style record storage with shared strides (the reference's
- *             and vLLM's layout) and 8-byte aligned strides and bases, else
- *             NVQSA_ERR_MISALIGNED.
+ *             and vLLM's layout) and 16-byte aligned strides and region
+ *             bases, else NVQSA_ERR_MISALIGNED.
  * rotation  : rotary_dim a multiple of 32 (NeoX) or 16 (GPT-J), at most 256;
  *             the cos/sin table's base and row stride 16-byte aligned.
  * norm_weight (fp32 [256], 16-byte aligned) or NULL; eps as the fused writer.

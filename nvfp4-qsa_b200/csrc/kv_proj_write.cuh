@@ -59,6 +59,7 @@ struct __align__(1024) SmemPw {
   float lut[2][256];
   float quot[2][16];
 };
+constexpr int kPwRecRow = 144;   // staged record bytes per token row: 128 code bytes + 16 scale bytes
 constexpr int kPwRedStride = 33;  // floats per token row of the norm partials (conflict-free), in the free stages
 
 struct ProjParams {
@@ -120,6 +121,27 @@ __device__ __forceinline__ void pw_load_bf16(uint32_t taddr, uint32_t (&w)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) w[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+}
+
+// Two groups' columns with both loads in flight before one wait.
+__device__ __forceinline__ void pw_load2_bf16(uint32_t ta, uint32_t tb, uint32_t (&wa)[8], uint32_t (&wb)[8]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(ta));
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(tb));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    wa[i] = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    wb[i] = pack_bf16x2(__uint_as_float(r[16 + 2 * i]), __uint_as_float(r[17 + 2 * i]));
+  }
 }
 
 template <int MH>
@@ -234,8 +256,28 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
     int64_t block = 0, offset = 0;
     bool slot_ok = pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
     const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
-    if (r == 0 && wp.rot_dim > 0 && c == 0)
-      for (int b = 0; b < wp.rot_dim * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + b / 2));
+    // cos/sin of this split's first rotation step (NeoX: 16 of each at 16c; GPT-J: 8 at 8c) into registers,
+    // the rest of the row into L2
+    uint32_t pre_c[8], pre_s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pre_c[i] = pre_s[i] = 0u;
+    if (r == 0 && wp.rot_dim > 0) {
+      if (wp.neox && 16 * c < half) {
+        load_bf16_run<16>(cs + 16 * c, pre_c);
+        load_bf16_run<16>(cs + half + 16 * c, pre_s);
+      } else if (!wp.neox && 16 * c < wp.rot_dim) {
+        uint32_t c4[4], s4[4];
+        load_bf16_run<8>(cs + 8 * c, c4);
+        load_bf16_run<8>(cs + half + 8 * c, s4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          pre_c[i] = c4[i];
+          pre_s[i] = s4[i];
+        }
+      }
+      if (c == 0)
+        for (int b = 0; b < wp.rot_dim * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + b / 2));
+    }
 
     const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
     pw_fence_after();
@@ -246,6 +288,11 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
     uint8_t* srow = rec + (r == 0 ? wp.off_ks : wp.off_vs);
     const uint32_t taddr = tmem + 256u * half_m + ((uint32_t)(32 * q) << 16);
     const float gs = wp.global_scale[r];
+    // the row's record bytes are staged in the free stage buffers and written out row by row (coalesced)
+    uint8_t* stage_base = &sm.a[0][0];
+    uint8_t* stage = stage_base + trow * kPwRecRow;
+    uint8_t** rowptr = reinterpret_cast<uint8_t**>(stage_base + S::kBM * kPwRecRow);
+    if (c == 0) rowptr[trow] = slot_ok ? drow : nullptr;
 
     // encode one finished 16-element group (bf16 pairs) and store its 8 code bytes and scale byte
     auto put_group = [&](int g, const uint32_t (&x)[8]) {
@@ -261,10 +308,8 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
       } else {
         encode_row<16, false>(x, sm.lut[r][sb], wp.zero, packed);
       }
-      if (slot_ok) {
-        *reinterpret_cast<uint2*>(drow + 8 * g) = make_uint2(packed[0], packed[1]);
-        srow[g] = (uint8_t)sb;
-      }
+      *reinterpret_cast<uint2*>(stage + 8 * g) = make_uint2(packed[0], packed[1]);
+      stage[128 + g] = (uint8_t)sb;
     };
     auto put_bf16 = [&](__nv_bfloat16* out, int g, const uint32_t (&x)[8]) {
       uint4* o = reinterpret_cast<uint4*>(out + 16 * g);
@@ -277,11 +322,15 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
                               ? p.value_out + row * p.value_out_stride_token + head * p.value_out_stride_head
                               : nullptr;
 #pragma unroll 1
-      for (int g = c; g < 16; g += 2) {
-        uint32_t x[8];
-        pw_load_bf16(taddr + 16 * g, x);
-        if (vo) put_bf16(vo, g, x);
-        put_group(g, x);
+      for (int g = c; g < 16; g += 4) {  // groups g and g + 2 of this thread's 8
+        uint32_t x0[8], x1[8];
+        pw_load2_bf16(taddr + 16 * g, taddr + 16 * (g + 2), x0, x1);
+        if (vo) {
+          put_bf16(vo, g, x0);
+          put_bf16(vo, g + 2, x1);
+        }
+        put_group(g, x0);
+        put_group(g + 2, x1);
       }
     } else {
       __nv_bfloat16* ko = (wp.key_out && pos_ok && ready)
@@ -293,11 +342,7 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
         // the writer's order: partial l = (even squares of [8l, 8l+8)) + (odd squares), then pairwise at
         // distances 16, 8, 4, 2, 1; each thread computes its groups' partials, both read all 32
         float* red = reinterpret_cast<float*>(&sm.b[0][0]) + trow * kPwRedStride;  // stages are free now
-#pragma unroll 1
-        for (int g = 0; g < 16; ++g) {
-          if (own(g) != c) continue;
-          uint32_t x[8];
-          pw_load_bf16(taddr + 16 * g, x);
+        auto partials = [&](int g, const uint32_t (&x)[8]) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float2 a = make_float2(0.0f, 0.0f);
@@ -308,6 +353,13 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
             }
             red[2 * g + h] = __fadd_rn(a.x, a.y);
           }
+        };
+#pragma unroll 1
+        for (int g = c; g < 16; g += 4) {  // this split's partials: groups g and g + 2
+          uint32_t x0[8], x1[8];
+          pw_load2_bf16(taddr + 16 * g, taddr + 16 * (g + 2), x0, x1);
+          partials(g, x0);
+          partials(g + 2, x1);
         }
         asm volatile("bar.sync 1, %0;" ::"r"(32 * S::kEpiWarps) : "memory");  // epilogue warps only
         float part[32];
@@ -320,9 +372,8 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
         rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(part[0], wp.inv_head_dim), wp.norm_eps)));
       }
       const float2 rr2 = make_float2(rr, rr);
-      // group g read back, rounded, normed: y = bf16((x * r) * (w + offset))
-      auto load_normed = [&](int g, uint32_t (&x)[8]) {
-        pw_load_bf16(taddr + 16 * g, x);
+      // group g (read back and rounded) normed: y = bf16((x * r) * (w + offset))
+      auto normed = [&](int g, uint32_t (&x)[8]) {
         if (norm) {
           const float2* wv = reinterpret_cast<const float2*>(sm.nw + 16 * g);
 #pragma unroll
@@ -342,10 +393,19 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
         for (int ga = 0; ga < P; ++ga) {
           if (own(ga) != c) continue;
           uint32_t x1[8], x2[8], cw[8], sw[8];
-          load_bf16_run<16>(cs + 16 * ga, cw);
-          load_bf16_run<16>(cs + half + 16 * ga, sw);
-          load_normed(ga, x1);
-          load_normed(ga + P, x2);
+          if (ga == c) {  // the first pair of this split: cos/sin loaded during the mainloop
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              cw[i] = pre_c[i];
+              sw[i] = pre_s[i];
+            }
+          } else {
+            load_bf16_run<16>(cs + 16 * ga, cw);
+            load_bf16_run<16>(cs + half + 16 * ga, sw);
+          }
+          pw_load2_bf16(taddr + 16 * ga, taddr + 16 * (ga + P), x1, x2);
+          normed(ga, x1);
+          normed(ga + P, x2);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t a = x1[i], b = x2[i];
@@ -360,9 +420,18 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
 #pragma unroll 1
         for (int g = c; g < rot_groups; g += 2) {
           uint32_t x[8], cw[4], sw[4];
-          load_bf16_run<8>(cs + 8 * g, cw);
-          load_bf16_run<8>(cs + half + 8 * g, sw);
-          load_normed(g, x);
+          if (g == c) {  // the first rotated group of this split: cos/sin loaded during the mainloop
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              cw[i] = pre_c[i];
+              sw[i] = pre_s[i];
+            }
+          } else {
+            load_bf16_run<8>(cs + 8 * g, cw);
+            load_bf16_run<8>(cs + half + 8 * g, sw);
+          }
+          pw_load_bf16(taddr + 16 * g, x);
+          normed(g, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t sel = (i & 1) ? 0x3232u : 0x1010u;
@@ -372,13 +441,35 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
           finish(g, x);
         }
       }
-      const int first_plain = wp.rot_dim > 0 ? rot_groups : 0;  // dims past the rotation pass through
+      // dims past the rotation pass through: this split's groups g = c (mod 2) from there, two at a time
+      int g = wp.rot_dim > 0 ? rot_groups : 0;
+      if ((g & 1) != c) ++g;
 #pragma unroll 1
-      for (int g = first_plain; g < 16; ++g) {
-        if (own(g) != c) continue;
-        uint32_t x[8];
-        load_normed(g, x);
-        finish(g, x);
+      for (; g < 16; g += 4) {
+        uint32_t x0[8], x1[8];
+        if (g + 2 < 16) {
+          pw_load2_bf16(taddr + 16 * g, taddr + 16 * (g + 2), x0, x1);
+          normed(g, x0);
+          finish(g, x0);
+          normed(g + 2, x1);
+          finish(g + 2, x1);
+        } else {
+          pw_load_bf16(taddr + 16 * g, x0);
+          normed(g, x0);
+          finish(g, x0);
+        }
+      }
+    }
+    // write the staged records: 9 chunks of 16 bytes per row (8 of codes, 1 of scales), consecutive threads
+    // on consecutive chunks
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * S::kEpiWarps) : "memory");  // epilogue warps only
+    const int64_t sdelta = srow - drow;
+    for (int idx = tid; idx < S::kBM * 9; idx += 32 * S::kEpiWarps) {
+      const int rr = idx / 9, j = idx - 9 * rr;
+      uint8_t* d = rowptr[rr];
+      if (d) {
+        const uint4 v = *reinterpret_cast<const uint4*>(stage_base + rr * kPwRecRow + 16 * j);
+        *reinterpret_cast<uint4*>(j < 8 ? d + 16 * j : d + sdelta) = v;
       }
     }
   }

@@ -1061,9 +1061,9 @@ extern "C" int nvqsa_kv_proj_write_cache(
                                vs_stride_token, vs_stride_head, slot_mapping, num_tokens, kv_heads, head_dim,
                                num_blocks, page_size, key_global_scale, value_global_scale);
   if (st != NVQSA_OK || !go) return st;
-  // the epilogue addresses a token's four regions from one record base and stores 8-byte code runs
-  if (!w.record || !aligned_to(w.data[0], 8) || w.off_ks % 8 != 0 || w.off_vd % 8 != 0 || w.rec_block32 % 8 != 0 ||
-      w.rec_token32 % 8 != 0 || w.rec_head32 % 8 != 0)
+  // the epilogue addresses a token's four regions from one record base and writes them in 16-byte chunks
+  if (!w.record || !aligned_to(w.data[0], 16) || w.off_ks % 16 != 0 || w.off_vd % 16 != 0 || w.off_vs % 16 != 0 ||
+      w.rec_block32 % 16 != 0 || w.rec_token32 % 16 != 0 || w.rec_head32 % 16 != 0)
     return NVQSA_ERR_MISALIGNED;
   w.norm_weight = norm_weight;
   w.norm_offset = norm_weight_offset;
