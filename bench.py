@@ -95,6 +95,7 @@ NCU_TRAFFIC = {
     "fused_write": 18579712,   # write_cache_kernel<256,...,FUSE>, 8,192 tokens
     "bf16": 413479424,         # sparse_attention_bf16_kernel, 96 rows x top-2048 (48-row capture x 2)
     "topk": 50476800,          # topk_indices_kernel, 96 rows x 131,072 scores, k = 2048
+    "kv_proj": 80963072,       # kv_proj_write_kernel<2>, 8,192 tokens x hidden 4,096 -> 1,024 K|V columns
 }
 
 
@@ -432,7 +433,9 @@ def bench_kv_proj_write(device, steps):
         "speedup_vs_unfused": chain / fused,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind, "kernel": "kv_proj_write_kernel",
-                     "algorithmic_flops_per_launch": flops, "traffic": None},
+                     "algorithmic_flops_per_launch": flops, "traffic": NCU_TRAFFIC["kv_proj"],
+                     "algorithmic_bytes_per_launch": tokens * hidden * 2 + cols * hidden * 2 + tokens * (
+                         16 + rot * 2 + KV_HEADS * RECORD)},
         "gpu_launches": launches,
     }
 
