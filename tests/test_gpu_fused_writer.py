@@ -63,7 +63,9 @@ CASES = [  # (head_dim, rotary_dim, neox, norm, kv_heads)
     (256, 64, False, True, 2),    # GPT-J pairs
     (256, 0, True, True, 2),      # norm only
     (256, 64, True, False, 2),    # rotary only
-    (256, 16, True, True, 3),     # smallest rotary for 256; odd head count
+    (256, 16, True, True, 3),     # smallest rotary for 256; odd head count (half-group lanes)
+    (256, 32, True, True, 3),     # one NeoX pair of groups; odd head count (lane-per-group kernel)
+    (256, 16, False, True, 1),    # GPT-J over one group; one head
     (128, 32, True, True, 1),
     (64, 64, False, True, 2),
     (64, 4, True, True, 2),
