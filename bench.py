@@ -388,8 +388,8 @@ def bench_kv_proj_write(device, steps):
     def chain_round():
         for x, wkv, regs, slots, pos, kv in bufs:
             torch.mm(x, wkv.t(), out=kv)
-            k = kv[:, :cols // 2].view(tokens, KV_HEADS, HEAD_DIM)
-            v = kv[:, cols // 2:].view(tokens, KV_HEADS, HEAD_DIM)
+            k = kv[:, :cols // 2].view(-1, KV_HEADS, HEAD_DIM)
+            v = kv[:, cols // 2:].view(-1, KV_HEADS, HEAD_DIM)
             kernels.qsa_norm_rope_write_cache_nvfp4(k, v, *regs, slots, 1.0, 1.0, positions=pos,
                                                     cos_sin_cache=cos_sin, k_norm_weight=weight, eps=1e-6)
 
@@ -417,6 +417,12 @@ def bench_kv_proj_write(device, steps):
     fused, launches = measure(fused_round)
     chain, _ = measure(chain_round)
     gemm, _ = measure(gemm_round)
+    # a decode-size batch (96 tokens, the config-5a row count) through both paths, same buffers
+    full = bufs
+    bufs = [(x[:96], wkv, regs, slots[:96], pos[:96], kv[:96]) for x, wkv, regs, slots, pos, kv in full]
+    fused96, launches96 = measure(fused_round)
+    chain96, _ = measure(chain_round)
+    bufs = full
     flops = 2.0 * tokens * hidden * cols
     peak, kind = measured_tensor_peak()
     achieved = flops / fused / 1e12
@@ -431,12 +437,14 @@ def bench_kv_proj_write(device, steps):
         "unfused": "torch.mm (cuBLAS) into bf16 K|V [8192, 1024], then nvqsa_norm_rope_write_cache",
         "cublas_gemm_only_us": gemm * 1e6,
         "speedup_vs_unfused": chain / fused,
+        "decode_96_tokens": {"us_per_launch": fused96 * 1e6, "unfused_us": chain96 * 1e6,
+                             "what": "the same call on the first 96 tokens: 4 CTAs, bound by reading the weights"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind, "kernel": "kv_proj_write_kernel",
                      "algorithmic_flops_per_launch": flops, "traffic": NCU_TRAFFIC["kv_proj"],
                      "algorithmic_bytes_per_launch": tokens * hidden * 2 + cols * hidden * 2 + tokens * (
                          16 + rot * 2 + KV_HEADS * RECORD)},
-        "gpu_launches": launches,
+        "gpu_launches": launches + launches96,
     }
 
 

@@ -60,13 +60,16 @@ struct __align__(1024) SmemPw {
   float quot[2][16];
 };
 constexpr int kPwRecRow = 144;   // staged record bytes per token row: 128 code bytes + 16 scale bytes
-constexpr int kPwRedStride = 33;  // floats per token row of the norm partials (conflict-free), in the free stages
+constexpr int kPwRedStride = 33;
+constexpr int kPwPartStride = 260;  // floats per token row of a k-split partial (16-byte skew per row)  // floats per token row of the norm partials (conflict-free), in the free stages
 
 struct ProjParams {
   CUtensorMap map_x;      // hidden [tokens, hidden] bf16, box 64 x (128 MH)
   CUtensorMap map_w[2];   // K / V weight rows [kv_heads * 256, hidden] bf16, box 64 x 256
   WriteParams w;          // cache regions, slots, scales, norm and rotation (head_dim 256, record layout)
   int32_t kblocks;        // hidden / 64, rounded up (the tail is zero-filled by TMA)
+  int32_t ksplit;         // CTAs of a cluster splitting the k-blocks of one tile (1: no split, MH = 1 only)
+  int32_t kbs;            // k-blocks per split rank (every rank has at least one)
   __nv_bfloat16* value_out;  // optional bf16 V projection [tokens, kv_heads, 256]
   int64_t value_out_stride_token, value_out_stride_head;
 };
@@ -106,6 +109,42 @@ __device__ __forceinline__ uint64_t pw_desc(uint32_t addr) {
 // Instruction descriptor: D f32, A and B bf16, both K-major, N = 256, M = 128.
 constexpr uint32_t kPwIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPwBN >> 3) << 17) |
                               ((uint32_t)(128 >> 4) << 24);
+
+// Every thread of every CTA of the cluster arrives; shared-memory writes before it are visible after it.
+__device__ __forceinline__ void pw_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ float4 pw_ld_cluster_f4(uint32_t addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(addr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void pw_tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void pw_tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])));
+}
 
 __device__ __forceinline__ void pw_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void pw_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
@@ -154,7 +193,10 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
   const WriteParams& wp = p.w;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kvh = wp.kv_heads;
-  const int nt = blockIdx.x;  // 0 .. kvh-1: K head nt; kvh .. 2 kvh-1: V head nt - kvh
+  const int ks = p.ksplit;                 // CTAs of this tile's cluster, each with its own k-blocks
+  const int rank = blockIdx.x % ks;
+  const int nt = blockIdx.x / ks;  // 0 .. kvh-1: K head nt; kvh .. 2 kvh-1: V head nt - kvh
+  const int kb0 = rank * p.kbs;
   const int r = nt < kvh ? 0 : 1;
   const int head = nt - r * kvh;
   const int64_t m0 = (int64_t)blockIdx.y * S::kBM;
@@ -180,7 +222,52 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
   __syncthreads();
   pw_fence_after();
   const uint32_t tmem = sm.tmem;
-  const int kb = p.kblocks;
+  const int kb = min(p.kblocks - kb0, p.kbs);  // this CTA's k-blocks, from kb0
+
+  // ---------------- epilogue rows: two threads per token row ----------------
+  // warp w: lane quarter w % 4 of accumulator half (w / 4) % MH, column split c = w / (4 MH); split c
+  // finishes the groups g with own(g) == c, keeping each NeoX pair (g, g + half/16) in one thread
+  const int q = warp & 3, half_m = (warp >> 2) % MH, c = warp / (4 * MH);
+  const int trow = 128 * half_m + 32 * q + lane;  // row inside the tile
+  const int64_t row = m0 + trow;
+  const bool live = warp < S::kEpiWarps && row < wp.num_tokens && (ks == 1 || trow / ((S::kBM + ks - 1) / ks) == rank);
+  const int half = wp.rot_dim >> 1;
+  const int P = wp.neox ? (half >> 4) : 0;  // NeoX: groups [0, P) pair with [P, 2P)
+  auto own = [&](int g) -> int { return (g < 2 * P) ? (P == 1 ? 0 : (g % P) & 1) : (g & 1); };
+
+  // per-row loads while the mainloop runs: position, slot, and the cos/sin row into L2
+  int64_t pos = 0;
+  bool pos_ok = live;
+  if (live && wp.rot_dim > 0) {
+    pos = __ldg(wp.positions + row);
+    pos_ok = pos >= 0 && pos < wp.max_position;
+    if (!pos_ok) pos = 0;
+  }
+  int64_t block = 0, offset = 0;
+  bool slot_ok = pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
+  const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
+  // cos/sin of this split's first rotation step (NeoX: 16 of each at 16c; GPT-J: 8 at 8c) into registers,
+  // the rest of the row into L2
+  uint32_t pre_c[8], pre_s[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pre_c[i] = pre_s[i] = 0u;
+  if (r == 0 && wp.rot_dim > 0 && warp < S::kEpiWarps) {
+    if (wp.neox && 16 * c < half) {
+      load_bf16_run<16>(cs + 16 * c, pre_c);
+      load_bf16_run<16>(cs + half + 16 * c, pre_s);
+    } else if (!wp.neox && 16 * c < wp.rot_dim) {
+      uint32_t c4[4], s4[4];
+      load_bf16_run<8>(cs + 8 * c, c4);
+      load_bf16_run<8>(cs + half + 8 * c, s4);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        pre_c[i] = c4[i];
+        pre_s[i] = s4[i];
+      }
+    }
+    if (c == 0)
+      for (int b = 0; b < wp.rot_dim * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + b / 2));
+  }
 
   if (warp == S::kTmaWarp) {
     // ---------------- producer: TMA into the stage ring ----------------
@@ -193,14 +280,15 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(full),
                      "r"(S::kStageA + kPwStageB)
                      : "memory");
-        pw_tma_2d(smem_u32(sm.a[s]), &p.map_x, i * kPwBK, (int32_t)m0, full);
-        pw_tma_2d(smem_u32(sm.b[s]), &p.map_w[r], i * kPwBK, head * kPwBN, full);
+        pw_tma_2d(smem_u32(sm.a[s]), &p.map_x, (kb0 + i) * kPwBK, (int32_t)m0, full);
+        pw_tma_2d(smem_u32(sm.b[s]), &p.map_w[r], (kb0 + i) * kPwBK, head * kPwBN, full);
         issued = i + 1;
       }
       // copies still in flight land before the CTA can leave (only a timed-out consumer leaves them)
       for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
         pw_wait(smem_u32(&sm.full[j % kStages]), (uint32_t)((j / kStages) & 1));
     }
+    __syncwarp();
   } else if (warp == S::kMmaWarp) {
     // ---------------- MMA issue: one thread ----------------
     if (lane == 0) {
@@ -233,52 +321,79 @@ __global__ void __launch_bounds__(PwShape<MH>::kThreads, 1) kv_proj_write_kernel
                    : "memory");
     }
     __syncwarp();
-  } else {
-    // ---------------- epilogue: two threads per token row ----------------
-    // warp w: lane quarter w % 4 of accumulator half (w / 4) % MH, column split c = w / (4 MH); split c
-    // finishes the groups g with own(g) == c, keeping each NeoX pair (g, g + half/16) in one thread
-    const int q = warp & 3, half_m = (warp >> 2) % MH, c = warp / (4 * MH);
-    const int trow = 128 * half_m + 32 * q + lane;  // row inside the tile
-    const int64_t row = m0 + trow;
-    const bool live = row < wp.num_tokens;
-    const int half = wp.rot_dim >> 1;
-    const int P = wp.neox ? (half >> 4) : 0;  // NeoX: groups [0, P) pair with [P, 2P)
-    auto own = [&](int g) -> int { return (g < 2 * P) ? (P == 1 ? 0 : (g % P) & 1) : (g & 1); };
+  }
 
-    // per-row loads before the accumulator is ready: position, slot, and the cos/sin row into L2
-    int64_t pos = 0;
-    bool pos_ok = live;
-    if (live && wp.rot_dim > 0) {
-      pos = __ldg(wp.positions + row);
-      pos_ok = pos >= 0 && pos < wp.max_position;
-      if (!pos_ok) pos = 0;
-    }
-    int64_t block = 0, offset = 0;
-    bool slot_ok = pos_ok && slot_position<true>(wp, __ldg(wp.slots + row), block, offset);
-    const __nv_bfloat16* cs = wp.cos_sin + pos * wp.cos_sin_stride;
-    // cos/sin of this split's first rotation step (NeoX: 16 of each at 16c; GPT-J: 8 at 8c) into registers,
-    // the rest of the row into L2
-    uint32_t pre_c[8], pre_s[8];
+  // ---------------- k-split: sum the cluster's partial accumulators (all warps take the cluster barriers) ----------------
+  // Each rank parks its fp32 partial in its free stage buffers; rank j then adds, for its rows
+  // [j R, j R + R) (R = 128 / ks rounded up), the partials of ranks 0, 1, ..., ks - 1 in that order over
+  // distributed shared memory and writes the sums into its own tensor memory, which the epilogue reads.
+  if (MH == 1 && ks > 1) {
+    float* part = reinterpret_cast<float*>(&sm.a[0][0]);  // [128][kPwPartStride]: stages a and b are contiguous
+    const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + 128u * c;
+    float* prow = part + trow * kPwPartStride + 128 * c;
+    if (warp < S::kEpiWarps) {
+      pw_wait(smem_u32(&sm.accum), 0u);
+      pw_fence_after();
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) {
+        float v[16];
+        pw_tmem_ld16(ta + 16 * j, v);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pre_c[i] = pre_s[i] = 0u;
-    if (r == 0 && wp.rot_dim > 0) {
-      if (wp.neox && 16 * c < half) {
-        load_bf16_run<16>(cs + 16 * c, pre_c);
-        load_bf16_run<16>(cs + half + 16 * c, pre_s);
-      } else if (!wp.neox && 16 * c < wp.rot_dim) {
-        uint32_t c4[4], s4[4];
-        load_bf16_run<8>(cs + 8 * c, c4);
-        load_bf16_run<8>(cs + half + 8 * c, s4);
+        for (int i = 0; i < 4; ++i)
+          reinterpret_cast<float4*>(prow + 16 * j)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    pw_fence_before();
+    pw_cluster_sync();
+    const int rows_per_rank = (S::kBM + ks - 1) / ks;
+    const int row0 = rank * rows_per_rank;
+    if (warp < S::kEpiWarps) {
+      // this rank's rows, 16 bytes per thread at a time (consecutive threads on consecutive chunks): the
+      // sum over ranks 0, 1, ..., ks - 1 in that order, written in place (no other rank reads these rows)
+      const int nrows = min(rows_per_rank, S::kBM - row0);
+      for (int f = tid; f < nrows * (kPwBN / 4); f += 32 * S::kEpiWarps) {
+        float* loc = part + (row0 + f / (kPwBN / 4)) * kPwPartStride + 4 * (f % (kPwBN / 4));
+        const uint32_t a = smem_u32(loc);
+        float4 v[8];
+#pragma unroll
+        for (int k2 = 0; k2 < 8; ++k2)
+          if (k2 < ks) v[k2] = pw_ld_cluster_f4(a, (uint32_t)k2);
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int k2 = 0; k2 < 8; ++k2)
+          if (k2 < ks) {
+            acc.x = __fadd_rn(acc.x, v[k2].x);
+            acc.y = __fadd_rn(acc.y, v[k2].y);
+            acc.z = __fadd_rn(acc.z, v[k2].z);
+            acc.w = __fadd_rn(acc.w, v[k2].w);
+          }
+        *reinterpret_cast<float4*>(loc) = acc;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * S::kEpiWarps) : "memory");  // epilogue warps only
+      // the sums into this thread's tensor-memory row half (rows of other ranks get zeros; the epilogue
+      // skips them)
+      const bool owned = trow / rows_per_rank == rank;
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) {
+        float acc[16];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          pre_c[i] = c4[i];
-          pre_s[i] = s4[i];
+          const float4 v = owned ? reinterpret_cast<const float4*>(prow + 16 * j)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+          acc[4 * i] = v.x;
+          acc[4 * i + 1] = v.y;
+          acc[4 * i + 2] = v.z;
+          acc[4 * i + 3] = v.w;
         }
+        pw_tmem_st16(ta + 16 * j, acc);
       }
-      if (c == 0)
-        for (int b = 0; b < wp.rot_dim * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(cs + b / 2));
+      asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
     }
+    pw_fence_before();
+    pw_cluster_sync();  // every remote read is done (the stage buffers may be reused) and the sums are in place
+    pw_fence_after();
+  }
 
+  if (warp < S::kEpiWarps) {
     const bool ready = pw_wait(smem_u32(&sm.accum), 0u);
     pw_fence_after();
     slot_ok = slot_ok && ready;

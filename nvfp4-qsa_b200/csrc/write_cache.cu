@@ -1082,6 +1082,8 @@ extern "C" int nvqsa_kv_proj_write_cache(
   ProjParams pp;
   pp.w = w;
   pp.kblocks = (hidden_size + kPwBK - 1) / kPwBK;
+  pp.ksplit = 1;
+  pp.kbs = pp.kblocks;
   pp.value_out = static_cast<__nv_bfloat16*>(value_out);
   pp.value_out_stride_token = value_out_stride_token;
   pp.value_out_stride_head = value_out_stride_head;
@@ -1107,7 +1109,37 @@ extern "C" int nvqsa_kv_proj_write_cache(
       return NVQSA_ERR_CUDA;
     g_pw_smem_set[dev][mh - 1].store(1, std::memory_order_release);
   }
-  const dim3 grid((unsigned)(2 * kv_heads), (unsigned)((num_tokens + bm - 1) / bm));
+  const unsigned mtiles = (unsigned)((num_tokens + bm - 1) / bm);
+  if (mh == 1) {
+    // few tiles (decode batches): split each tile's k-blocks over a cluster of up to 8 CTAs so that the
+    // weights are read by that many more SMs; every rank keeps at least one k-block
+    const int64_t tiles = (int64_t)mtiles * 2 * kv_heads;
+    const int fill = (int)std::min<int64_t>(8, (sms > 0 ? sms : 148) / std::max<int64_t>(tiles, 1));
+    const int cand = std::min(fill, pp.kblocks);
+    if (cand >= 2) {
+      pp.kbs = (pp.kblocks + cand - 1) / cand;
+      pp.ksplit = (pp.kblocks + pp.kbs - 1) / pp.kbs;
+    }
+    if (pp.ksplit > 1) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(2 * kv_heads * pp.ksplit), mtiles);
+      cfg.blockDim = dim3(PwShape<1>::kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = as_stream(stream);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)pp.ksplit;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaLaunchKernelEx(&cfg, kv_proj_write_kernel<1>, pp) == cudaSuccess) return NVQSA_OK;
+      (void)cudaGetLastError();  // clusters of this size not schedulable here: run unsplit
+      pp.ksplit = 1;
+      pp.kbs = pp.kblocks;
+    }
+  }
+  const dim3 grid((unsigned)(2 * kv_heads), mtiles);
   if (mh == 2)
     kv_proj_write_kernel<2><<<grid, PwShape<2>::kThreads, smem, as_stream(stream)>>>(pp);
   else

@@ -9,7 +9,8 @@ the rotary embedding on K, then qsa_write_cache_nvfp4
   2. on random inputs, K and V within one bf16 rounding of an fp32 projection
      computed by torch, and cache bytes and rotated K bit-identical to the
      oracle's chain run on the kernel's own projection (read back with the
-     norm and rotation off: the kernel's accumulation order is fixed).
+     norm and rotation off: the kernel's accumulation order is fixed for a
+     given shape, including the rank order of a split k-loop).
 """
 import numpy as np
 import pytest
@@ -68,6 +69,9 @@ def _slots_positions(rng, tokens, blocks, page, max_pos, holes=True):
     (77, 1000, 4, 64, False, True),      # GPT-J pairs, hidden not a multiple of 64 (zero-filled tail)
     (200, 768, 2, 0, True, False),       # no rotation, no norm: the plain writer on the projection
     (2400, 512, 4, 256, True, True),     # more 128-token CTAs than SMs: 256-token CTAs, ragged last one
+    (3000, 256, 2, 64, True, True),      # 128-token CTAs, one wave, no k-split
+    (96, 4096, 2, 64, True, True),       # a decode batch: each tile's k-blocks split over a cluster of 8 CTAs
+    (1000, 640, 2, 64, False, True),     # 10 k-blocks over clusters of 4 (3, 3, 3, 1)
 ])
 def test_exact_projection_matches_oracle_chain(tokens, hidden_size, kvh, rot, neox, norm):
     rng = np.random.default_rng(tokens + hidden_size + kvh)
