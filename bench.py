@@ -438,7 +438,7 @@ def bench_kv_proj_write(device, steps):
         "cublas_gemm_only_us": gemm * 1e6,
         "speedup_vs_unfused": chain / fused,
         "decode_96_tokens": {"us_per_launch": fused96 * 1e6, "unfused_us": chain96 * 1e6,
-                             "what": "the same call on the first 96 tokens: 4 CTAs, bound by reading the weights"},
+                             "what": "the same call on the first 96 tokens: 4 tiles, each k-loop split over a cluster of 8 CTAs"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_kind": kind, "kernel": "kv_proj_write_kernel",
                      "algorithmic_flops_per_launch": flops, "traffic": NCU_TRAFFIC["kv_proj"],
