@@ -50,7 +50,8 @@ int nvqsa_abi_version(void);
 /*
  * Device error flags raised by the kernels on the current device (bit 0: a
  * bounded wait on a shared-memory barrier ran out, the affected CTA skipped
- * its output; bit 1: a split-KV peer's slot did not arrive within 2 s).  Kernels never trap; this synchronous query (it copies one
+ * its output; bit 1: a split-KV peer's slot did not arrive within 2 s; bit 2:
+ * a bounded wait of nvqsa_kv_proj_write_cache ran out).  Kernels never trap; this synchronous query (it copies one
  * word from the device) is for tests and diagnostics.  clear != 0 resets the
  * flags after reading.  No counterpart in the reference.
  */

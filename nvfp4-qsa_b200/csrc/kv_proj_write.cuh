@@ -25,7 +25,14 @@
 // summation order: each thread's partial sums go through shared memory and
 // both add all 32 in that order), the rotation (bf16 arithmetic, NeoX halves
 // or GPT-J pairs; a NeoX pair of groups stays in one thread), then the group
-// scale and E2M1 codes; for V the codes alone.
+// scale and E2M1 codes; for V the codes alone.  Each row's 144 record bytes
+// are staged in the freed stage buffers and written as 16-byte chunks,
+// consecutive threads on consecutive chunks.
+//
+// Small batches (fewer 128-token tiles than SMs) split each tile's k-blocks
+// over a thread-block cluster of up to 8 CTAs; the partial accumulators are
+// summed over distributed shared memory in rank order (see the k-split block
+// below) before the same epilogue runs on each rank's share of the rows.
 constexpr int kPwBN = 256;        // columns per CTA: one head
 constexpr int kPwBK = 64;         // k-slice per stage: 128 bytes of bf16 (one swizzle atom row)
 constexpr uint32_t kPwStageB = kPwBN * kPwBK * 2;  // 32 KB
