@@ -95,7 +95,7 @@ NCU_TRAFFIC = {
     "fused_write": 18579712,   # write_cache_kernel<256,...,FUSE>, 8,192 tokens
     "bf16": 413479424,         # sparse_attention_bf16_kernel, 96 rows x top-2048 (48-row capture x 2)
     "topk": 50476800,          # topk_indices_kernel, 96 rows x 131,072 scores, k = 2048
-    "kv_proj": 80963072,       # kv_proj_write_kernel<2>, 8,192 tokens x hidden 4,096 -> 1,024 K|V columns
+    "kv_proj": 79862272,       # kv_proj_write_kernel<2>, 8,192 tokens x hidden 4,096 -> 1,024 K|V columns
 }
 
 
